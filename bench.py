@@ -1,0 +1,449 @@
+#!/usr/bin/env python
+"""Benchmark of the tensor-parallel Q8_0 FFN op (Mistral-7B shape) on 1..8 B200.
+
+Workload (the isolated tensor-parallel FFN op with Mistral-7B shape): hidden 4096,
+intermediate 14336, gated SiLU, gate/up/down N(0, 0.02) (seeded CUDA generator, bf16,
+stored [in, out]) quantized to Q8_0 with f16 scales; activations bf16 N(0, 1). The
+intermediate dim is split over the ranks with Dirichlet(5) ratios (seed 1) rounded to
+32-element blocks; every rank ends with the full [T, 4096] sum.
+
+A step is one FFN op call (gate/up + SiLU·mul, down + cross-rank sum) on one batch of
+T tokens (T = 1: decode). Steps rotate over 32 distinct weight sets (one per layer of
+the 7B shape), so the weights each step streams are never L2-resident (32 x shard >
+126 MB L2 at every rank count). The K timed steps run as one captured CUDA graph.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Q8_0 7B-shape decode tok/s + prefill tok/s at 1/2/4/8 B200; FFN % HBM roofline"
+H, I = 4096, 14336
+N_SETS = 32
+Q8_BYTES_PER_PARAM = 34 / 32          # int8 + one f16 scale per 32
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--prefill-tokens", type=int, default=512)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        d = json.loads(PEAKS.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------
+# CPU leg: the reference's own per-call FFN arithmetic (oracle restatement).
+# ---------------------------------------------------------------------------------------
+
+def cpu_reference_leg(tokens: int, budget_s: float, steps: int | None = None):
+    """Times what a reference worker does per FFN message on this host: dequantize its
+    Q8_0 shard (src/orchestrator/worker_node.py:59-69 dequantizes on every access) and run
+    the f32 graph (src/ffn/builder.py:37-45; numpy BLAS stands in for the MAX CPU engine),
+    on the full 4096 x 14336 shard. Returns (tok/s, info)."""
+    from oracle import ffn as offn, q80 as oq80
+    rng = np.random.default_rng(1)
+    qw = []
+    for shape in ((H, I), (H, I), (I, H)):
+        w = (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+        qw.append(oq80.quantize_q80(w))
+        del w
+    x = rng.standard_normal((tokens, H)).astype(np.float32)
+    offn.worker_ffn_step(x, *qw)                     # warm-up (page-in, BLAS threads)
+    times = []
+    t_all = time.perf_counter()
+    n = steps if steps is not None else 10 ** 9
+    while len(times) < n:
+        t0 = time.perf_counter()
+        offn.worker_ffn_step(x, *qw)
+        times.append(time.perf_counter() - t0)
+        if steps is None and time.perf_counter() - t_all > budget_s:
+            break
+    step = statistics.median(times)
+    cores = os.cpu_count() or 1
+    return tokens / step, {
+        "value": tokens / step, "unit": "tok/s", "cores": cores, "kind": "port",
+        "sample": f"{len(times)} reference-worker FFN calls (Q8_0 dequantize + f32 gated FFN, numpy BLAS "
+                  f"with {cores} threads) on the full 4096x14336 shard at T={tokens}; median {step * 1e3:.1f} ms/call",
+        "cpu_model": platform.processor() or platform.machine(),
+    }
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampler (NVML reads only)
+# ---------------------------------------------------------------------------------------
+
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, dev_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(dev_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self.nv
+        get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append((time.perf_counter(), nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                     int(get_r(self.h))))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self, t0: float, t1: float):
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not win and self.samples:
+            mid = 0.5 * (t0 + t1)
+            win = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+        mhz = [s[1] for s in win]
+        bits = 0
+        for s in win:
+            bits |= s[2]
+        reasons = [name for b, name in self.REASONS.items() if bits & b and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(win)}
+
+
+# ---------------------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------------------
+
+def make_sets(rank, bounds, n_sets, device):
+    """Per weight set (one per layer): full matrices from a seeded CUDA generator (identical
+    on every rank), Q8_0 on the GPU, then this rank's shard."""
+    import torch
+    from pyre_b200.quantizer import Q80Weight
+    s, e = bounds[rank]
+    sets = []
+    for layer in range(n_sets):
+        g = torch.Generator(device=device).manual_seed(1 + 1000 * layer)
+        trip = []
+        for shape in ((I, H), (I, H), (H, I)):
+            w = (torch.randn(shape, generator=g, device=device) * 0.02).to(torch.bfloat16).t().contiguous()
+            trip.append(Q80Weight.from_float(w, torch.float16))
+            del w
+        gq, uq, dq = trip
+        sets.append((gq.cols(s, e), uq.cols(s, e), dq.rows(s, e)))
+        del trip, gq, uq, dq
+    torch.cuda.synchronize()
+    return sets
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from pyre_b200 import _native as N
+    from pyre_b200.ffn import FfnShardOp
+    from pyre_b200.ffn.captured import CapturedFfn
+    from pyre_b200.tp import ShardPlan, TPComm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    N.load()
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+    T = args.tokens
+    plan = ShardPlan.dirichlet(I, world, 5.0, 1)
+    bounds = plan.bounds
+    W = plan.widths[rank]
+    sets = make_sets(rank, bounds, N_SETS, dev)
+    comm = TPComm(H, max_tokens=max(T, args.prefill_tokens), timeout_s=5.0) if world > 1 else None
+    op = FfnShardOp(H, W, max_tokens=max(T, args.prefill_tokens if not args.no_prefill else T), comm=comm, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn((T, H), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((T, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def capture(n_steps, with_events=False):
+        g = torch.cuda.CUDAGraph()
+        evs = []
+        with torch.cuda.stream(stream):
+            op(x, *sets[0], out=out, stream=stream)       # eager once before capture
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n_steps):
+                gq, uq, dq = sets[i % N_SETS]
+                if with_events:
+                    e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+                    e[0].record(stream)
+                    # the two kernels of the op, recorded separately
+                    h = torch.empty((T, W), dtype=op.h_dtype(T), device=dev)
+                    _gateup(op, x, gq, uq, h, stream)
+                    e[1].record(stream)
+                    _down(op, h, dq, out, stream)
+                    e[2].record(stream)
+                    evs.append(e)
+                else:
+                    op(x, gq, uq, dq, out=out, stream=stream)
+        return g, evs
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    # warm-up and timed graphs
+    g_warm, _ = capture(max(args.warmup, 3))
+    g_main, _ = capture(args.steps)
+    g_probe, probe_ev = capture(N_SETS, with_events=True)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        g_warm.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.05)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    with torch.cuda.stream(stream):
+        g_warm.replay()
+    stream.synchronize()
+    barrier()
+    t_wall0 = time.perf_counter()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        g_main.replay()
+    ev1.record(stream)
+    stream.synchronize()
+    t_wall1 = time.perf_counter()
+    barrier()
+    if comm is not None:
+        comm.check(stream)
+    elapsed_ms = ev0.elapsed_time(ev1)
+
+    # per-kernel durations (probe graph with external event nodes, 32 distinct weight sets)
+    gu_ms, dn_ms = [], []
+    for _ in range(4):
+        barrier()
+        with torch.cuda.stream(stream):
+            g_probe.replay()
+        stream.synchronize()
+        for e in probe_ev:
+            gu_ms.append(e[0].elapsed_time(e[1]))
+            dn_ms.append(e[1].elapsed_time(e[2]))
+    sampler.stop()
+    if comm is not None:
+        comm.check(stream)
+
+    # end-to-end through the public API: pinned host x in, host partial sum out, per call
+    e2e_runners = [CapturedFfn(op, *sets[i], tokens=T) for i in range(min(N_SETS, 8))]
+    xh = x.float().cpu().to(torch.bfloat16)
+    for r in e2e_runners:
+        r.execute(xh)
+    barrier()
+    e2e_steps = max(args.steps, 20)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_runners[i % len(e2e_runners)].execute(xh)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+
+    # prefill: T = 512 tokens per call, 4 weight sets rotating (prefill weight traffic is
+    # amortised over 512 tokens; the GEMM is compute-bound)
+    prefill = None
+    if not args.no_prefill:
+        TP = args.prefill_tokens
+        xp = torch.randn((TP, H), generator=gen, device=dev).to(torch.bfloat16)
+        outp = torch.empty((TP, H), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                op(xp, *sets[i % N_SETS], out=outp, stream=stream)
+        stream.synchronize()
+        n_pf = 8
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gp, stream=stream):
+            for i in range(n_pf):
+                op(xp, *sets[i % N_SETS], out=outp, stream=stream)
+        with torch.cuda.stream(stream):
+            gp.replay()
+        stream.synchronize()
+        barrier()
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        with torch.cuda.stream(stream):
+            gp.replay()
+        p1.record(stream)
+        stream.synchronize()
+        barrier()
+        pf_ms = p0.elapsed_time(p1) / n_pf
+        prefill = {"tokens": TP, "ms_per_step": pf_ms}
+
+    # max over ranks
+    vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(gu_ms), statistics.mean(dn_ms),
+                         prefill["ms_per_step"] if prefill else 0.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_s, gu_avg, dn_avg, pf_ms = vals.tolist()
+    clocks = sampler.summary(t_wall0, t_wall1)
+
+    if rank == 0:
+        ms_step = elapsed_ms / args.steps
+        value = T / (ms_step / 1e3)
+        # algorithmic bytes of the slowest rank's shard are the critical path; the roofline
+        # of the dominant kernel is reported for rank 0's shard and its measured duration
+        W0 = plan.widths[0]
+        gu_bytes = 2 * H * W0 * Q8_BYTES_PER_PARAM + T * H * 2 + T * W0 * 4
+        dn_bytes = W0 * H * Q8_BYTES_PER_PARAM + T * W0 * 4 + T * H * 4
+        gu_gbs = gu_bytes / (gu_avg * 1e-3) / 1e9
+        step_bytes_all = 3 * H * I * Q8_BYTES_PER_PARAM
+        res = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 accumulate on int8 Q8_0 weights (f16 scales), bf16 activations",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "tensor-parallel gated-SiLU FFN op, Mistral-7B shape (hidden 4096, intermediate 14336), decode",
+                       "tokens": T, "widths": list(plan.widths), "partition": "Dirichlet(5) seed 1, 32-element blocks",
+                       "weight_sets": N_SETS, "l2": "inputs larger than L2: 32 rotating weight sets per rank",
+                       "parallelism": f"tp{world}", "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "kernel": "q80_gemv_kernel (gate/up + SiLU·mul), rank 0 shard",
+                         "achieved": round(gu_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gu_gbs / hbm, 4),
+                         "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": int(gu_bytes), "avg_launch_us": round(gu_avg * 1e3, 3),
+                         "down_kernel": {"avg_launch_us": round(dn_avg * 1e3, 3),
+                                         "achieved": round(dn_bytes / (dn_avg * 1e-3) / 1e9, 1)},
+                         "step_aggregate": {"bytes_all_ranks": int(step_bytes_all),
+                                            "achieved_per_gpu": round(step_bytes_all / world / (ms_step * 1e-3) / 1e9, 1),
+                                            "frac_of_aggregate": round(step_bytes_all / (ms_step * 1e-3) / 1e9 / (hbm * world), 4)}},
+            "gpu_launches": args.steps * op.launches_per_call,
+            "e2e": {"value": round(e2e_steps * T / e2e_s, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": e2e_runners[0].h2d_bytes, "d2h_bytes_per_step": e2e_runners[0].d2h_bytes,
+                    "how": "CapturedFfn.execute(host x) per call: pinned H2D, graph of the op, D2H, stream sync"},
+            "clocks": clocks,
+        }
+        if prefill:
+            flops = 6 * args.prefill_tokens * H * I
+            res["prefill"] = {"tokens": args.prefill_tokens, "ms_per_step": round(pf_ms, 4),
+                              "tok_s": round(args.prefill_tokens / (pf_ms * 1e-3), 1),
+                              "tflops": round(flops / (pf_ms * 1e-3) / 1e12, 2),
+                              "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / (tf_burst * world), 4)}
+        if not args.no_cpu:
+            _, cpu = cpu_reference_leg(T, args.cpu_seconds)
+            res["cpu_baseline"] = cpu
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        barrier()
+        del g_main, g_warm, g_probe, e2e_runners
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def _gateup(op, x, gq, uq, h, stream):
+    import ctypes
+    from pyre_b200 import _device as D, _native as N
+    N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), x.shape[0], op.hidden, D.ptr(gq.q),
+           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, op.width, D.ptr(h), D.dtype_code(h),
+           D.ptr(op.workspace), op.workspace.numel(), ctypes.c_void_p(stream.cuda_stream))
+
+
+def _down(op, h, dq, out, stream):
+    import ctypes
+    from pyre_b200 import _device as D, _native as N
+    N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), h.shape[0], op.width, D.ptr(dq.q), D.ptr(dq.scale),
+           dq.scale_code, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
+           ctypes.c_void_p(op.comm.handle if op.comm is not None else 0), ctypes.c_void_p(stream.cuda_stream))
+
+
+def run_reference(args):
+    """The reference's CPU FFN call on this host (rank 0 only; other ranks exit)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    T = args.tokens
+    # size the sample so W + K calls fit in a few minutes
+    from oracle import ffn as offn  # noqa: F401  (import check)
+    steps = args.steps
+    t0 = time.perf_counter()
+    _, info0 = cpu_reference_leg(T, 0.0, steps=1)
+    per_call = 1.0 / info0["value"] * T
+    budget = 150.0
+    n_w = max(0, min(args.warmup, int(budget * 0.2 / per_call)))
+    n_k = max(1, min(steps, int(budget / per_call)))
+    value, info = cpu_reference_leg(T, 0.0, steps=n_k + n_w)
+    info["sample"] += f"; {n_k} timed of {steps} requested steps (bounded to ~{budget:.0f} s)"
+    res = {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "tok/s", "n_gpus": args.gpus,
+           "steps": n_k, "warmup": n_w, "ms_per_step": round(1e3 * T / value, 3), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "tensor-parallel gated-SiLU FFN op, Mistral-7B shape (hidden 4096, intermediate 14336), decode",
+                      "tokens": T},
+           "cpu_baseline": {k: info[k] for k in ("value", "unit", "cores", "kind", "sample")},
+           "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "wall_s": round(time.perf_counter() - t0, 1)}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

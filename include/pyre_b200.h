@@ -1,0 +1,140 @@
+/*
+ * pyre_b200.h — C ABI of the B200 (sm_100a) tensor-parallel forward hot path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers and sizes (no framework types),
+ *   - is asynchronous on the caller-supplied stream (a cudaStream_t passed as void*;
+ *     NULL means the legacy default stream),
+ *   - returns an int status: PYRE_OK (0) or one of the PYRE_E* codes below. The message
+ *     of the last failure on the calling thread is available through pyre_last_error().
+ *
+ * The caller owns every buffer it passes in. The library never frees caller memory;
+ * pyre_comm_t owns only what pyre_comm_create() allocates (peer table, status word).
+ *
+ * Q8_0 device format (the reference's own orientation, see
+ * src/orchestrator/quantizer.py:11-26 and src/orchestrator/llama_loader.py:1132-1134):
+ * a weight stored as [K, N] row-major float (K = input dim, N = output dim) is
+ * quantized in flattened C order in 32-element blocks, so each block runs along N.
+ *   q      int8  [K, N]
+ *   scale  f32 or f16 [K, N/32]   (scale[k, j/32] belongs to q[k, j])
+ * N must be a multiple of 32 for the GEMV/GEMM entry points.
+ */
+#ifndef PYRE_B200_H
+#define PYRE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PYRE_API __attribute__((visibility("default")))
+#else
+#define PYRE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define PYRE_OK        0
+#define PYRE_EINVAL    1  /* bad argument: null pointer, size, alignment, dtype        */
+#define PYRE_ECUDA     2  /* a CUDA runtime/driver call failed                          */
+#define PYRE_ETIMEOUT  3  /* a bounded device-side wait on a peer ran out               */
+#define PYRE_ENOMEM    4  /* caller-supplied workspace too small / allocation failed    */
+
+/* ---- element types ----------------------------------------------------------------- */
+#define PYRE_F32   0
+#define PYRE_BF16  1
+#define PYRE_F16   2
+
+typedef struct pyre_comm pyre_comm_t;
+
+/* Library version (major*10000 + minor*100 + patch). */
+PYRE_API int pyre_version(void);
+
+/* Copies the last error message of the calling thread into buf (NUL-terminated,
+ * truncated to len). Returns the length of the full message. */
+PYRE_API int pyre_last_error(char* buf, int len);
+
+/* ---- Q8_0 format ------------------------------------------------------------------
+ * pyre_q80_quantize replaces quantize_q80 (src/orchestrator/quantizer.py:11-26):
+ *   flatten -> zero-pad to a multiple of 32 -> per block absmax (0 -> 1.0) ->
+ *   scale = f32(absmax / 127) -> q = clip(round_half_even(x / scale), -128, 127).
+ * Bit-exact with the reference for finite inputs. src is f32 or bf16 (src_dtype).
+ * q receives ceil(n/32)*32 bytes; scale_f32 and scale_f16 receive ceil(n/32)
+ * entries each; either scale pointer may be NULL (not both). scale_f16 holds
+ * f16(scale_f32), round-to-nearest-even. */
+PYRE_API int pyre_q80_quantize(const void* src, int src_dtype, int64_t n,
+                      int8_t* q, float* scale_f32, uint16_t* scale_f16, void* stream);
+
+/* pyre_q80_dequantize replaces dequantize_q80 (src/orchestrator/quantizer.py:29-40)
+ * and pyre_kernels.q80_dequantize (src/kernels/mojo/pyre_kernels.mojo:172-185):
+ * out[i] = f32(q[i]) * scale[i/32], for i < n. scale_dtype is PYRE_F32 or PYRE_F16. */
+PYRE_API int pyre_q80_dequantize(const int8_t* q, const void* scale, int scale_dtype, int64_t n,
+                        float* out, void* stream);
+
+/* ---- gated-SiLU FFN shard ---------------------------------------------------------
+ * The shard [ffn_start, ffn_end) of width W of the intermediate dim, as built by
+ * build_ffn_graph (src/ffn/builder.py:20-53) and run by the root's decode FFN
+ * (src/orchestrator/root_node.py:956-980).
+ *
+ * Bytes of scratch the two FFN calls below need for T tokens, hidden H, width W. */
+PYRE_API int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes);
+
+/* h[T, W] = silu(x @ Wg) * (x @ Wu)      (gated,   src/ffn/builder.py:37-43)
+ * h[T, W] = silu(x @ Wu)                 (ungated, src/ffn/builder.py:47-49; qg == NULL)
+ * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16). Wg, Wu: Q8_0 [H, W] (scales [H, W/32]
+ * of scale_dtype). h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
+ * as in pyre_kernels.silu_mul (src/kernels/mojo/pyre_kernels.mojo:121-129).
+ * workspace: zero-initialised device memory of at least pyre_ffn_workspace_bytes();
+ * it is left zeroed where it must start at zero, so it can be reused call after call on
+ * one stream (calls that overlap on the GPU need separate workspaces). */
+PYRE_API int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H,
+                             const int8_t* qg, const void* sg,
+                             const int8_t* qu, const void* su, int scale_dtype, int W,
+                             void* h, int h_dtype, void* workspace, int64_t ws_bytes,
+                             void* stream);
+
+/* out[T, H] = h @ Wd   (src/ffn/builder.py:44), and with comm != NULL also the sum of
+ * that partial over every rank of comm (src/orchestrator/root_node.py:582-594 and
+ * :982-995, `ffn_out += partial`), in rank order 0..world-1 on every rank. For
+ * T <= PYRE_FUSED_REDUCE_MAX_T the reduction happens in the GEMV epilogue through
+ * NVLink peer stores and bounded flag waits; above it a two-shot peer-memory
+ * all-reduce follows the GEMM. h: [T, W] of h_dtype; Wd: Q8_0 [W, H]; out: f32 [T, H]. */
+#define PYRE_FUSED_REDUCE_MAX_T 4
+PYRE_API int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W,
+                      const int8_t* qd, const void* sd, int scale_dtype, int H,
+                      float* out, void* workspace, int64_t ws_bytes,
+                      pyre_comm_t* comm, void* stream);
+
+/* ---- peer-memory communicator (one process per GPU, NVLink / NVSwitch) ------------
+ * Replaces the reference's TCP gather of FFN partials (src/orchestrator/net.py:18-48
+ * used at src/orchestrator/root_node.py:582-594) inside one box.
+ *
+ * Bytes of the symmetric receive buffer each rank allocates for world ranks, up to
+ * max_tokens tokens of a hidden-wide f32 row. */
+PYRE_API int pyre_comm_buffer_bytes(int world, int max_tokens, int hidden, int64_t* bytes);
+/* cudaMalloc + zero a receive buffer and export its IPC handle (64 bytes). */
+PYRE_API int pyre_comm_alloc(int64_t bytes, void** dev_ptr, void* ipc_handle_out);
+PYRE_API int pyre_comm_free(void* dev_ptr);
+/* Map a peer's exported buffer into this process (cudaIpcOpenMemHandle). */
+PYRE_API int pyre_comm_open_peer(const void* ipc_handle, void** peer_ptr);
+PYRE_API int pyre_comm_close_peer(void* peer_ptr);
+/* bufs[r] is rank r's receive buffer as seen from this process (bufs[rank] is the
+ * local one). All ranks must pass the same world, max_tokens and hidden. */
+PYRE_API int pyre_comm_create(int rank, int world, void* const* bufs, int max_tokens, int hidden,
+                     pyre_comm_t** out);
+PYRE_API int pyre_comm_destroy(pyre_comm_t* comm);
+/* Limit of every device-side wait on a peer flag, in nanoseconds (default 2 s). */
+PYRE_API int pyre_comm_set_timeout_ns(pyre_comm_t* comm, uint64_t ns);
+/* Synchronises stream, then reads and clears the device status word of comm:
+ * *status = PYRE_OK, or PYRE_ETIMEOUT if some wait since the last check ran out. */
+PYRE_API int pyre_comm_check(pyre_comm_t* comm, int* status, void* stream);
+/* In-place sum over ranks of a f32 buffer of n elements (two-shot: reduce-scatter then
+ * all-gather through peer memory), rank order 0..world-1. n <= max_tokens * hidden. */
+PYRE_API int pyre_allreduce_sum_f32(pyre_comm_t* comm, float* buf, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PYRE_B200_H */

@@ -1,0 +1,51 @@
+// Library-wide C ABI pieces: version, per-thread error text, device queries.
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace pyre {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PYRE_OK;
+  return set_error(PYRE_ECUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                                   cudaGetErrorString(e) + ")");
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace pyre
+
+extern "C" int pyre_version(void) { return 100; }
+
+extern "C" int pyre_last_error(char* buf, int len) {
+  const std::string& s = pyre::g_last_error;
+  if (buf != nullptr && len > 0) {
+    const size_t n = s.size() < static_cast<size_t>(len - 1) ? s.size() : static_cast<size_t>(len - 1);
+    std::memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+  }
+  return static_cast<int>(s.size());
+}

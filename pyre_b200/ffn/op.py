@@ -1,0 +1,88 @@
+"""The FFN shard op on Q8_0 weights: ``partial = (silu(x@Wg) * (x@Wu)) @ Wd``.
+
+This is the compute of ``build_ffn_graph`` (``src/ffn/builder.py:37-45``) and of the root's
+decode FFN (``src/orchestrator/root_node.py:956-980``), plus, when a :class:`TPComm` is
+given, the cross-rank sum ``ffn_out += partial`` (``root_node.py:582-594``, ``:982-995``)
+done inside the down-projection's epilogue over NVLink.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .. import _device as D
+from .. import _native as N
+from ..quantizer import Q80Weight
+
+
+def workspace_bytes(tokens: int, hidden: int, width: int) -> int:
+    out = ctypes.c_int64(0)
+    N.call("pyre_ffn_workspace_bytes", int(tokens), int(hidden), int(width), ctypes.byref(out))
+    return int(out.value)
+
+
+class FfnShardOp:
+    """One rank's FFN shard for up to ``max_tokens`` tokens.
+
+    Holds the zero-initialised scratch the stream-K GEMV needs (reused call after call
+    on one stream) and launches two kernels per call: gate/up + SiLU·mul, then down
+    (+ the tensor-parallel reduction when ``comm`` is set).
+    """
+
+    def __init__(self, hidden_dim: int, width: int, max_tokens: int = 1, *, gated: bool = True,
+                 comm=None, device: torch.device | None = None):
+        D.require_cuda()
+        if width <= 0 or hidden_dim <= 0:
+            raise ValueError(f"ShardSpec width must be positive, got {width}")
+        if width % 32 or hidden_dim % 32:
+            raise ValueError("FFN shard width and hidden dim must be multiples of 32 (Q8_0 blocks)")
+        self.hidden = int(hidden_dim)
+        self.width = int(width)
+        self.max_tokens = int(max_tokens)
+        self.gated = gated
+        self.comm = comm
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        wsb = workspace_bytes(min(self.max_tokens, N.PYRE_FUSED_REDUCE_MAX_T), self.hidden, self.width)
+        self.workspace = torch.zeros(wsb, dtype=torch.uint8, device=self.device)
+        self.launches_per_call = 2 + (1 if (comm is not None and comm.world > 1 and
+                                            self.max_tokens > N.PYRE_FUSED_REDUCE_MAX_T) else 0)
+
+    def h_dtype(self, tokens: int) -> torch.dtype:
+        # decode keeps the intermediate in f32; larger T stores bf16 (tensor-core operand)
+        return torch.float32 if tokens <= N.PYRE_FUSED_REDUCE_MAX_T else torch.bfloat16
+
+    def __call__(self, x: torch.Tensor, gate: Q80Weight | None, up: Q80Weight, down: Q80Weight,
+                 out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError(f"x must be [T, {self.hidden}], got {tuple(x.shape)}")
+        T = x.shape[0]
+        if T < 1 or T > self.max_tokens:
+            raise ValueError(f"T={T} outside [1, {self.max_tokens}]")
+        if x.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("x must be float32 or bfloat16")
+        if not x.is_contiguous():
+            x = x.contiguous()
+        if self.gated and gate is None:
+            raise ValueError("gated FFN needs a gate weight")
+        for name, w, shp in (("gate", gate, (self.hidden, self.width)), ("up", up, (self.hidden, self.width)),
+                             ("down", down, (self.width, self.hidden))):
+            if w is None:
+                continue
+            if tuple(w.shape) != shp:
+                raise ValueError(f"{name} weight must be {shp}, got {tuple(w.shape)}")
+        if gate is not None and gate.scale.dtype != up.scale.dtype:
+            raise ValueError("gate and up scales must share a dtype")
+        s = D.stream_ptr(stream)
+        h = torch.empty((T, self.width), dtype=self.h_dtype(T), device=x.device)
+        if out is None:
+            out = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
+        ws = self.workspace
+        N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
+               D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
+               D.ptr(up.q), D.ptr(up.scale), up.scale_code, self.width,
+               D.ptr(h), D.dtype_code(h), D.ptr(ws), ws.numel(), s)
+        N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), T, self.width, D.ptr(down.q), D.ptr(down.scale),
+               down.scale_code, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(),
+               ctypes.c_void_p(self.comm.handle if self.comm is not None else 0), s)
+        return out
