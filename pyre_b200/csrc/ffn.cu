@@ -41,6 +41,7 @@ struct Params {
   int upt;                   // units per tile = ceil(K / kUnitRows)
   int64_t total_units;       // tiles * upt
   int pmax;                  // piece slots per tile in ws
+  int64_t ws_cap;            // bytes of ws (after the counters)
   float* ws;                 // [tiles, pmax, NMAT, T, kCols]
   unsigned int* counters;    // [tiles], zero between calls
   void* out;                 // [T, N]
@@ -398,6 +399,8 @@ int launch_gemv(Params p, cudaStream_t s) {
   auto kern = q80_gemv_kernel<T, NMAT, EPI, XT, ST>;
   const int G = gemv_grid(kern, p.total_units);
   p.pmax = pmax_for(p.tiles, p.upt, G);
+  if (static_cast<int64_t>(p.tiles) * p.pmax * NMAT * T * kCols * 4 > p.ws_cap)
+    return set_error(PYRE_ENOMEM, "q80_gemv: stream-K workspace too small for this grid");
   kern<<<G, kThreads, 0, s>>>(p);
   PYRE_LAUNCH_CHECK("q80_gemv_kernel");
   return PYRE_OK;
@@ -490,6 +493,7 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = static_cast<unsigned int*>(workspace);
   p.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+  p.ws_cap = ws_bytes - kCounterBytes;
   p.out = h;
   p.out_bf16 = h_dtype == PYRE_BF16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -525,6 +529,7 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = static_cast<unsigned int*>(workspace);
   p.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+  p.ws_cap = ws_bytes - kCounterBytes;
   p.out = out;
   p.out_bf16 = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
