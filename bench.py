@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
     return ap.parse_args()
 
 
@@ -208,7 +209,8 @@ def run_ours(args):
     plan = ShardPlan.dirichlet(I, world, 5.0, 1)
     bounds = plan.bounds
     W = plan.widths[rank]
-    sets = make_sets(rank, bounds, N_SETS, dev)
+    n_sets = args.sets
+    sets = make_sets(rank, bounds, n_sets, dev)
     comm = TPComm(H, max_tokens=max(T, args.prefill_tokens), timeout_s=5.0) if world > 1 else None
     op = FfnShardOp(H, W, max_tokens=max(T, args.prefill_tokens if not args.no_prefill else T), comm=comm, device=dev)
     gen = torch.Generator(device=dev).manual_seed(1)
@@ -224,7 +226,7 @@ def run_ours(args):
         stream.synchronize()
         with torch.cuda.graph(g, stream=stream):
             for i in range(n_steps):
-                gq, uq, dq = sets[i % N_SETS]
+                gq, uq, dq = sets[i % n_sets]
                 if with_events:
                     e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
                     e[0].record(stream)
@@ -247,7 +249,7 @@ def run_ours(args):
     # warm-up and timed graphs
     g_warm, _ = capture(max(args.warmup, 3))
     g_main, _ = capture(args.steps)
-    g_probe, probe_ev = capture(N_SETS, with_events=True)
+    g_probe, probe_ev = capture(n_sets, with_events=True)
     torch.cuda.synchronize()
     for _ in range(2):
         g_warm.replay()
@@ -290,7 +292,7 @@ def run_ours(args):
         comm.check(stream)
 
     # end-to-end through the public API: pinned host x in, host partial sum out, per call
-    e2e_runners = [CapturedFfn(op, *sets[i], tokens=T) for i in range(min(N_SETS, 8))]
+    e2e_runners = [CapturedFfn(op, *sets[i], tokens=T) for i in range(min(n_sets, 8))]
     xh = x.float().cpu().to(torch.bfloat16)
     for r in e2e_runners:
         r.execute(xh)
@@ -311,13 +313,13 @@ def run_ours(args):
         outp = torch.empty((TP, H), dtype=torch.float32, device=dev)
         with torch.cuda.stream(stream):
             for i in range(3):
-                op(xp, *sets[i % N_SETS], out=outp, stream=stream)
+                op(xp, *sets[i % n_sets], out=outp, stream=stream)
         stream.synchronize()
         n_pf = 8
         gp = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gp, stream=stream):
             for i in range(n_pf):
-                op(xp, *sets[i % N_SETS], out=outp, stream=stream)
+                op(xp, *sets[i % n_sets], out=outp, stream=stream)
         with torch.cuda.stream(stream):
             gp.replay()
         stream.synchronize()
@@ -358,7 +360,7 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
             "config": {"workload": "tensor-parallel gated-SiLU FFN op, Mistral-7B shape (hidden 4096, intermediate 14336), decode",
                        "tokens": T, "widths": list(plan.widths), "partition": "Dirichlet(5) seed 1, 32-element blocks",
-                       "weight_sets": N_SETS, "l2": "inputs larger than L2: 32 rotating weight sets per rank",
+                       "weight_sets": n_sets, "l2": f"inputs larger than L2: {n_sets} rotating weight sets per rank",
                        "parallelism": f"tp{world}", "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "kernel": "q80_gemv_kernel (gate/up + SiLU·mul), rank 0 shard",
                          "achieved": round(gu_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gu_gbs / hbm, 4),
@@ -397,7 +399,8 @@ def _gateup(op, x, gq, uq, h, stream):
     import ctypes
     from pyre_b200 import _device as D, _native as N
     N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), x.shape[0], op.hidden, D.ptr(gq.q),
-           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, op.width, D.ptr(h), D.dtype_code(h),
+           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, uq.scale_ld, op.width, D.ptr(h),
+           D.dtype_code(h),
            D.ptr(op.workspace), op.workspace.numel(), ctypes.c_void_p(stream.cuda_stream))
 
 
@@ -405,7 +408,7 @@ def _down(op, h, dq, out, stream):
     import ctypes
     from pyre_b200 import _device as D, _native as N
     N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), h.shape[0], op.width, D.ptr(dq.q), D.ptr(dq.scale),
-           dq.scale_code, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
+           dq.scale_code, dq.scale_ld, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
            ctypes.c_void_p(op.comm.handle if op.comm is not None else 0), ctypes.c_void_p(stream.cuda_stream))
 
 

@@ -17,33 +17,42 @@
 #include <algorithm>
 
 #include "comm.cuh"
+#include "tma.cuh"
 
 namespace pyre {
 namespace ffn {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kCols = 128;
-constexpr int kUnitRows = 32;
+constexpr int kTileN = 256;           // output columns per tile
+constexpr int kUnitRows = 32;         // input rows per work unit = one pipeline stage
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;   // + one producer warp
 constexpr int kMaxGrid = 1024;
-constexpr int kCounterWords = 2048;  // tiles <= 2048 (N <= 262144)
+constexpr int kCounterWords = 2048;         // word kCounterWords-1 is the status word
+constexpr int kMaxTiles = kCounterWords - 1;
 
 enum Epi : int { EPI_SILU_MUL = 0, EPI_SILU = 1, EPI_STORE = 2, EPI_TP = 3 };
 
-struct Params {
-  const void* x;             // [T, K]
-  const int8_t* q0;          // gate (NMAT == 2) or the single matrix
+struct alignas(64) Params {
+  CUtensorMap tq[2];         // int8 q [K, N], box 32 x 256
+  CUtensorMap ts[2];         // scales [K, scale_ld], box 32 x 8
+  CUtensorMap tx;            // activations [T, K], box T x 32
+  // plain pointers (SIMT GEMM path)
+  const void* x;
+  const int8_t* q0;
   const void* s0;
-  const int8_t* q1;          // up (NMAT == 2)
+  const int8_t* q1;
   const void* s1;
   int K, N, T;
-  int tiles;                 // ceil(N / kCols)
+  int scale_ld;              // entries per scale row (>= N/32)
+  int tiles;                 // ceil(N / kTileN)
   int upt;                   // units per tile = ceil(K / kUnitRows)
   int64_t total_units;       // tiles * upt
   int pmax;                  // piece slots per tile in ws
   int64_t ws_cap;            // bytes of ws (after the counters)
-  float* ws;                 // [tiles, pmax, NMAT, T, kCols]
+  float* ws;                 // [tiles, pmax, NMAT, T, kTileN]
   unsigned int* counters;    // [tiles], zero between calls
+  int* status;               // device status word (bounded waits)
   void* out;                 // [T, N]
   int out_bf16;
   comm::DevComm comm;        // EPI_TP only
@@ -69,35 +78,37 @@ __device__ __forceinline__ void store_out(const Params& p, int t, int col, float
     static_cast<float*>(p.out)[o] = v;
 }
 
-// First / last CTA whose unit range [c*U/G, (c+1)*U/G) contains unit index x.
+// CTA whose unit range [c*U/G, (c+1)*U/G) contains unit index x.
 __host__ __device__ __forceinline__ int cta_of_unit(int64_t x, int64_t U, int G) {
   return static_cast<int>(((x + 1) * G - 1) / U);
 }
 
-// Epilogue over the finished tile sums vals(m, t, c) held in shared memory `fin`
-// ([NMAT][T][kCols]).
+__device__ __forceinline__ void consumer_sync() { named_bar(1, kConsumers); }
+
+// Epilogue over the finished tile sums held in shared memory `fin` ([NMAT][T][kTileN]).
+// Runs on the consumer threads only (tid in [0, kConsumers)).
 template <int T, int NMAT, int EPI>
-__device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint32_t epoch) {
-  const int col_base = tile * kCols;
+__device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint32_t epoch, int tid) {
+  const int col_base = tile * kTileN;
   if constexpr (EPI == EPI_TP) {
     const comm::DevComm& c = p.comm;
     const int slot = epoch & 1u;
-    const int n = T * kCols;
+    const int n = T * kTileN;
     // push this rank's tile partial into every rank's receive slot (self included)
     for (int peer = 0; peer < c.world; ++peer) {
       float* dst = comm::fused_slot(c, peer, slot, c.rank) + static_cast<int64_t>(tile) * n;
-      for (int i = threadIdx.x; i < n; i += kThreads) dst[i] = fin[i];
+      for (int i = tid; i < n; i += kConsumers) dst[i] = fin[i];
     }
     __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < c.world) st_release_sys(comm::fused_flag(c, threadIdx.x, slot, c.rank, tile), epoch);
-    if (threadIdx.x < c.world) {
-      if (!wait_flag_eq(comm::fused_flag(c, c.rank, slot, threadIdx.x, tile), epoch, c.timeout_ns))
+    consumer_sync();
+    if (tid < c.world) st_release_sys(comm::fused_flag(c, tid, slot, c.rank, tile), epoch);
+    if (tid < c.world) {
+      if (!wait_flag_eq(comm::fused_flag(c, c.rank, slot, tid, tile), epoch, c.timeout_ns))
         atomicExch(c.status, PYRE_ETIMEOUT);
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += kThreads) {
-      const int t = i / kCols, cc = i % kCols;
+    consumer_sync();
+    for (int i = tid; i < n; i += kConsumers) {
+      const int t = i / kTileN, cc = i % kTileN;
       const int col = col_base + cc;
       if (col >= p.N) continue;
       float acc = 0.f;
@@ -106,13 +117,13 @@ __device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint3
       store_out(p, t, col, acc);
     }
   } else {
-    for (int i = threadIdx.x; i < T * kCols; i += kThreads) {
-      const int t = i / kCols, cc = i % kCols;
+    for (int i = tid; i < T * kTileN; i += kConsumers) {
+      const int t = i / kTileN, cc = i % kTileN;
       const int col = col_base + cc;
       if (col >= p.N) continue;
       float v;
       if constexpr (EPI == EPI_SILU_MUL) {
-        v = silu_f32(fin[i]) * fin[T * kCols + i];
+        v = silu_f32(fin[i]) * fin[T * kTileN + i];
       } else if constexpr (EPI == EPI_SILU) {
         v = silu_f32(fin[i]);
       } else {
@@ -123,156 +134,222 @@ __device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint3
   }
 }
 
-template <int T, int NMAT>
+template <int T, int NMAT, typename XT, typename ST>
 struct GemvCfg {
-  static constexpr int kUnroll = (T * NMAT <= 2) ? 4 : 2;
-  static constexpr int kMinBlocks = (T * NMAT <= 2) ? 2 : 1;
+  static constexpr int kStages = (T <= 2) ? 8 : 5;
+  static constexpr int kQBytes = kUnitRows * kTileN;                       // 8 KB per matrix
+  static constexpr int kSBytes = kUnitRows * 8 * static_cast<int>(sizeof(ST));   // 8 scale columns
+  static constexpr int kXBytes = T * kUnitRows * static_cast<int>(sizeof(XT));
+  static constexpr int kTxBytes = NMAT * (kQBytes + kSBytes) + kXBytes;
+  static constexpr int kStageBytes = (kTxBytes + 127) / 128 * 128;
+  static constexpr int kRedFloats = kConsumerWarps * NMAT * T * kTileN;
+  static constexpr int kFinFloats = NMAT * T * kTileN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + (kRedFloats + kFinFloats) * 4 + 2 * kStages * 8 + 16;
 };
 
+// Decode GEMV over Q8_0 weights, TMA-fed.
+//   warp 8 (producer): lane 0 streams, per unit, the int8 tile [32 rows x 256 cols] and
+//     its scale tile [32 x 8] of each matrix plus the activation slice [T x 32] into an
+//     mbarrier ring of kStages stages.
+//   warps 0-7 (consumers): lane (rs, cc) owns columns 16cc..16cc+15 and rows
+//     2*warp + rs (+16) of each unit; int8 -> f32 by byte-permute, scale folded into the
+//     activation, packed f32x2 FMA into f32 accumulators.
+// The (tile, unit) space is split evenly over the grid (stream-K); CTAs that share a
+// tile add their pieces in CTA order, so the result is deterministic.
 template <int T, int NMAT, int EPI, typename XT, typename ST>
-__global__ void __launch_bounds__(kThreads, (GemvCfg<T, NMAT>::kMinBlocks))
-q80_gemv_kernel(const Params p) {
-  constexpr int UNR = GemvCfg<T, NMAT>::kUnroll;
-  __shared__ float red[kWarps][NMAT * T * kCols];
-  __shared__ float fin[NMAT * T * kCols];
-  __shared__ int s_last;
+__global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_constant__ Params p) {
+  using C = GemvCfg<T, NMAT, XT, ST>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  float* red = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  float* fin = red + C::kRedFloats;
+  uint64_t* full = reinterpret_cast<uint64_t*>(fin + C::kFinFloats);
+  uint64_t* empty = full + C::kStages;
+  int* s_last = reinterpret_cast<int*>(empty + C::kStages);
 
-  const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int rs = lane >> 3;
-  const int cc = lane & 7;
+  const int lane = threadIdx.x & 31;
   const int G = gridDim.x;
   const int c = blockIdx.x;
   const int64_t U = p.total_units;
-  int64_t u = (static_cast<int64_t>(c) * U) / G;
+  const int64_t u_begin = (static_cast<int64_t>(c) * U) / G;
   const int64_t u_end = (static_cast<int64_t>(c + 1) * U) / G;
-  const int nsb = p.N / 32;
-  const int8_t* qm[2] = {p.q0, p.q1};
-  const void* sm[2] = {p.s0, p.s1};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
   uint32_t epoch = 0;
   if constexpr (EPI == EPI_TP) epoch = comm::epoch_begin(p.comm);
 
-  while (u < u_end) {
-    const int tile = static_cast<int>(u / p.upt);
-    const int64_t tile_u0 = static_cast<int64_t>(tile) * p.upt;
-    const int64_t seg_end = min(u_end, tile_u0 + p.upt);
-    const int col0 = tile * kCols + cc * 16;
-    const bool col_ok = col0 < p.N;
-
-    float acc[NMAT][T][16];
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-      for (int t = 0; t < T; ++t)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[m][t][i] = 0.f;
-
-    for (int64_t ub = u; ub < seg_end; ub += UNR) {
-      int4 wv[UNR][NMAT];
-      float sv[UNR][NMAT];
-      float xv[UNR][T];
-#pragma unroll
-      for (int j = 0; j < UNR; ++j) {
-        const int64_t uj = ub + j;
-        const int k = static_cast<int>((uj - tile_u0) * kUnitRows) + warp * 4 + rs;
-        const bool ok = col_ok && (uj < seg_end) && (k < p.K);
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          if (ok) {
-            wv[j][m] = ld_stream16(qm[m] + static_cast<int64_t>(k) * p.N + col0);
-            sv[j][m] = ld_scale<ST>(sm[m], static_cast<int64_t>(k) * nsb + (col0 >> 5));
-          } else {
-            wv[j][m] = make_int4(0, 0, 0, 0);
-            sv[j][m] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int t = 0; t < T; ++t) xv[j][t] = ok ? ld_x<XT>(p.x, static_cast<int64_t>(t) * p.K + k) : 0.f;
+  if (warp == kConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      for (int m = 0; m < NMAT; ++m) {
+        prefetch_tmap(&p.tq[m]);
+        prefetch_tmap(&p.ts[m]);
       }
-#pragma unroll
-      for (int j = 0; j < UNR; ++j) {
-#pragma unroll
+      prefetch_tmap(&p.tx);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t u = u_begin; u < u_end; ++u) {
+        const int tile = static_cast<int>(u / p.upt);
+        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.upt) * kUnitRows;
+        mbar_wait(&empty[s], ph ^ 1u, p.status);
+        uint8_t* st = stages + s * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[s], C::kTxBytes);
         for (int m = 0; m < NMAT; ++m) {
-          const uint32_t words[4] = {static_cast<uint32_t>(wv[j][m].x), static_cast<uint32_t>(wv[j][m].y),
-                                     static_cast<uint32_t>(wv[j][m].z), static_cast<uint32_t>(wv[j][m].w)};
-          float a[T];
-#pragma unroll
-          for (int t = 0; t < T; ++t) a[t] = xv[j][t] * sv[j][m];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            float f[4];
-            s8x4_to_f32(words[w], f);
-#pragma unroll
-            for (int t = 0; t < T; ++t)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) acc[m][t][w * 4 + i] = fmaf(a[t], f[i], acc[m][t][w * 4 + i]);
-          }
+          tma_load_2d(st + m * C::kQBytes, &p.tq[m], tile * kTileN, k0, &full[s]);
+          tma_load_2d(st + NMAT * C::kQBytes + m * C::kSBytes, &p.ts[m], tile * 8, k0, &full[s]);
+        }
+        tma_load_2d(st + NMAT * (C::kQBytes + C::kSBytes), &p.tx, k0, 0, &full[s]);
+        if (++s == C::kStages) {
+          s = 0;
+          ph ^= 1u;
         }
       }
     }
+  } else {
+    // ---------------- consumers ----------------
+    const int tid = threadIdx.x;
+    const int rs = lane >> 4;
+    const int cc = lane & 15;
+    int s = 0;
+    uint32_t ph = 0;
+    int64_t u = u_begin;
+    while (u < u_end) {
+      const int tile = static_cast<int>(u / p.upt);
+      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.upt;
+      const int64_t seg_end = min(u_end, tile_u0 + p.upt);
 
-    u = seg_end;
-
-    // reduce the 4 row lanes of each column chunk, then across warps
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-      for (int t = 0; t < T; ++t)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v = acc[m][t][i];
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          acc[m][t][i] = v;
-        }
-    if (rs == 0) {
+      float2 acc[NMAT][T][8];
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
 #pragma unroll
         for (int t = 0; t < T; ++t)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) red[warp][(m * T + t) * kCols + cc * 16 + i] = acc[m][t][i];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < NMAT * T * kCols; i += kThreads) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += red[w][i];
-      fin[i] = v;
-    }
-    __syncthreads();
+          for (int i = 0; i < 8; ++i) acc[m][t][i] = make_float2(0.f, 0.f);
 
-    const int cf = cta_of_unit(tile_u0, U, G);
-    const int cl = cta_of_unit(tile_u0 + p.upt - 1, U, G);
-    if (cf == cl) {
-      tile_epilogue<T, NMAT, EPI>(p, tile, fin, epoch);
-    } else {
-      const int piece = c - cf;
-      const int np = cl - cf + 1;
-      float* slot = p.ws + (static_cast<int64_t>(tile) * p.pmax + piece) * (NMAT * T * kCols);
-      for (int i = threadIdx.x; i < NMAT * T * kCols; i += kThreads) __stcg(slot + i, fin[i]);
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(p.counters + tile, 1u);
-        s_last = (prev == static_cast<unsigned>(np - 1));
-      }
-      __syncthreads();
-      if (s_last) {
-        __threadfence();
-        const float* base = p.ws + static_cast<int64_t>(tile) * p.pmax * (NMAT * T * kCols);
-        for (int i = threadIdx.x; i < NMAT * T * kCols; i += kThreads) {
-          float v = 0.f;
-          for (int pc = 0; pc < np; ++pc) v += __ldcg(base + static_cast<int64_t>(pc) * (NMAT * T * kCols) + i);
-          fin[i] = v;
+      for (; u < seg_end; ++u) {
+        mbar_wait(&full[s], ph, p.status);
+        const uint8_t* st = stages + s * C::kStageBytes;
+        const ST* ss = reinterpret_cast<const ST*>(st + NMAT * C::kQBytes);
+        const XT* xs = reinterpret_cast<const XT*>(st + NMAT * (C::kQBytes + C::kSBytes));
+#pragma unroll
+        for (int pass = 0; pass < 2; ++pass) {
+          const int r = pass * 16 + warp * 2 + rs;
+          float xv[T];
+#pragma unroll
+          for (int t = 0; t < T; ++t) xv[t] = to_f32(xs[t * kUnitRows + r]);
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            const float sc = to_f32(ss[m * (C::kSBytes / sizeof(ST)) + r * 8 + (cc >> 1)]);
+            const int4 w = *reinterpret_cast<const int4*>(st + m * C::kQBytes + r * kTileN + cc * 16);
+            const uint32_t words[4] = {static_cast<uint32_t>(w.x), static_cast<uint32_t>(w.y),
+                                       static_cast<uint32_t>(w.z), static_cast<uint32_t>(w.w)};
+            float2 a2[T];
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+              const float a = xv[t] * sc;
+              a2[t] = make_float2(a, a);
+            }
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const uint32_t uu = words[wi] ^ 0x80808080u;
+              const float2 magic = make_float2(-8388736.0f, -8388736.0f);
+              const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(uu, 0x4B000000u, 0x7540u)),
+                                                        __uint_as_float(__byte_perm(uu, 0x4B000000u, 0x7541u))),
+                                            magic);
+              const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(uu, 0x4B000000u, 0x7542u)),
+                                                        __uint_as_float(__byte_perm(uu, 0x4B000000u, 0x7543u))),
+                                            magic);
+#pragma unroll
+              for (int t = 0; t < T; ++t) {
+                acc[m][t][wi * 2] = __ffma2_rn(a2[t], f01, acc[m][t][wi * 2]);
+                acc[m][t][wi * 2 + 1] = __ffma2_rn(a2[t], f23, acc[m][t][wi * 2 + 1]);
+              }
+            }
+          }
         }
-        __syncthreads();
-        tile_epilogue<T, NMAT, EPI>(p, tile, fin, epoch);
-        if (threadIdx.x == 0) p.counters[tile] = 0u;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == C::kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
+
+      // reduce the two row lanes of each column chunk, then across warps
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float2 v = acc[m][t][i];
+            v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
+            v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
+            acc[m][t][i] = v;
+          }
+      if (rs == 0) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+          for (int t = 0; t < T; ++t) {
+            float4* dst = reinterpret_cast<float4*>(red + static_cast<int64_t>(warp) * NMAT * T * kTileN +
+                                                    (m * T + t) * kTileN + cc * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_float4(acc[m][t][2 * i].x, acc[m][t][2 * i].y, acc[m][t][2 * i + 1].x,
+                                   acc[m][t][2 * i + 1].y);
+          }
+      }
+      consumer_sync();
+      for (int i = tid; i < NMAT * T * kTileN; i += kConsumers) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) v += red[w * NMAT * T * kTileN + i];
+        fin[i] = v;
+      }
+      consumer_sync();
+
+      const int cf = cta_of_unit(tile_u0, U, G);
+      const int cl = cta_of_unit(tile_u0 + p.upt - 1, U, G);
+      if (cf == cl) {
+        tile_epilogue<T, NMAT, EPI>(p, tile, fin, epoch, tid);
+      } else {
+        const int piece = c - cf;
+        const int np = cl - cf + 1;
+        float* slot = p.ws + (static_cast<int64_t>(tile) * p.pmax + piece) * (NMAT * T * kTileN);
+        for (int i = tid; i < NMAT * T * kTileN; i += kConsumers) __stcg(slot + i, fin[i]);
+        __threadfence();
+        consumer_sync();
+        if (tid == 0) {
+          const unsigned prev = atomicAdd(p.counters + tile, 1u);
+          *s_last = (prev == static_cast<unsigned>(np - 1));
+        }
+        consumer_sync();
+        if (*s_last) {
+          __threadfence();
+          const float* base = p.ws + static_cast<int64_t>(tile) * p.pmax * (NMAT * T * kTileN);
+          for (int i = tid; i < NMAT * T * kTileN; i += kConsumers) {
+            float v = 0.f;
+            for (int pc = 0; pc < np; ++pc) v += __ldcg(base + static_cast<int64_t>(pc) * (NMAT * T * kTileN) + i);
+            fin[i] = v;
+          }
+          consumer_sync();
+          tile_epilogue<T, NMAT, EPI>(p, tile, fin, epoch, tid);
+          if (tid == 0) p.counters[tile] = 0u;
+        }
+      }
+      consumer_sync();
     }
-    __syncthreads();
   }
+  __syncthreads();
   if constexpr (EPI == EPI_TP) comm::epoch_end(p.comm, epoch);
 }
 
@@ -289,7 +366,7 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
   const int ty = threadIdx.x >> 4;   // token group
   const int n0 = blockIdx.x * kGN;
   const int t0 = blockIdx.y * kGM;
-  const int nsb = p.N / 32;
+  const int nsb = p.scale_ld;
   float acc[NMAT][4][4];
 #pragma unroll
   for (int m = 0; m < NMAT; ++m)
@@ -360,18 +437,7 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
 
 // ---- host side ------------------------------------------------------------------------
 
-int tiles_of(int N) { return (N + kCols - 1) / kCols; }
-
-// Grid of the GEMV for one instantiation: every CTA co-resident, capped by the work.
-template <typename K>
-int gemv_grid(K kernel, int64_t units) {
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, 0) != cudaSuccess || occ < 1) occ = 1;
-  int64_t g = static_cast<int64_t>(occ) * sm_count();
-  if (g > kMaxGrid) g = kMaxGrid;
-  if (g > units) g = units;
-  return static_cast<int>(g < 1 ? 1 : g);
-}
+int tiles_of(int N) { return (N + kTileN - 1) / kTileN; }
 
 int pmax_for(int tiles, int upt, int G) {
   const int64_t U = static_cast<int64_t>(tiles) * upt;
@@ -385,23 +451,55 @@ int pmax_for(int tiles, int upt, int G) {
 }
 
 // Upper bound of the piece workspace for any grid <= kMaxGrid.
-int64_t gemv_ws_bytes(int T, int K, int N, int nmat) {
+int64_t gemv_ws_bytes(int T, int N, int nmat) {
   const int tiles = tiles_of(N);
   const int64_t pmax = (kMaxGrid + tiles - 1) / tiles + 1;
-  (void)K;
-  return static_cast<int64_t>(tiles) * pmax * nmat * T * kCols * 4;
+  return static_cast<int64_t>(tiles) * pmax * nmat * T * kTileN * 4;
 }
 
 constexpr int64_t kCounterBytes = kCounterWords * 4;
 
+template <typename XT>
+CUtensorMapDataType tma_dtype();
+template <>
+CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <>
+CUtensorMapDataType tma_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <>
+CUtensorMapDataType tma_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+
 template <int T, int NMAT, int EPI, typename XT, typename ST>
 int launch_gemv(Params p, cudaStream_t s) {
+  using C = GemvCfg<T, NMAT, XT, ST>;
   auto kern = q80_gemv_kernel<T, NMAT, EPI, XT, ST>;
-  const int G = gemv_grid(kern, p.total_units);
+  static bool attr_set[64] = {};  // per instantiation and device
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    PYRE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  // tensor maps
+  const int8_t* qs[2] = {p.q0, p.q1};
+  const void* ss[2] = {p.s0, p.s1};
+  for (int m = 0; m < NMAT; ++m) {
+    int rc = make_tmap_2d(&p.tq[m], qs[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.N, p.N, kUnitRows, kTileN);
+    if (rc) return rc;
+    rc = make_tmap_2d(&p.ts[m], ss[m], tma_dtype<ST>(), sizeof(ST), p.K, p.scale_ld,
+                      static_cast<uint64_t>(p.scale_ld) * sizeof(ST), kUnitRows, 8);
+    if (rc) return rc;
+  }
+  int rc = make_tmap_2d(&p.tx, p.x, tma_dtype<XT>(), sizeof(XT), p.T, p.K, static_cast<uint64_t>(p.K) * sizeof(XT),
+                        T, kUnitRows);
+  if (rc) return rc;
+  int64_t g = sm_count();
+  if (g > kMaxGrid) g = kMaxGrid;
+  if (g > p.total_units) g = p.total_units;
+  const int G = static_cast<int>(g < 1 ? 1 : g);
   p.pmax = pmax_for(p.tiles, p.upt, G);
-  if (static_cast<int64_t>(p.tiles) * p.pmax * NMAT * T * kCols * 4 > p.ws_cap)
+  if (static_cast<int64_t>(p.tiles) * p.pmax * NMAT * T * kTileN * 4 > p.ws_cap)
     return set_error(PYRE_ENOMEM, "q80_gemv: stream-K workspace too small for this grid");
-  kern<<<G, kThreads, 0, s>>>(p);
+  kern<<<G, kThreads, C::kSmemBytes, s>>>(p);
   PYRE_LAUNCH_CHECK("q80_gemv_kernel");
   return PYRE_OK;
 }
@@ -433,7 +531,7 @@ int dispatch_types(Params p, int x_dtype, int scale_dtype, cudaStream_t s) {
   return dispatch_T<NMAT, EPI, float, float>(p, s);
 }
 
-int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
+int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, int scale_ld, const void* out,
                  const void* ws, int64_t ws_bytes, const char* fn) {
   std::string f(fn);
   PYRE_CHECK_ARG(x != nullptr && out != nullptr, f + ": null input/output");
@@ -441,16 +539,22 @@ int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtyp
   PYRE_CHECK_ARG(N % 32 == 0, f + ": output width must be a multiple of 32 (Q8_0 blocks run along it)");
   PYRE_CHECK_ARG(x_dtype == PYRE_F32 || x_dtype == PYRE_BF16, f + ": activation dtype must be f32 or bf16");
   PYRE_CHECK_ARG(scale_dtype == PYRE_F32 || scale_dtype == PYRE_F16, f + ": scale dtype must be f32 or f16");
-  PYRE_CHECK_ARG(tiles_of(N) <= kCounterWords, f + ": output width too large");
+  PYRE_CHECK_ARG(scale_ld >= N / 32, f + ": scale_ld must be >= N/32");
+  PYRE_CHECK_ARG((static_cast<int64_t>(scale_ld) * (scale_dtype == PYRE_F16 ? 2 : 4)) % 16 == 0,
+                 f + ": scale rows must be 16-byte multiples (pad scale_ld)");
+  PYRE_CHECK_ARG(tiles_of(N) <= kMaxTiles, f + ": output width too large");
+  PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || (static_cast<int64_t>(K) * (x_dtype == PYRE_BF16 ? 2 : 4)) % 16 == 0,
+                 f + ": activation rows must be 16-byte multiples");
   PYRE_CHECK_ARG(ws != nullptr || T > PYRE_FUSED_REDUCE_MAX_T, f + ": null workspace");
   PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(ws) % 16 == 0, f + ": workspace must be 16-byte aligned");
+  PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0, f + ": activations must be 16-byte aligned");
   PYRE_CHECK_ARG(ws_bytes >= 0, f + ": negative workspace size");
   return PYRE_OK;
 }
 
-int64_t ws_need(int T, int K, int N, int nmat) {
+int64_t ws_need(int T, int N, int nmat) {
   if (T > PYRE_FUSED_REDUCE_MAX_T) return 0;
-  return kCounterBytes + gemv_ws_bytes(T, K, N, nmat);
+  return kCounterBytes + gemv_ws_bytes(T, N, nmat);
 }
 
 }  // namespace ffn
@@ -462,8 +566,8 @@ using namespace pyre::ffn;
 extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   PYRE_CHECK_ARG(bytes != nullptr, "pyre_ffn_workspace_bytes: null bytes");
   PYRE_CHECK_ARG(T >= 1 && H >= 1 && W >= 1, "pyre_ffn_workspace_bytes: sizes must be positive");
-  const int64_t a = ws_need(T, H, W, 2);   // gate/up: K = H, N = W
-  const int64_t b = ws_need(T, W, H, 1);   // down:    K = W, N = H
+  const int64_t a = ws_need(T, W, 2);   // gate/up: K = H, N = W
+  const int64_t b = ws_need(T, H, 1);   // down:    K = W, N = H
   int64_t need = std::max(a, b);
   if (need < kCounterBytes) need = kCounterBytes;
   *bytes = need;
@@ -472,15 +576,16 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
 
 extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H, const int8_t* qg,
                                         const void* sg, const int8_t* qu, const void* su, int scale_dtype,
-                                        int W, void* h, int h_dtype, void* workspace, int64_t ws_bytes,
-                                        void* stream) {
-  int rc = check_common(x, x_dtype, T, H, W, scale_dtype, h, workspace, ws_bytes, "pyre_ffn_gateup_silu_q80");
+                                        int scale_ld, int W, void* h, int h_dtype, void* workspace,
+                                        int64_t ws_bytes, void* stream) {
+  int rc = check_common(x, x_dtype, T, H, W, scale_dtype, scale_ld, h, workspace, ws_bytes,
+                        "pyre_ffn_gateup_silu_q80");
   if (rc) return rc;
   PYRE_CHECK_ARG(qu != nullptr && su != nullptr, "pyre_ffn_gateup_silu_q80: null up weight");
   PYRE_CHECK_ARG((qg == nullptr) == (sg == nullptr), "pyre_ffn_gateup_silu_q80: gate q/scale mismatch");
   PYRE_CHECK_ARG(h_dtype == PYRE_F32 || h_dtype == PYRE_BF16, "pyre_ffn_gateup_silu_q80: h dtype must be f32 or bf16");
   const bool gated = qg != nullptr;
-  const int64_t need = ws_need(T, H, W, gated ? 2 : 1);
+  const int64_t need = ws_need(T, W, gated ? 2 : 1);
   if (ws_bytes < need)
     return set_error(PYRE_ENOMEM, "pyre_ffn_gateup_silu_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   Params p{};
@@ -488,10 +593,12 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   p.K = H;
   p.N = W;
   p.T = T;
+  p.scale_ld = scale_ld;
   p.tiles = tiles_of(W);
   p.upt = (H + kUnitRows - 1) / kUnitRows;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = static_cast<unsigned int*>(workspace);
+  p.status = static_cast<int*>(workspace) + (kCounterWords - 1);
   p.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   p.ws_cap = ws_bytes - kCounterBytes;
   p.out = h;
@@ -506,12 +613,12 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
 }
 
 extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const int8_t* qd, const void* sd,
-                                 int scale_dtype, int H, float* out, void* workspace, int64_t ws_bytes,
-                                 pyre_comm_t* comm, void* stream) {
-  int rc = check_common(h, h_dtype, T, W, H, scale_dtype, out, workspace, ws_bytes, "pyre_ffn_down_q80");
+                                 int scale_dtype, int scale_ld, int H, float* out, void* workspace,
+                                 int64_t ws_bytes, pyre_comm_t* comm, void* stream) {
+  int rc = check_common(h, h_dtype, T, W, H, scale_dtype, scale_ld, out, workspace, ws_bytes, "pyre_ffn_down_q80");
   if (rc) return rc;
   PYRE_CHECK_ARG(qd != nullptr && sd != nullptr, "pyre_ffn_down_q80: null weight");
-  const int64_t need = ws_need(T, W, H, 1);
+  const int64_t need = ws_need(T, H, 1);
   if (ws_bytes < need)
     return set_error(PYRE_ENOMEM, "pyre_ffn_down_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   if (comm != nullptr) {
@@ -524,10 +631,12 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   p.K = W;
   p.N = H;
   p.T = T;
+  p.scale_ld = scale_ld;
   p.tiles = tiles_of(H);
   p.upt = (W + kUnitRows - 1) / kUnitRows;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = static_cast<unsigned int*>(workspace);
+  p.status = static_cast<int*>(workspace) + (kCounterWords - 1);
   p.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   p.ws_cap = ws_bytes - kCounterBytes;
   p.out = out;

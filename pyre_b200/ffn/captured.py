@@ -53,6 +53,7 @@ class CapturedFfn:
         partial (the op's cross-rank sum when it has a communicator). The returned tensor
         is the runner's pinned output buffer, overwritten by the next call."""
         self.x_host.copy_(torch.as_tensor(x).reshape(self.x_host.shape))
-        self.graph.replay()
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
         self.stream.synchronize()
         return self.out_host

@@ -11,7 +11,10 @@ with the arithmetic done by the sm_100a kernels of ``libpyre_b200.so``:
 
 :class:`Q80Weight` is the GEMV/GEMM operand: int8 ``q[K, N]`` plus scales ``[K, N/32]``
 (f16 by default, f32 for the exact-scale variant), i.e. the reference tuple reshaped so
-each row of the stored ``[in, out]`` matrix is ``N/32`` whole blocks.
+each row of the stored ``[in, out]`` matrix is ``N/32`` whole blocks. Scale rows are padded
+with zeros to a multiple of 16 bytes (``scale_ld`` entries) so the kernels can stream
+them with TMA; for N a multiple of 256 there is no padding and the scales are exactly the
+reference's flat array.
 """
 from __future__ import annotations
 
@@ -136,15 +139,31 @@ def _numel(v) -> int:
     return int(v.numel()) if isinstance(v, torch.Tensor) else int(v.size)
 
 
+def pad_scale_rows(s: torch.Tensor) -> torch.Tensor:
+    """[K, nb] scales -> [K, scale_ld] with zero padding so each row is 16-byte aligned."""
+    per16 = 16 // s.element_size()
+    nb = s.shape[1]
+    ld = (nb + per16 - 1) // per16 * per16
+    if ld == nb:
+        return s.contiguous()
+    out = torch.zeros((s.shape[0], ld), dtype=s.dtype, device=s.device)
+    out[:, :nb] = s
+    return out
+
+
 @dataclass
 class Q80Weight:
     """A ``[K, N]`` weight (stored ``[in, out]`` like the reference) in Q8_0 on the device.
 
-    ``q`` is int8 ``[K, N]``; ``scale`` is f16 (default) or f32 ``[K, N/32]``.
+    ``q`` is int8 ``[K, N]``; ``scale`` is f16 (default) or f32 ``[K, scale_ld]`` whose first
+    ``N/32`` entries per row are the block scales (the rest is zero padding).
     """
 
     q: torch.Tensor
     scale: torch.Tensor
+
+    def __post_init__(self):
+        self.scale = pad_scale_rows(self.scale)
 
     @property
     def shape(self) -> Tuple[int, int]:
@@ -155,8 +174,18 @@ class Q80Weight:
         return D.dtype_code(self.scale)
 
     @property
+    def scale_ld(self) -> int:
+        return int(self.scale.shape[1])
+
+    @property
+    def block_scales(self) -> torch.Tensor:
+        """Unpadded ``[K, N/32]`` scales."""
+        return self.scale[:, : self.q.shape[1] // BLOCK]
+
+    @property
     def nbytes(self) -> int:
-        return self.q.numel() + self.scale.numel() * self.scale.element_size()
+        """Bytes of the format proper (int8 + one scale per 32 weights, padding excluded)."""
+        return self.q.numel() + self.block_scales.numel() * self.scale.element_size()
 
     @classmethod
     def from_float(cls, w, scale_dtype: torch.dtype = torch.float16) -> "Q80Weight":
@@ -178,7 +207,7 @@ class Q80Weight:
         N.call("pyre_q80_quantize", D.ptr(t), D.dtype_code(t), K * Nn, D.ptr(q), D.ptr(s32), D.ptr(s16),
                D.stream_ptr())
         del nb
-        return cls(q, s32 if s32 is not None else s16)
+        return cls(q, s32 if s32 is not None else s16)  # rows padded in __post_init__
 
     @classmethod
     def from_tuple(cls, tup, scale_dtype: torch.dtype | None = None) -> "Q80Weight":
@@ -201,9 +230,15 @@ class Q80Weight:
     def dequantize(self) -> torch.Tensor:
         K, Nn = self.shape
         out = torch.empty((K, Nn), dtype=torch.float32, device=self.q.device)
-        N.call("pyre_q80_dequantize", D.ptr(self.q), D.ptr(self.scale), self.scale_code, K * Nn, D.ptr(out),
+        s = self.block_scales.contiguous()
+        N.call("pyre_q80_dequantize", D.ptr(self.q), D.ptr(s), self.scale_code, K * Nn, D.ptr(out),
                D.stream_ptr())
         return out
+
+    def to_tuple(self) -> tuple:
+        """Reference tuple ``("q8", q [n_blocks, 32], scales [n_blocks], shape)`` (device tensors)."""
+        K, Nn = self.shape
+        return ("q8", self.q.reshape(-1, BLOCK), self.block_scales.contiguous().reshape(-1), (K, Nn))
 
     def cols(self, start: int, end: int) -> "Q80Weight":
         """Columns [start, end) (a gate/up shard); both multiples of 32."""
