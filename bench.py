@@ -399,7 +399,7 @@ def _gateup(op, x, gq, uq, h, stream):
     import ctypes
     from pyre_b200 import _device as D, _native as N
     N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), x.shape[0], op.hidden, D.ptr(gq.q),
-           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, uq.scale_ld, op.width, D.ptr(h),
+           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, op.width, D.ptr(h),
            D.dtype_code(h),
            D.ptr(op.workspace), op.workspace.numel(), ctypes.c_void_p(stream.cuda_stream))
 
@@ -408,7 +408,7 @@ def _down(op, h, dq, out, stream):
     import ctypes
     from pyre_b200 import _device as D, _native as N
     N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), h.shape[0], op.width, D.ptr(dq.q), D.ptr(dq.scale),
-           dq.scale_code, dq.scale_ld, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
+           dq.scale_code, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
            ctypes.c_void_p(op.comm.handle if op.comm is not None else 0), ctypes.c_void_p(stream.cuda_stream))
 
 

@@ -11,16 +11,18 @@
  * The caller owns every buffer it passes in. The library never frees caller memory;
  * pyre_comm_t owns only what pyre_comm_create() allocates (peer table, status word).
  *
- * Q8_0 device format (the reference's own orientation, see
- * src/orchestrator/quantizer.py:11-26 and src/orchestrator/llama_loader.py:1132-1134):
- * a weight stored as [K, N] row-major float (K = input dim, N = output dim) is
- * quantized in flattened C order in 32-element blocks, so each block runs along N.
- *   q      int8  [K, N]
- *   scale  f32 or f16 [K, scale_ld], scale_ld >= N/32   (scale[k, j/32] belongs to q[k, j])
- * N must be a multiple of 32 for the GEMV/GEMM entry points, and every scale row must
- * start on a 16-byte boundary (scale_ld * sizeof(scale) % 16 == 0): the kernels stream
- * weight and scale tiles with TMA. The reference's flat scale array is [K, N/32] with
- * scale_ld = N/32, which satisfies this whenever N is a multiple of 256.
+ * Q8_0 format. The reference quantizes a weight stored as [K, N] row-major float
+ * (K = input dim, N = output dim) in flattened C order in 32-element blocks
+ * (src/orchestrator/quantizer.py:11-26, src/orchestrator/llama_loader.py:1132-1134), so
+ * every block runs along N: q int8 [K, N], scale [K, N/32], scale[k, j/32] for q[k, j].
+ *
+ * Device weight layout (column-slab tiled, used by the FFN entry points): N is padded with
+ * zeros to a multiple of 256 and cut into NT = N_pad/256 slabs; slab j holds
+ *   q     int8        [K, 256]  = q[:, 256j : 256j+256]
+ *   scale f16 or f32  [K, 8]    = scale[:, 8j : 8j+8]
+ * stored slab after slab: q_tiled [NT, K, 256], scale_tiled [NT, K, 8]. The int8 values
+ * and scales are exactly the reference's; each 32-row x 256-column work unit is one
+ * contiguous 8 KB run, which the kernels stream with bulk copies.
  */
 #ifndef PYRE_B200_H
 #define PYRE_B200_H
@@ -85,15 +87,16 @@ PYRE_API int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes);
 
 /* h[T, W] = silu(x @ Wg) * (x @ Wu)      (gated,   src/ffn/builder.py:37-43)
  * h[T, W] = silu(x @ Wu)                 (ungated, src/ffn/builder.py:47-49; qg == NULL)
- * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16), 16-byte aligned rows. Wg, Wu: Q8_0
- * [H, W] (scales [H, scale_ld] of scale_dtype, shared layout for both). h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
+ * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16), 16-byte aligned rows. Wg, Wu: [H, W] in
+ * the tiled device layout (scales of scale_dtype). For T <= PYRE_FUSED_REDUCE_MAX_T the
+ * input dim (H here, W for the down projection) must be a multiple of 32. h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
  * as in pyre_kernels.silu_mul (src/kernels/mojo/pyre_kernels.mojo:121-129).
  * workspace: zero-initialised device memory of at least pyre_ffn_workspace_bytes();
  * it is left zeroed where it must start at zero, so it can be reused call after call on
  * one stream (calls that overlap on the GPU need separate workspaces). */
 PYRE_API int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H,
                              const int8_t* qg, const void* sg,
-                             const int8_t* qu, const void* su, int scale_dtype, int scale_ld, int W,
+                             const int8_t* qu, const void* su, int scale_dtype, int W,
                              void* h, int h_dtype, void* workspace, int64_t ws_bytes,
                              void* stream);
 
@@ -102,10 +105,10 @@ PYRE_API int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H,
  * :982-995, `ffn_out += partial`), in rank order 0..world-1 on every rank. For
  * T <= PYRE_FUSED_REDUCE_MAX_T the reduction happens in the GEMV epilogue through
  * NVLink peer stores and bounded flag waits; above it a two-shot peer-memory
- * all-reduce follows the GEMM. h: [T, W] of h_dtype; Wd: Q8_0 [W, H]; out: f32 [T, H]. */
+ * all-reduce follows the GEMM. h: [T, W] of h_dtype; Wd: [W, H] tiled; out: f32 [T, H]. */
 #define PYRE_FUSED_REDUCE_MAX_T 4
 PYRE_API int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W,
-                      const int8_t* qd, const void* sd, int scale_dtype, int scale_ld, int H,
+                      const int8_t* qd, const void* sd, int scale_dtype, int H,
                       float* out, void* workspace, int64_t ws_bytes,
                       pyre_comm_t* comm, void* stream);
 

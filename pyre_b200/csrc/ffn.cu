@@ -6,14 +6,18 @@
 // Wg, Wu, Wd dequantized from Q8_0 (src/orchestrator/quantizer.py:29-40) as a reference
 // worker does (src/orchestrator/worker_node.py:59-69). Accumulation is f32.
 //
-// Decode GEMV layout. A weight is int8 [K, N] row-major with scales [K, N/32]. The output
-// columns are cut into tiles of 128; a tile is covered by work units of 32 input rows.
-// A warp reads 4 rows x 128 columns per unit step: lane (rs, cc) streams the 16 bytes
-// q[k, 16cc .. 16cc+15] of row k = 4*warp + rs with one 128-bit load, so each row
-// segment is a full 128-byte line. The (tile, unit) space is split evenly over a grid of
-// co-resident CTAs (stream-K): a CTA sums its units of a tile in registers, reduces across
-// its warps in shared memory and, when the tile is shared with other CTAs, the last CTA
-// to finish adds the pieces in CTA order (deterministic) and runs the epilogue.
+// Device weight layout (column-slab tiled Q8_0). A [K, N] weight is cut into slabs of
+// 256 output columns; slab j stores q[:, 256j : 256j+256] row-major (K x 256 int8,
+// contiguous) and its scales [:, 8j : 8j+8] (K x 8), N padded with zeros to a multiple of
+// 256. The values are exactly the reference's Q8_0 blocks; only the order differs, so a
+// 32-row x 256-column work unit is one contiguous 8 KB run of HBM.
+//
+// Decode GEMV: the output columns of a slab form a tile; a tile is covered by work units
+// of 32 input rows. The (tile, unit) space is split evenly over one CTA per SM
+// (stream-K); a CTA streams its units through a shared-memory ring with bulk copies,
+// sums them in registers, reduces across its warps and, when the tile is shared with
+// other CTAs, the last CTA to finish adds the pieces in CTA order (deterministic) and
+// runs the epilogue.
 #include <algorithm>
 
 #include "comm.cuh"
@@ -34,17 +38,13 @@ constexpr int kMaxTiles = kCounterWords - 1;
 enum Epi : int { EPI_SILU_MUL = 0, EPI_SILU = 1, EPI_STORE = 2, EPI_TP = 3 };
 
 struct alignas(64) Params {
-  CUtensorMap tq[2];         // int8 q [K, N], box 32 x 256
-  CUtensorMap ts[2];         // scales [K, scale_ld], box 32 x 8
   CUtensorMap tx;            // activations [T, K], box T x 32
-  // plain pointers (SIMT GEMM path)
   const void* x;
-  const int8_t* q0;
-  const void* s0;
-  const int8_t* q1;
+  const int8_t* q0;          // tiled q [tiles, K, 256]; gate (NMAT == 2) or the single matrix
+  const void* s0;            // tiled scales [tiles, K, 8]
+  const int8_t* q1;          // up (NMAT == 2)
   const void* s1;
   int K, N, T;
-  int scale_ld;              // entries per scale row (>= N/32)
   int tiles;                 // ceil(N / kTileN)
   int upt;                   // units per tile = ceil(K / kUnitRows)
   int64_t total_units;       // tiles * upt
@@ -189,11 +189,9 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_cons
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      for (int m = 0; m < NMAT; ++m) {
-        prefetch_tmap(&p.tq[m]);
-        prefetch_tmap(&p.ts[m]);
-      }
       prefetch_tmap(&p.tx);
+      const int8_t* qm[2] = {p.q0, p.q1};
+      const uint8_t* sm[2] = {static_cast<const uint8_t*>(p.s0), static_cast<const uint8_t*>(p.s1)};
       int s = 0;
       uint32_t ph = 0;
       for (int64_t u = u_begin; u < u_end; ++u) {
@@ -202,9 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_cons
         mbar_wait(&empty[s], ph ^ 1u, p.status);
         uint8_t* st = stages + s * C::kStageBytes;
         mbar_arrive_expect_tx(&full[s], C::kTxBytes);
+        const int64_t row0 = static_cast<int64_t>(tile) * p.K + k0;
         for (int m = 0; m < NMAT; ++m) {
-          tma_load_2d(st + m * C::kQBytes, &p.tq[m], tile * kTileN, k0, &full[s]);
-          tma_load_2d(st + NMAT * C::kQBytes + m * C::kSBytes, &p.ts[m], tile * 8, k0, &full[s]);
+          bulk_load(st + m * C::kQBytes, qm[m] + row0 * kTileN, C::kQBytes, &full[s]);
+          bulk_load(st + NMAT * C::kQBytes + m * C::kSBytes, sm[m] + row0 * (C::kSBytes / kUnitRows), C::kSBytes,
+                    &full[s]);
         }
         tma_load_2d(st + NMAT * (C::kQBytes + C::kSBytes), &p.tx, k0, 0, &full[s]);
         if (++s == C::kStages) {
@@ -366,7 +366,6 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
   const int ty = threadIdx.x >> 4;   // token group
   const int n0 = blockIdx.x * kGN;
   const int t0 = blockIdx.y * kGM;
-  const int nsb = p.scale_ld;
   float acc[NMAT][4][4];
 #pragma unroll
   for (int m = 0; m < NMAT; ++m)
@@ -389,9 +388,11 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
         const int kk = i / kGN, nn = i % kGN;
         const int k = k0 + kk, n = n0 + nn;
         float w = 0.f;
-        if (k < p.K && n < p.N)
-          w = static_cast<float>(qm[m][static_cast<int64_t>(k) * p.N + n]) *
-              ld_scale<ST>(sm[m], static_cast<int64_t>(k) * nsb + (n >> 5));
+        if (k < p.K && n < p.N) {
+          const int64_t row = static_cast<int64_t>(n / kTileN) * p.K + k;
+          w = static_cast<float>(qm[m][row * kTileN + (n % kTileN)]) *
+              ld_scale<ST>(sm[m], row * 8 + ((n % kTileN) >> 5));
+        }
         wsm[m][kk][nn] = w;
       }
     }
@@ -479,16 +480,6 @@ int launch_gemv(Params p, cudaStream_t s) {
     PYRE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  // tensor maps
-  const int8_t* qs[2] = {p.q0, p.q1};
-  const void* ss[2] = {p.s0, p.s1};
-  for (int m = 0; m < NMAT; ++m) {
-    int rc = make_tmap_2d(&p.tq[m], qs[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.N, p.N, kUnitRows, kTileN);
-    if (rc) return rc;
-    rc = make_tmap_2d(&p.ts[m], ss[m], tma_dtype<ST>(), sizeof(ST), p.K, p.scale_ld,
-                      static_cast<uint64_t>(p.scale_ld) * sizeof(ST), kUnitRows, 8);
-    if (rc) return rc;
-  }
   int rc = make_tmap_2d(&p.tx, p.x, tma_dtype<XT>(), sizeof(XT), p.T, p.K, static_cast<uint64_t>(p.K) * sizeof(XT),
                         T, kUnitRows);
   if (rc) return rc;
@@ -531,7 +522,7 @@ int dispatch_types(Params p, int x_dtype, int scale_dtype, cudaStream_t s) {
   return dispatch_T<NMAT, EPI, float, float>(p, s);
 }
 
-int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, int scale_ld, const void* out,
+int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
                  const void* ws, int64_t ws_bytes, const char* fn) {
   std::string f(fn);
   PYRE_CHECK_ARG(x != nullptr && out != nullptr, f + ": null input/output");
@@ -539,9 +530,7 @@ int check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtyp
   PYRE_CHECK_ARG(N % 32 == 0, f + ": output width must be a multiple of 32 (Q8_0 blocks run along it)");
   PYRE_CHECK_ARG(x_dtype == PYRE_F32 || x_dtype == PYRE_BF16, f + ": activation dtype must be f32 or bf16");
   PYRE_CHECK_ARG(scale_dtype == PYRE_F32 || scale_dtype == PYRE_F16, f + ": scale dtype must be f32 or f16");
-  PYRE_CHECK_ARG(scale_ld >= N / 32, f + ": scale_ld must be >= N/32");
-  PYRE_CHECK_ARG((static_cast<int64_t>(scale_ld) * (scale_dtype == PYRE_F16 ? 2 : 4)) % 16 == 0,
-                 f + ": scale rows must be 16-byte multiples (pad scale_ld)");
+  PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || K % 32 == 0, f + ": the input dim must be a multiple of 32");
   PYRE_CHECK_ARG(tiles_of(N) <= kMaxTiles, f + ": output width too large");
   PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || (static_cast<int64_t>(K) * (x_dtype == PYRE_BF16 ? 2 : 4)) % 16 == 0,
                  f + ": activation rows must be 16-byte multiples");
@@ -576,10 +565,9 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
 
 extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H, const int8_t* qg,
                                         const void* sg, const int8_t* qu, const void* su, int scale_dtype,
-                                        int scale_ld, int W, void* h, int h_dtype, void* workspace,
-                                        int64_t ws_bytes, void* stream) {
-  int rc = check_common(x, x_dtype, T, H, W, scale_dtype, scale_ld, h, workspace, ws_bytes,
-                        "pyre_ffn_gateup_silu_q80");
+                                        int W, void* h, int h_dtype, void* workspace, int64_t ws_bytes,
+                                        void* stream) {
+  int rc = check_common(x, x_dtype, T, H, W, scale_dtype, h, workspace, ws_bytes, "pyre_ffn_gateup_silu_q80");
   if (rc) return rc;
   PYRE_CHECK_ARG(qu != nullptr && su != nullptr, "pyre_ffn_gateup_silu_q80: null up weight");
   PYRE_CHECK_ARG((qg == nullptr) == (sg == nullptr), "pyre_ffn_gateup_silu_q80: gate q/scale mismatch");
@@ -593,7 +581,6 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   p.K = H;
   p.N = W;
   p.T = T;
-  p.scale_ld = scale_ld;
   p.tiles = tiles_of(W);
   p.upt = (H + kUnitRows - 1) / kUnitRows;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
@@ -613,9 +600,9 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
 }
 
 extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const int8_t* qd, const void* sd,
-                                 int scale_dtype, int scale_ld, int H, float* out, void* workspace,
-                                 int64_t ws_bytes, pyre_comm_t* comm, void* stream) {
-  int rc = check_common(h, h_dtype, T, W, H, scale_dtype, scale_ld, out, workspace, ws_bytes, "pyre_ffn_down_q80");
+                                 int scale_dtype, int H, float* out, void* workspace, int64_t ws_bytes,
+                                 pyre_comm_t* comm, void* stream) {
+  int rc = check_common(h, h_dtype, T, W, H, scale_dtype, out, workspace, ws_bytes, "pyre_ffn_down_q80");
   if (rc) return rc;
   PYRE_CHECK_ARG(qd != nullptr && sd != nullptr, "pyre_ffn_down_q80: null weight");
   const int64_t need = ws_need(T, H, 1);
@@ -631,7 +618,6 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   p.K = W;
   p.N = H;
   p.T = T;
-  p.scale_ld = scale_ld;
   p.tiles = tiles_of(H);
   p.upt = (W + kUnitRows - 1) / kUnitRows;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;

@@ -76,8 +76,8 @@ class FfnShardOp:
                 continue
             if tuple(w.shape) != shp:
                 raise ValueError(f"{name} weight must be {shp}, got {tuple(w.shape)}")
-        if gate is not None and (gate.scale.dtype != up.scale.dtype or gate.scale_ld != up.scale_ld):
-            raise ValueError("gate and up scales must share a dtype and row stride")
+        if gate is not None and gate.scale.dtype != up.scale.dtype:
+            raise ValueError("gate and up scales must share a dtype")
         s = D.stream_ptr(stream)
         h = torch.empty((T, self.width), dtype=self.h_dtype(T), device=x.device)
         if out is None:
@@ -85,9 +85,9 @@ class FfnShardOp:
         ws = self.workspace
         N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
                D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
-               D.ptr(up.q), D.ptr(up.scale), up.scale_code, up.scale_ld, self.width,
+               D.ptr(up.q), D.ptr(up.scale), up.scale_code, self.width,
                D.ptr(h), D.dtype_code(h), D.ptr(ws), ws.numel(), s)
         N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), T, self.width, D.ptr(down.q), D.ptr(down.scale),
-               down.scale_code, down.scale_ld, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(),
+               down.scale_code, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(),
                ctypes.c_void_p(self.comm.handle if self.comm is not None else 0), s)
         return out

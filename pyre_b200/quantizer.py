@@ -9,12 +9,11 @@ with the arithmetic done by the sm_100a kernels of ``libpyre_b200.so``:
 * :func:`quantize_weights_dict` / :func:`dequantize_weights_dict` — ``quantizer.py:70-114``
   (``("q8", q, s, shape)`` tags, ``MIN_QUANTIZE_ELEMS`` threshold).
 
-:class:`Q80Weight` is the GEMV/GEMM operand: int8 ``q[K, N]`` plus scales ``[K, N/32]``
-(f16 by default, f32 for the exact-scale variant), i.e. the reference tuple reshaped so
-each row of the stored ``[in, out]`` matrix is ``N/32`` whole blocks. Scale rows are padded
-with zeros to a multiple of 16 bytes (``scale_ld`` entries) so the kernels can stream
-them with TMA; for N a multiple of 256 there is no padding and the scales are exactly the
-reference's flat array.
+:class:`Q80Weight` is the GEMV/GEMM operand: the reference's Q8_0 blocks of a ``[K, N]``
+weight (stored ``[in, out]``), laid out in column slabs of 256 (``q [NT, K, 256]`` int8,
+``scale [NT, K, 8]`` f16 by default or f32), N zero-padded to a multiple of 256. Each
+32-row unit of a slab is one contiguous 8 KB run that the kernels stream with bulk
+copies; the int8 values and scales are exactly the reference's.
 """
 from __future__ import annotations
 
@@ -139,53 +138,56 @@ def _numel(v) -> int:
     return int(v.numel()) if isinstance(v, torch.Tensor) else int(v.size)
 
 
-def pad_scale_rows(s: torch.Tensor) -> torch.Tensor:
-    """[K, nb] scales -> [K, scale_ld] with zero padding so each row is 16-byte aligned."""
-    per16 = 16 // s.element_size()
-    nb = s.shape[1]
-    ld = (nb + per16 - 1) // per16 * per16
-    if ld == nb:
-        return s.contiguous()
-    out = torch.zeros((s.shape[0], ld), dtype=s.dtype, device=s.device)
-    out[:, :nb] = s
-    return out
+SLAB = 256
+SLAB_SCALES = SLAB // BLOCK
 
 
 @dataclass
 class Q80Weight:
-    """A ``[K, N]`` weight (stored ``[in, out]`` like the reference) in Q8_0 on the device.
+    """A ``[K, N]`` weight in Q8_0, column-slab tiled on the device (see module doc)."""
 
-    ``q`` is int8 ``[K, N]``; ``scale`` is f16 (default) or f32 ``[K, scale_ld]`` whose first
-    ``N/32`` entries per row are the block scales (the rest is zero padding).
-    """
-
-    q: torch.Tensor
-    scale: torch.Tensor
-
-    def __post_init__(self):
-        self.scale = pad_scale_rows(self.scale)
+    q: torch.Tensor       # [NT, K, 256] int8
+    scale: torch.Tensor   # [NT, K, 8] f16 or f32
+    n: int                # logical output width N
 
     @property
     def shape(self) -> Tuple[int, int]:
-        return tuple(self.q.shape)
+        return (int(self.q.shape[1]), int(self.n))
 
     @property
     def scale_code(self) -> int:
         return D.dtype_code(self.scale)
 
     @property
-    def scale_ld(self) -> int:
-        return int(self.scale.shape[1])
+    def nbytes(self) -> int:
+        """Bytes of the format proper (int8 + one scale per 32 weights, padding excluded)."""
+        K, Nn = self.shape
+        return K * Nn + K * (Nn // BLOCK) * self.scale.element_size()
+
+    @classmethod
+    def from_plain(cls, q: torch.Tensor, s: torch.Tensor) -> "Q80Weight":
+        """From plain ``q [K, N]`` int8 and ``s [K, N/32]`` block scales (device tensors)."""
+        K, Nn = q.shape
+        if Nn % BLOCK or tuple(s.shape) != (K, Nn // BLOCK):
+            raise ValueError("Q80Weight.from_plain: need q [K, N] with N % 32 == 0 and s [K, N/32]")
+        nt = (Nn + SLAB - 1) // SLAB
+        qp = torch.zeros((K, nt * SLAB), dtype=torch.int8, device=q.device)
+        qp[:, :Nn] = q
+        sp = torch.zeros((K, nt * SLAB_SCALES), dtype=s.dtype, device=s.device)
+        sp[:, : Nn // BLOCK] = s
+        return cls(qp.view(K, nt, SLAB).permute(1, 0, 2).contiguous(),
+                   sp.view(K, nt, SLAB_SCALES).permute(1, 0, 2).contiguous(), Nn)
+
+    def plain(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Plain ``(q [K, N], s [K, N/32])`` views of the tiled storage (copies)."""
+        nt, K, _ = self.q.shape
+        q = self.q.permute(1, 0, 2).reshape(K, nt * SLAB)[:, : self.n]
+        s = self.scale.permute(1, 0, 2).reshape(K, nt * SLAB_SCALES)[:, : self.n // BLOCK]
+        return q.contiguous(), s.contiguous()
 
     @property
     def block_scales(self) -> torch.Tensor:
-        """Unpadded ``[K, N/32]`` scales."""
-        return self.scale[:, : self.q.shape[1] // BLOCK]
-
-    @property
-    def nbytes(self) -> int:
-        """Bytes of the format proper (int8 + one scale per 32 weights, padding excluded)."""
-        return self.q.numel() + self.block_scales.numel() * self.scale.element_size()
+        return self.plain()[1]
 
     @classmethod
     def from_float(cls, w, scale_dtype: torch.dtype = torch.float16) -> "Q80Weight":
@@ -198,16 +200,15 @@ class Q80Weight:
             raise ValueError(f"output width {Nn} must be a multiple of 32")
         if t.dtype not in (torch.float32, torch.bfloat16):
             t = t.to(torch.float32)
-        q = torch.empty((K, Nn), dtype=torch.int8, device=t.device)
-        nb = K * Nn // BLOCK
-        s32 = torch.empty((K, Nn // BLOCK), dtype=torch.float32, device=t.device) if scale_dtype == torch.float32 else None
-        s16 = torch.empty((K, Nn // BLOCK), dtype=torch.float16, device=t.device) if scale_dtype == torch.float16 else None
-        if s32 is None and s16 is None:
+        if scale_dtype not in (torch.float16, torch.float32):
             raise ValueError("scale_dtype must be torch.float16 or torch.float32")
+        q = torch.empty((K, Nn), dtype=torch.int8, device=t.device)
+        s = torch.empty((K, Nn // BLOCK), dtype=scale_dtype, device=t.device)
+        s32 = s if scale_dtype == torch.float32 else None
+        s16 = s if scale_dtype == torch.float16 else None
         N.call("pyre_q80_quantize", D.ptr(t), D.dtype_code(t), K * Nn, D.ptr(q), D.ptr(s32), D.ptr(s16),
                D.stream_ptr())
-        del nb
-        return cls(q, s32 if s32 is not None else s16)  # rows padded in __post_init__
+        return cls.from_plain(q, s)
 
     @classmethod
     def from_tuple(cls, tup, scale_dtype: torch.dtype | None = None) -> "Q80Weight":
@@ -225,27 +226,27 @@ class Q80Weight:
             st = st.to(scale_dtype)
         elif st.dtype not in (torch.float16, torch.float32):
             st = st.to(torch.float32)
-        return cls(qt.contiguous(), st.contiguous())
+        return cls.from_plain(qt, st)
 
     def dequantize(self) -> torch.Tensor:
         K, Nn = self.shape
+        q, s = self.plain()
         out = torch.empty((K, Nn), dtype=torch.float32, device=self.q.device)
-        s = self.block_scales.contiguous()
-        N.call("pyre_q80_dequantize", D.ptr(self.q), D.ptr(s), self.scale_code, K * Nn, D.ptr(out),
-               D.stream_ptr())
+        N.call("pyre_q80_dequantize", D.ptr(q), D.ptr(s), self.scale_code, K * Nn, D.ptr(out), D.stream_ptr())
         return out
 
     def to_tuple(self) -> tuple:
         """Reference tuple ``("q8", q [n_blocks, 32], scales [n_blocks], shape)`` (device tensors)."""
-        K, Nn = self.shape
-        return ("q8", self.q.reshape(-1, BLOCK), self.block_scales.contiguous().reshape(-1), (K, Nn))
+        q, s = self.plain()
+        return ("q8", q.reshape(-1, BLOCK), s.reshape(-1), self.shape)
 
     def cols(self, start: int, end: int) -> "Q80Weight":
         """Columns [start, end) (a gate/up shard); both multiples of 32."""
         if start % BLOCK or end % BLOCK:
             raise ValueError("column shard bounds must be multiples of 32")
-        return Q80Weight(self.q[:, start:end].contiguous(), self.scale[:, start // BLOCK:end // BLOCK].contiguous())
+        q, s = self.plain()
+        return Q80Weight.from_plain(q[:, start:end].contiguous(), s[:, start // BLOCK:end // BLOCK].contiguous())
 
     def rows(self, start: int, end: int) -> "Q80Weight":
         """Rows [start, end) (a down shard)."""
-        return Q80Weight(self.q[start:end].contiguous(), self.scale[start:end].contiguous())
+        return Q80Weight(self.q[:, start:end].contiguous(), self.scale[:, start:end].contiguous(), self.n)

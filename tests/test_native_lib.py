@@ -52,17 +52,17 @@ def test_quantize_argument_checks_need_no_gpu(native_lib):
     assert native_lib.pyre_q80_quantize(None, N.PYRE_F32, 0, None, None, None, None) == N.PYRE_OK
     assert native_lib.pyre_q80_quantize(ctypes.c_void_p(16), 7, 32, ctypes.c_void_p(16),
                                         ctypes.c_void_p(16), None, None) == N.PYRE_EINVAL
-    assert native_lib.pyre_ffn_gateup_silu_q80(None, N.PYRE_F32, 1, 64, None, None, None, None, N.PYRE_F32, 4, 64,
+    assert native_lib.pyre_ffn_gateup_silu_q80(None, N.PYRE_F32, 1, 64, None, None, None, None, N.PYRE_F32, 64,
                                                None, N.PYRE_F32, None, 0, None) == N.PYRE_EINVAL
     assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 64, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), N.PYRE_F32, 4, 48, ctypes.c_void_p(16),
+                                        ctypes.c_void_p(16), N.PYRE_F32, 48, ctypes.c_void_p(16),
                                         ctypes.c_void_p(16), 1 << 20, None, None) == N.PYRE_EINVAL
     assert "multiple of 32" in N.last_error()
-    # scale rows that are not 16-byte multiples are rejected (TMA)
-    assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 64, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), N.PYRE_F16, 3, 96, ctypes.c_void_p(16),
+    # decode path needs the input dim on whole 32-row units
+    assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 48, ctypes.c_void_p(16),
+                                        ctypes.c_void_p(16), N.PYRE_F16, 64, ctypes.c_void_p(16),
                                         ctypes.c_void_p(16), 1 << 20, None, None) == N.PYRE_EINVAL
-    assert "16-byte" in N.last_error()
+    assert "input dim" in N.last_error()
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):

@@ -105,3 +105,14 @@ def test_weights_dict_roundtrip_tags():
     rd = dequantize_weights_dict(qd)
     q, s, sh = oq80.quantize_q80(d["ffn"]["gate"])
     np.testing.assert_array_equal(rd["ffn"]["gate"].cpu().numpy(), oq80.dequantize_q80(q, s, sh))
+
+
+def test_q80weight_tuple_roundtrip_is_reference_bits():
+    from pyre_b200.quantizer import Q80Weight
+    z = np.load(GOLDEN / "q80_golden.npz")
+    x, q, s = z["normal_64x96__x"], z["normal_64x96__q"], z["normal_64x96__s"]
+    w = Q80Weight.from_tuple(("q8", q, s, x.shape), scale_dtype=torch.float32)
+    _, q2, s2, sh = w.to_tuple()
+    assert sh == x.shape
+    np.testing.assert_array_equal(q2.cpu().numpy(), q)
+    np.testing.assert_array_equal(s2.cpu().numpy().view(np.uint32), s.view(np.uint32))
