@@ -26,9 +26,14 @@
 namespace pyre {
 namespace ffn {
 
+#ifndef PYRE_GEMV_CONSUMER_WARPS
+#define PYRE_GEMV_CONSUMER_WARPS 8
+#endif
 constexpr int kTileN = 256;           // output columns per tile
 constexpr int kUnitRows = 32;         // input rows per work unit = one pipeline stage
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = PYRE_GEMV_CONSUMER_WARPS;
+constexpr int kPasses = kUnitRows / (2 * kConsumerWarps);   // row pairs per warp per unit
+static_assert(kPasses >= 1 && kPasses * 2 * kConsumerWarps == kUnitRows, "consumer warps must divide 16");
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;   // + one producer warp
 constexpr int kMaxGrid = 1024;
@@ -134,9 +139,15 @@ __device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint3
   }
 }
 
+#ifndef PYRE_GEMV_STAGES
+#define PYRE_GEMV_STAGES 4
+#endif
 template <int T, int NMAT, typename XT, typename ST>
 struct GemvCfg {
-  static constexpr int kStages = (T <= 2) ? 8 : 5;
+  // T <= 2: two CTAs per SM with a 4-stage ring each; T >= 3 (larger reduction buffers):
+  // one CTA per SM with 5 stages.
+  static constexpr int kCtasPerSm = (T <= 2) ? 2 : 1;
+  static constexpr int kStages = (T <= 2) ? PYRE_GEMV_STAGES : 5;
   static constexpr int kQBytes = kUnitRows * kTileN;                       // 8 KB per matrix
   static constexpr int kSBytes = kUnitRows * 8 * static_cast<int>(sizeof(ST));   // 8 scale columns
   static constexpr int kXBytes = T * kUnitRows * static_cast<int>(sizeof(XT));
@@ -157,7 +168,8 @@ struct GemvCfg {
 // The (tile, unit) space is split evenly over the grid (stream-K); CTAs that share a
 // tile add their pieces in CTA order, so the result is deterministic.
 template <int T, int NMAT, int EPI, typename XT, typename ST>
-__global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, (GemvCfg<T, NMAT, XT, ST>::kCtasPerSm))
+q80_gemv_kernel(const __grid_constant__ Params p) {
   using C = GemvCfg<T, NMAT, XT, ST>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -240,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_cons
         const ST* ss = reinterpret_cast<const ST*>(st + NMAT * C::kQBytes);
         const XT* xs = reinterpret_cast<const XT*>(st + NMAT * (C::kQBytes + C::kSBytes));
 #pragma unroll
-        for (int pass = 0; pass < 2; ++pass) {
-          const int r = pass * 16 + warp * 2 + rs;
+        for (int pass = 0; pass < kPasses; ++pass) {
+          const int r = pass * (2 * kConsumerWarps) + warp * 2 + rs;
           float xv[T];
 #pragma unroll
           for (int t = 0; t < T; ++t) xv[t] = to_f32(xs[t * kUnitRows + r]);
@@ -337,8 +349,17 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemv_kernel(const __grid_cons
           __threadfence();
           const float* base = p.ws + static_cast<int64_t>(tile) * p.pmax * (NMAT * T * kTileN);
           for (int i = tid; i < NMAT * T * kTileN; i += kConsumers) {
+            // all piece loads in flight at once, then summed in piece order
             float v = 0.f;
-            for (int pc = 0; pc < np; ++pc) v += __ldcg(base + static_cast<int64_t>(pc) * (NMAT * T * kTileN) + i);
+            for (int pc0 = 0; pc0 < np; pc0 += 16) {
+              float pv[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                pv[j] = (pc0 + j < np) ? __ldcg(base + static_cast<int64_t>(pc0 + j) * (NMAT * T * kTileN) + i) : 0.f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (pc0 + j < np) v += pv[j];
+            }
             fin[i] = v;
           }
           consumer_sync();
@@ -483,7 +504,13 @@ int launch_gemv(Params p, cudaStream_t s) {
   int rc = make_tmap_2d(&p.tx, p.x, tma_dtype<XT>(), sizeof(XT), p.T, p.K, static_cast<uint64_t>(p.K) * sizeof(XT),
                         T, kUnitRows);
   if (rc) return rc;
-  int64_t g = sm_count();
+  // every CTA must be co-resident (the tensor-parallel epilogue waits on peers), so the
+  // grid never exceeds what the occupancy calculator says fits at once
+  int occ = 0;
+  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, C::kSmemBytes));
+  if (occ < 1) return set_error(PYRE_ECUDA, "q80_gemv: kernel does not fit on an SM");
+  if (occ > C::kCtasPerSm) occ = C::kCtasPerSm;
+  int64_t g = static_cast<int64_t>(occ) * sm_count();
   if (g > kMaxGrid) g = kMaxGrid;
   if (g > p.total_units) g = p.total_units;
   const int G = static_cast<int>(g < 1 ? 1 : g);
