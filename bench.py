@@ -228,14 +228,10 @@ def run_ours(args):
             for i in range(n_steps):
                 gq, uq, dq = sets[i % n_sets]
                 if with_events:
-                    e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+                    e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)]
                     e[0].record(stream)
-                    # the two kernels of the op, recorded separately
-                    h = torch.empty((T, W), dtype=op.h_dtype(T), device=dev)
-                    _gateup(op, x, gq, uq, h, stream)
+                    op(x, gq, uq, dq, out=out, stream=stream)     # one launch (decode kernel)
                     e[1].record(stream)
-                    _down(op, h, dq, out, stream)
-                    e[2].record(stream)
                     evs.append(e)
                 else:
                     op(x, gq, uq, dq, out=out, stream=stream)
@@ -277,16 +273,16 @@ def run_ours(args):
         comm.check(stream)
     elapsed_ms = ev0.elapsed_time(ev1)
 
-    # per-kernel durations (probe graph with external event nodes, 32 distinct weight sets)
-    gu_ms, dn_ms = [], []
+    # per-launch durations of the decode kernel (probe graph with external event nodes
+    # around each launch, over the distinct weight sets)
+    k_ms = []
     for _ in range(4):
         barrier()
         with torch.cuda.stream(stream):
             g_probe.replay()
         stream.synchronize()
         for e in probe_ev:
-            gu_ms.append(e[0].elapsed_time(e[1]))
-            dn_ms.append(e[1].elapsed_time(e[2]))
+            k_ms.append(e[0].elapsed_time(e[1]))
     sampler.stop()
     if comm is not None:
         comm.check(stream)
@@ -336,22 +332,20 @@ def run_ours(args):
         prefill = {"tokens": TP, "ms_per_step": pf_ms}
 
     # max over ranks
-    vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(gu_ms), statistics.mean(dn_ms),
-                         prefill["ms_per_step"] if prefill else 0.0], dtype=torch.float64, device=dev)
+    vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(k_ms), prefill["ms_per_step"] if prefill else 0.0],
+                        dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_s, gu_avg, dn_avg, pf_ms = vals.tolist()
+    elapsed_ms, e2e_s, k_avg, pf_ms = vals.tolist()
     clocks = sampler.summary(t_wall0, t_wall1)
 
     if rank == 0:
         ms_step = elapsed_ms / args.steps
         value = T / (ms_step / 1e3)
-        # algorithmic bytes of the slowest rank's shard are the critical path; the roofline
-        # of the dominant kernel is reported for rank 0's shard and its measured duration
+        # the decode kernel streams rank 0's shard of all three matrices once per launch
         W0 = plan.widths[0]
-        gu_bytes = 2 * H * W0 * Q8_BYTES_PER_PARAM + T * H * 2 + T * W0 * 4
-        dn_bytes = W0 * H * Q8_BYTES_PER_PARAM + T * W0 * 4 + T * H * 4
-        gu_gbs = gu_bytes / (gu_avg * 1e-3) / 1e9
+        k_bytes = 3 * H * W0 * Q8_BYTES_PER_PARAM + T * H * 2 + T * W0 * 4 * 2 + T * H * 4
+        k_gbs = k_bytes / (k_avg * 1e-3) / 1e9
         step_bytes_all = 3 * H * I * Q8_BYTES_PER_PARAM
         res = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -362,16 +356,15 @@ def run_ours(args):
                        "tokens": T, "widths": list(plan.widths), "partition": "Dirichlet(5) seed 1, 32-element blocks",
                        "weight_sets": n_sets, "l2": f"inputs larger than L2: {n_sets} rotating weight sets per rank",
                        "parallelism": f"tp{world}", "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
-            "roofline": {"bound": "hbm", "kernel": "q80_gemv_kernel (gate/up + SiLU·mul), rank 0 shard",
-                         "achieved": round(gu_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gu_gbs / hbm, 4),
+            "roofline": {"bound": "hbm",
+                         "kernel": "q80_ffn_decode_kernel (gate/up + SiLU\u00b7mul + down [+ NVLink reduce], one launch), rank 0 shard",
+                         "achieved": round(k_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
                          "peak_kind": peak_kind, "traffic": None,
-                         "algorithmic_bytes_per_launch": int(gu_bytes), "avg_launch_us": round(gu_avg * 1e3, 3),
-                         "down_kernel": {"avg_launch_us": round(dn_avg * 1e3, 3),
-                                         "achieved": round(dn_bytes / (dn_avg * 1e-3) / 1e9, 1)},
+                         "algorithmic_bytes_per_launch": int(k_bytes), "avg_launch_us": round(k_avg * 1e3, 3),
                          "step_aggregate": {"bytes_all_ranks": int(step_bytes_all),
                                             "achieved_per_gpu": round(step_bytes_all / world / (ms_step * 1e-3) / 1e9, 1),
                                             "frac_of_aggregate": round(step_bytes_all / (ms_step * 1e-3) / 1e9 / (hbm * world), 4)}},
-            "gpu_launches": args.steps * op.launches_per_call,
+            "gpu_launches": args.steps * op.launches(T),
             "e2e": {"value": round(e2e_steps * T / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": e2e_runners[0].h2d_bytes, "d2h_bytes_per_step": e2e_runners[0].d2h_bytes,
                     "how": "CapturedFfn.execute(host x) per call: pinned H2D, graph of the op, D2H, stream sync"},
@@ -393,23 +386,6 @@ def run_ours(args):
         if comm is not None:
             comm.close()
         dist.destroy_process_group()
-
-
-def _gateup(op, x, gq, uq, h, stream):
-    import ctypes
-    from pyre_b200 import _device as D, _native as N
-    N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), x.shape[0], op.hidden, D.ptr(gq.q),
-           D.ptr(gq.scale), D.ptr(uq.q), D.ptr(uq.scale), uq.scale_code, op.width, D.ptr(h),
-           D.dtype_code(h),
-           D.ptr(op.workspace), op.workspace.numel(), ctypes.c_void_p(stream.cuda_stream))
-
-
-def _down(op, h, dq, out, stream):
-    import ctypes
-    from pyre_b200 import _device as D, _native as N
-    N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), h.shape[0], op.width, D.ptr(dq.q), D.ptr(dq.scale),
-           dq.scale_code, op.hidden, D.ptr(out), D.ptr(op.workspace), op.workspace.numel(),
-           ctypes.c_void_p(op.comm.handle if op.comm is not None else 0), ctypes.c_void_p(stream.cuda_stream))
 
 
 def run_reference(args):

@@ -82,7 +82,8 @@ PYRE_API int pyre_q80_dequantize(const int8_t* q, const void* scale, int scale_d
  * build_ffn_graph (src/ffn/builder.py:20-53) and run by the root's decode FFN
  * (src/orchestrator/root_node.py:956-980).
  *
- * Bytes of scratch the two FFN calls below need for T tokens, hidden H, width W. */
+ * Bytes of scratch the FFN calls below need for T tokens, hidden H, width W (256-byte
+ * aligned, zero-initialised once by the caller). */
 PYRE_API int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes);
 
 /* h[T, W] = silu(x @ Wg) * (x @ Wu)      (gated,   src/ffn/builder.py:37-43)
@@ -99,6 +100,21 @@ PYRE_API int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H,
                              const int8_t* qu, const void* su, int scale_dtype, int W,
                              void* h, int h_dtype, void* workspace, int64_t ws_bytes,
                              void* stream);
+
+/* The whole shard FFN for T <= PYRE_FUSED_REDUCE_MAX_T tokens in one persistent launch:
+ *   out[T, H] = (silu(x @ Wg) * (x @ Wu)) @ Wd          (src/ffn/builder.py:37-45, the
+ *   root's decode FFN src/orchestrator/root_node.py:956-980; qg == NULL: silu(x @ Wu) @ Wd)
+ * and, with comm != NULL, the sum over the ranks of comm in rank order
+ * (src/orchestrator/root_node.py:982-995), reduced in the down-projection epilogue through
+ * NVLink peer stores. The gate/up product h lives in the workspace; the down projection of
+ * rows k..k+31 of h starts as soon as the gate/up slab holding them is finished.
+ * x: [T, H] (PYRE_F32 or PYRE_BF16, 16-byte aligned rows); Wg, Wu: [H, W] and Wd: [W, H] in
+ * the tiled device layout; H and W multiples of 32; out: f32 [T, H]. */
+PYRE_API int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H,
+                                 const int8_t* qg, const void* sg, const int8_t* qu, const void* su,
+                                 const int8_t* qd, const void* sd, int scale_dtype, int W,
+                                 float* out, void* workspace, int64_t ws_bytes,
+                                 pyre_comm_t* comm, void* stream);
 
 /* out[T, H] = h @ Wd   (src/ffn/builder.py:44), and with comm != NULL also the sum of
  * that partial over every rank of comm (src/orchestrator/root_node.py:582-594 and

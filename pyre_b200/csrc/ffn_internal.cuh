@@ -1,0 +1,108 @@
+// Internal pieces shared by ffn.cu (two-call FFN) and ffn_decode.cu (one-launch decode FFN).
+#pragma once
+
+#include "gemv_common.cuh"
+
+namespace pyre {
+namespace ffn {
+
+using namespace gemv;
+
+enum Epi : int { EPI_SILU_MUL = 0, EPI_SILU = 1, EPI_STORE = 2, EPI_TP = 3 };
+
+struct alignas(64) Params {
+  CUtensorMap tx;            // activations [T, K], box T x 32
+  const void* x;
+  const int8_t* q0;          // tiled q [tiles, K, 256]; gate (NMAT == 2) or the single matrix
+  const void* s0;            // tiled scales [tiles, K, 8]
+  const int8_t* q1;          // up (NMAT == 2)
+  const void* s1;
+  int K, N, T;
+  int tiles;                 // ceil(N / kTileN)
+  int upt;                   // units per tile = K / kUnitRows
+  int64_t total_units;       // tiles * upt
+  int pmax;                  // piece slots per tile in ws
+  int64_t ws_cap;            // bytes available for pieces
+  float* ws;                 // [tiles, pmax, NMAT, T, kTileN]
+  unsigned int* counters;    // [tiles], zero between calls
+  int* status;               // device status word (bounded waits)
+  void* out;                 // [T, N]
+  int out_bf16;
+  comm::DevComm comm;        // EPI_TP only
+};
+
+__device__ __forceinline__ void store_out(void* out, int out_bf16, int N, int t, int col, float v) {
+  const int64_t o = static_cast<int64_t>(t) * N + col;
+  if (out_bf16)
+    static_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(v);
+  else
+    static_cast<float*>(out)[o] = v;
+}
+
+// Cross-rank sum of one finished tile (the reference's `ffn_out += partial`,
+// src/orchestrator/root_node.py:582-594): push the partial into every rank's receive slot
+// (self included) over NVLink, release a flag per peer, wait (bounded) for every peer's
+// flag of this tile and add the partials in rank order 0..world-1 into out.
+template <int T>
+__device__ void tp_reduce_tile(const comm::DevComm& c, uint32_t epoch, int tile, const float* fin, float* out, int N,
+                               int tid) {
+  const int slot = epoch & 1u;
+  const int n = T * kTileN;
+  for (int peer = 0; peer < c.world; ++peer) {
+    float* dst = comm::fused_slot(c, peer, slot, c.rank) + static_cast<int64_t>(tile) * n;
+    for (int i = tid; i < n; i += kConsumers) dst[i] = fin[i];
+  }
+  __threadfence_system();
+  consumer_sync();
+  if (tid < c.world) st_release_sys(comm::fused_flag(c, tid, slot, c.rank, tile), epoch);
+  if (tid < c.world) {
+    if (!wait_flag_eq(comm::fused_flag(c, c.rank, slot, tid, tile), epoch, c.timeout_ns))
+      atomicExch(c.status, PYRE_ETIMEOUT);
+  }
+  consumer_sync();
+  for (int i = tid; i < n; i += kConsumers) {
+    const int t = i / kTileN, cc = i % kTileN;
+    const int col = tile * kTileN + cc;
+    if (col >= N) continue;
+    float acc = 0.f;
+    for (int src = 0; src < c.world; ++src)
+      acc += __ldcg(comm::fused_slot(c, c.rank, slot, src) + static_cast<int64_t>(tile) * n + i);
+    out[static_cast<int64_t>(t) * N + col] = acc;
+  }
+}
+
+template <typename K>
+int set_smem_once(K kern, int bytes) {
+  static bool done[64] = {};  // per kernel instantiation and device
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !done[dev]) {
+    PYRE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    if (dev >= 0 && dev < 64) done[dev] = true;
+  }
+  return PYRE_OK;
+}
+
+// Co-resident grid for a kernel: never more CTAs than fit at once (the tensor-parallel
+// epilogues and the per-slab ready flags wait on other CTAs), capped by want_per_sm and the
+// work.
+template <typename K>
+int coresident_grid(K kern, int threads, int smem, int want_per_sm, int64_t units, int* grid) {
+  int occ = 0;
+  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem));
+  if (occ < 1) return set_error(PYRE_ECUDA, "kernel does not fit on an SM");
+  if (occ > want_per_sm) occ = want_per_sm;
+  int64_t g = static_cast<int64_t>(occ) * sm_count();
+  if (g > kMaxGrid) g = kMaxGrid;
+  if (g > units) g = units;
+  *grid = static_cast<int>(g < 1 ? 1 : g);
+  return PYRE_OK;
+}
+
+}  // namespace ffn
+
+// Argument checks shared by the FFN entry points (defined in ffn.cu).
+int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
+                     const void* ws, int64_t ws_bytes, const char* fn);
+
+}  // namespace pyre

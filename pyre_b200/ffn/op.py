@@ -25,13 +25,15 @@ def workspace_bytes(tokens: int, hidden: int, width: int) -> int:
 class FfnShardOp:
     """One rank's FFN shard for up to ``max_tokens`` tokens.
 
-    Holds the zero-initialised scratch the stream-K GEMV needs (reused call after call
-    on one stream) and launches two kernels per call: gate/up + SiLU·mul, then down
-    (+ the tensor-parallel reduction when ``comm`` is set).
+    Holds the zero-initialised scratch the kernels need (reused call after call on one
+    stream). Decode (T <= 4) is one persistent launch (``pyre_ffn_decode_q80``: gate/up +
+    SiLU·mul, then down + the tensor-parallel reduction when ``comm`` is set); larger T,
+    or ``fused=False``, uses the two-call form (``pyre_ffn_gateup_silu_q80`` then
+    ``pyre_ffn_down_q80``).
     """
 
     def __init__(self, hidden_dim: int, width: int, max_tokens: int = 1, *, gated: bool = True,
-                 comm=None, device: torch.device | None = None):
+                 comm=None, device: torch.device | None = None, fused: bool = True):
         D.require_cuda()
         if width <= 0 or hidden_dim <= 0:
             raise ValueError(f"ShardSpec width must be positive, got {width}")
@@ -45,13 +47,18 @@ class FfnShardOp:
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         wsb = workspace_bytes(min(self.max_tokens, N.PYRE_FUSED_REDUCE_MAX_T), self.hidden, self.width)
         self.workspace = torch.zeros(wsb, dtype=torch.uint8, device=self.device)
-        self.launches_per_call = 2 + (1 if (comm is not None and comm.world > 1 and
-                                            self.max_tokens > N.PYRE_FUSED_REDUCE_MAX_T) else 0)
+        self.fused = fused
+
+    def launches(self, tokens: int) -> int:
+        """Kernel launches of one call with ``tokens`` tokens."""
+        if tokens <= N.PYRE_FUSED_REDUCE_MAX_T:
+            return 1 if self.fused else 2
+        return 2 + (1 if (self.comm is not None and self.comm.world > 1) else 0)
 
     def status(self) -> int:
-        """Status word of the op's kernels (PYRE_OK, or PYRE_ETIMEOUT if a pipeline wait
-        ran out); read after synchronising the stream."""
-        return int(self.workspace[:8192].view(torch.int32)[-1].item())
+        """Status word of the op's kernels (PYRE_OK, or PYRE_ETIMEOUT if a pipeline or flag
+        wait ran out); read after synchronising the stream."""
+        return int(self.workspace[8:12].view(torch.int32).item())
 
     def h_dtype(self, tokens: int) -> torch.dtype:
         # decode keeps the intermediate in f32; larger T stores bf16 (tensor-core operand)
@@ -78,16 +85,24 @@ class FfnShardOp:
                 raise ValueError(f"{name} weight must be {shp}, got {tuple(w.shape)}")
         if gate is not None and gate.scale.dtype != up.scale.dtype:
             raise ValueError("gate and up scales must share a dtype")
+        if down.scale.dtype != up.scale.dtype:
+            raise ValueError("down and up scales must share a dtype")
         s = D.stream_ptr(stream)
-        h = torch.empty((T, self.width), dtype=self.h_dtype(T), device=x.device)
         if out is None:
             out = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
         ws = self.workspace
+        comm = ctypes.c_void_p(self.comm.handle if self.comm is not None else 0)
+        if self.fused and T <= N.PYRE_FUSED_REDUCE_MAX_T:
+            N.call("pyre_ffn_decode_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
+                   D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
+                   D.ptr(up.q), D.ptr(up.scale), D.ptr(down.q), D.ptr(down.scale), up.scale_code, self.width,
+                   D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
+            return out
+        h = torch.empty((T, self.width), dtype=self.h_dtype(T), device=x.device)
         N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
                D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
                D.ptr(up.q), D.ptr(up.scale), up.scale_code, self.width,
                D.ptr(h), D.dtype_code(h), D.ptr(ws), ws.numel(), s)
         N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), T, self.width, D.ptr(down.q), D.ptr(down.scale),
-               down.scale_code, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(),
-               ctypes.c_void_p(self.comm.handle if self.comm is not None else 0), s)
+               down.scale_code, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
         return out

@@ -171,3 +171,41 @@ def test_mistral_shape_ffn_vs_oracle(T):
     ref = offn.ffn_shard(x.float().cpu().numpy(), *deq).astype(np.float64) if T > 4 else \
         offn.ffn_shard_f64(x.float().cpu().numpy(), *deq)
     assert rel_err(out, ref) < (TOL_F32 if T <= 4 else TOL_BF16)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("gated", [True, False])
+def test_two_call_decode_path_vs_oracle(T, gated):
+    """The two-call form (gate/up kernel, then down kernel) stays available and correct."""
+    from pyre_b200.ffn import FfnShardOp
+    rng = np.random.default_rng(100 + T)
+    H, W = 512, 1344
+    g, gd = make_weight((H, W), rng, torch.float16) if gated else (None, None)
+    u, ud = make_weight((H, W), rng, torch.float16)
+    d, dd = make_weight((W, H), rng, torch.float16)
+    x = bf16_round(rng.standard_normal((T, H)))
+    ref = offn.ffn_shard_f64(x, gd, ud, dd)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    two = FfnShardOp(H, W, max_tokens=T, gated=gated, fused=False)(xt, g, u, d).cpu().numpy()
+    one = FfnShardOp(H, W, max_tokens=T, gated=gated)(xt, g, u, d).cpu().numpy()
+    assert rel_err(two, ref) < TOL_F32 and rel_err(one, ref) < TOL_F32
+    assert rel_err(one, two.astype(np.float64)) < 1e-5
+
+
+def test_decode_repeated_calls_and_status():
+    """Many back-to-back one-launch calls on one workspace: the per-call epoch tags of the
+    ready flags must keep every call's phase B waiting for its own phase A."""
+    from pyre_b200.ffn import FfnShardOp
+    rng = np.random.default_rng(12)
+    H, W = 1024, 2816
+    ws = [tuple(make_weight(shape, rng, torch.float16)[0] for shape in ((H, W), (H, W), (W, H))) for _ in range(3)]
+    op = FfnShardOp(H, W, max_tokens=1)
+    xs = [torch.randn((1, H), device="cuda").to(torch.bfloat16) for _ in range(3)]
+    first = [op(xs[i], *ws[i]).clone() for i in range(3)]
+    outs = []
+    for it in range(60):
+        outs.append(op(xs[it % 3], *ws[it % 3]).clone())
+    torch.cuda.synchronize()
+    for it, o in enumerate(outs):
+        assert torch.equal(o, first[it % 3])
+    assert op.status() == 0
