@@ -1,6 +1,8 @@
 // Library-wide C ABI pieces: version, per-thread error text, device queries.
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 
@@ -34,6 +36,18 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+int set_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return PYRE_OK;
+  PYRE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({kernel, dev});
+  return PYRE_OK;
 }
 
 }  // namespace pyre

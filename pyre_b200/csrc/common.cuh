@@ -17,6 +17,8 @@ int set_error(int code, const std::string& msg);
 int cuda_status(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device).
+int set_smem_limit(const void* kernel, int bytes);
 
 #define PYRE_CHECK_ARG(cond, msg)                                   \
   do {                                                              \

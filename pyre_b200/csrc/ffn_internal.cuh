@@ -73,14 +73,7 @@ __device__ void tp_reduce_tile(const comm::DevComm& c, uint32_t epoch, int tile,
 
 template <typename K>
 int set_smem_once(K kern, int bytes) {
-  static bool done[64] = {};  // per kernel instantiation and device
-  int dev = 0;
-  PYRE_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64 || !done[dev]) {
-    PYRE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    if (dev >= 0 && dev < 64) done[dev] = true;
-  }
-  return PYRE_OK;
+  return set_smem_limit(reinterpret_cast<const void*>(kern), bytes);
 }
 
 // Co-resident grid for a kernel: never more CTAs than fit at once (the tensor-parallel
