@@ -83,7 +83,10 @@ def test_ffn_deterministic_and_workspace_reuse():
     outs = [op(x, g, u, d).clone() for _ in range(5)]
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
-    assert int(op.workspace[:8192].view(torch.int32).abs().sum()) == 0   # counters reset
+    hdr = op.workspace[:32768].view(torch.int32)
+    assert int(hdr[0]) == 5                                  # call epoch: one per call
+    assert int(hdr[2]) == 0                                  # status word
+    assert int(hdr[256:256 + 2 * 2048].abs().sum()) == 0     # stream-K counters reset
 
 
 def test_gated_golden_from_reference_builder():
