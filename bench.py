@@ -168,6 +168,7 @@ def make_sets(rank, bounds, n_sets, device):
     """Per weight set (one per layer): full matrices from a seeded CUDA generator (identical
     on every rank), Q8_0 on the GPU, then this rank's shard."""
     import torch
+    from pyre_b200.ffn import FfnWeights
     from pyre_b200.quantizer import Q80Weight
     s, e = bounds[rank]
     sets = []
@@ -179,7 +180,7 @@ def make_sets(rank, bounds, n_sets, device):
             trip.append(Q80Weight.from_float(w, torch.float16))
             del w
         gq, uq, dq = trip
-        sets.append((gq.cols(s, e), uq.cols(s, e), dq.rows(s, e)))
+        sets.append(FfnWeights.prepare(gq.cols(s, e), uq.cols(s, e), dq.rows(s, e)))
         del trip, gq, uq, dq
     torch.cuda.synchronize()
     return sets
@@ -222,19 +223,19 @@ def run_ours(args):
         g = torch.cuda.CUDAGraph()
         evs = []
         with torch.cuda.stream(stream):
-            op(x, *sets[0], out=out, stream=stream)       # eager once before capture
+            op.run(x, sets[0], out=out, stream=stream)       # eager once before capture
         stream.synchronize()
         with torch.cuda.graph(g, stream=stream):
             for i in range(n_steps):
-                gq, uq, dq = sets[i % n_sets]
+                wts = sets[i % n_sets]
                 if with_events:
                     e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)]
                     e[0].record(stream)
-                    op(x, gq, uq, dq, out=out, stream=stream)     # one launch (decode kernel)
+                    op.run(x, wts, out=out, stream=stream)     # one launch (decode kernel)
                     e[1].record(stream)
                     evs.append(e)
                 else:
-                    op(x, gq, uq, dq, out=out, stream=stream)
+                    op.run(x, wts, out=out, stream=stream)
         return g, evs
 
     def barrier():
@@ -288,7 +289,7 @@ def run_ours(args):
         comm.check(stream)
 
     # end-to-end through the public API: pinned host x in, host partial sum out, per call
-    e2e_runners = [CapturedFfn(op, *sets[i], tokens=T) for i in range(min(n_sets, 8))]
+    e2e_runners = [CapturedFfn(op, sets[i], tokens=T) for i in range(min(n_sets, 8))]
     xh = x.float().cpu().to(torch.bfloat16)
     for r in e2e_runners:
         r.execute(xh)
@@ -309,13 +310,13 @@ def run_ours(args):
         outp = torch.empty((TP, H), dtype=torch.float32, device=dev)
         with torch.cuda.stream(stream):
             for i in range(3):
-                op(xp, *sets[i % n_sets], out=outp, stream=stream)
+                op.run(xp, sets[i % n_sets], out=outp, stream=stream)
         stream.synchronize()
         n_pf = 8
         gp = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gp, stream=stream):
             for i in range(n_pf):
-                op(xp, *sets[i % n_sets], out=outp, stream=stream)
+                op.run(xp, sets[i % n_sets], out=outp, stream=stream)
         with torch.cuda.stream(stream):
             gp.replay()
         stream.synchronize()

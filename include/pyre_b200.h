@@ -16,13 +16,13 @@
  * (src/orchestrator/quantizer.py:11-26, src/orchestrator/llama_loader.py:1132-1134), so
  * every block runs along N: q int8 [K, N], scale [K, N/32], scale[k, j/32] for q[k, j].
  *
- * Device weight layout (column-slab tiled, used by the FFN entry points): N is padded with
- * zeros to a multiple of 256 and cut into NT = N_pad/256 slabs; slab j holds
- *   q     int8        [K, 256]  = q[:, 256j : 256j+256]
- *   scale f16 or f32  [K, 8]    = scale[:, 8j : 8j+8]
- * stored slab after slab: q_tiled [NT, K, 256], scale_tiled [NT, K, 8]. The int8 values
- * and scales are exactly the reference's; each 32-row x 256-column work unit is one
- * contiguous 8 KB run, which the kernels stream with bulk copies.
+ * Packed device weight layout (used by the FFN entry points). A group of M matrices that
+ * share [K, N] (M = 2: gate and up; M = 1: one matrix) is stored as contiguous blocks, one
+ * per (slab of 256 output columns j, unit of R = 64 / M input rows u), in (j, u) order:
+ *   [q of matrix 0: R x 256 int8] ... [q of matrix M-1] [scales of matrix 0: R x 8] ...
+ * with K padded to a multiple of R and N to a multiple of 256 by zeros. The int8 values and
+ * scales are exactly the reference's blocks; a block (~17 KB) is one pipeline stage that the
+ * kernels move with a single bulk copy. pyre_q80_pack() builds it from the plain form.
  */
 #ifndef PYRE_B200_H
 #define PYRE_B200_H
@@ -77,6 +77,15 @@ PYRE_API int pyre_q80_quantize(const void* src, int src_dtype, int64_t n,
 PYRE_API int pyre_q80_dequantize(const int8_t* q, const void* scale, int scale_dtype, int64_t n,
                         float* out, void* stream);
 
+/* Bytes of the packed layout of M (1 or 2) [K, N] matrices with scales of scale_dtype. */
+PYRE_API int pyre_q80_packed_bytes(int M, int K, int N, int scale_dtype, int64_t* bytes);
+
+/* Plain -> packed: q0/q1 int8 [K, N] row-major (16-byte aligned), s0/s1 scales [K, N/32]
+ * (the reference's flat Q8_0 tuple of a stored [in, out] weight, reshaped); M == 2 packs
+ * q0/s0 (gate) with q1/s1 (up) block by block. out: pyre_q80_packed_bytes() bytes. */
+PYRE_API int pyre_q80_pack(int M, const int8_t* q0, const void* s0, const int8_t* q1, const void* s1,
+                  int K, int N, int scale_dtype, void* out, void* stream);
+
 /* ---- gated-SiLU FFN shard ---------------------------------------------------------
  * The shard [ffn_start, ffn_end) of width W of the intermediate dim, as built by
  * build_ffn_graph (src/ffn/builder.py:20-53) and run by the root's decode FFN
@@ -87,32 +96,30 @@ PYRE_API int pyre_q80_dequantize(const int8_t* q, const void* scale, int scale_d
 PYRE_API int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes);
 
 /* h[T, W] = silu(x @ Wg) * (x @ Wu)      (gated,   src/ffn/builder.py:37-43)
- * h[T, W] = silu(x @ Wu)                 (ungated, src/ffn/builder.py:47-49; qg == NULL)
- * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16), 16-byte aligned rows. Wg, Wu: [H, W] in
- * the tiled device layout (scales of scale_dtype). For T <= PYRE_FUSED_REDUCE_MAX_T the
- * input dim (H here, W for the down projection) must be a multiple of 32. h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
+ * h[T, W] = silu(x @ Wu)                 (ungated, src/ffn/builder.py:47-49; gated == 0)
+ * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16), 16-byte aligned rows. wgu: gate and up
+ * [H, W] packed together (M = 2), or up alone (M = 1) when gated == 0, scales of
+ * scale_dtype. h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
  * as in pyre_kernels.silu_mul (src/kernels/mojo/pyre_kernels.mojo:121-129).
  * workspace: zero-initialised device memory of at least pyre_ffn_workspace_bytes();
  * it is left zeroed where it must start at zero, so it can be reused call after call on
  * one stream (calls that overlap on the GPU need separate workspaces). */
 PYRE_API int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H,
-                             const int8_t* qg, const void* sg,
-                             const int8_t* qu, const void* su, int scale_dtype, int W,
+                             const void* wgu, int gated, int scale_dtype, int W,
                              void* h, int h_dtype, void* workspace, int64_t ws_bytes,
                              void* stream);
 
 /* The whole shard FFN for T <= PYRE_FUSED_REDUCE_MAX_T tokens in one persistent launch:
  *   out[T, H] = (silu(x @ Wg) * (x @ Wu)) @ Wd          (src/ffn/builder.py:37-45, the
- *   root's decode FFN src/orchestrator/root_node.py:956-980; qg == NULL: silu(x @ Wu) @ Wd)
+ *   root's decode FFN src/orchestrator/root_node.py:956-980; gated == 0: silu(x @ Wu) @ Wd)
  * and, with comm != NULL, the sum over the ranks of comm in rank order
  * (src/orchestrator/root_node.py:982-995), reduced in the down-projection epilogue through
  * NVLink peer stores. The gate/up product h lives in the workspace; the down projection of
  * rows k..k+31 of h starts as soon as the gate/up slab holding them is finished.
- * x: [T, H] (PYRE_F32 or PYRE_BF16, 16-byte aligned rows); Wg, Wu: [H, W] and Wd: [W, H] in
- * the tiled device layout; H and W multiples of 32; out: f32 [T, H]. */
+ * x: [T, H] (PYRE_F32 or PYRE_BF16, 16-byte aligned rows); wgu: gate/up [H, W] packed as a
+ * pair (or up alone), wd: down [W, H] packed; H and W multiples of 32; out: f32 [T, H]. */
 PYRE_API int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H,
-                                 const int8_t* qg, const void* sg, const int8_t* qu, const void* su,
-                                 const int8_t* qd, const void* sd, int scale_dtype, int W,
+                                 const void* wgu, int gated, const void* wd, int scale_dtype, int W,
                                  float* out, void* workspace, int64_t ws_bytes,
                                  pyre_comm_t* comm, void* stream);
 
@@ -121,10 +128,10 @@ PYRE_API int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H,
  * :982-995, `ffn_out += partial`), in rank order 0..world-1 on every rank. For
  * T <= PYRE_FUSED_REDUCE_MAX_T the reduction happens in the GEMV epilogue through
  * NVLink peer stores and bounded flag waits; above it a two-shot peer-memory
- * all-reduce follows the GEMM. h: [T, W] of h_dtype; Wd: [W, H] tiled; out: f32 [T, H]. */
+ * all-reduce follows the GEMM. h: [T, W] of h_dtype; wd: [W, H] packed (M = 1); out: f32 [T, H]. */
 #define PYRE_FUSED_REDUCE_MAX_T 4
 PYRE_API int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W,
-                      const int8_t* qd, const void* sd, int scale_dtype, int H,
+                      const void* wd, int scale_dtype, int H,
                       float* out, void* workspace, int64_t ws_bytes,
                       pyre_comm_t* comm, void* stream);
 

@@ -48,9 +48,11 @@ _SIGNATURES = {
     "pyre_q80_quantize": [_vp, _i, _c_i64, _vp, _vp, _vp, _vp],
     "pyre_q80_dequantize": [_vp, _vp, _i, _c_i64, _vp, _vp],
     "pyre_ffn_workspace_bytes": [_i, _i, _i, ctypes.POINTER(_c_i64)],
-    "pyre_ffn_gateup_silu_q80": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp, _i, _vp, _c_i64, _vp],
-    "pyre_ffn_down_q80": [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
-    "pyre_ffn_decode_q80": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
+    "pyre_q80_packed_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
+    "pyre_q80_pack": [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp],
+    "pyre_ffn_gateup_silu_q80": [_vp, _i, _i, _i, _vp, _i, _i, _i, _vp, _i, _vp, _c_i64, _vp],
+    "pyre_ffn_down_q80": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
+    "pyre_ffn_decode_q80": [_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
     "pyre_comm_buffer_bytes": [_i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_comm_alloc": [_c_i64, ctypes.POINTER(_vp), _vp],
     "pyre_comm_free": [_vp],

@@ -8,10 +8,8 @@
 // weights dequantized from Q8_0 (src/orchestrator/quantizer.py:29-40) as a reference worker
 // does (src/orchestrator/worker_node.py:59-69). Accumulation is f32.
 //
-// Device weight layout (column-slab tiled Q8_0): a [K, N] weight is cut into slabs of 256
-// output columns; slab j stores q[:, 256j : 256j+256] (K x 256 int8, contiguous) and its
-// scales [:, 8j : 8j+8] (K x 8), N zero-padded to a multiple of 256. The values are exactly
-// the reference's Q8_0 blocks; only their order differs.
+// Weights are in the packed block layout of gemv_common.cuh (gate and up interleaved per
+// block for the gated form).
 #include <algorithm>
 
 #include "ffn_internal.cuh"
@@ -110,21 +108,15 @@ q80_gemv_kernel(const __grid_constant__ Params p) {
     // ---------------- producer ----------------
     if (lane == 0) {
       prefetch_tmap(&p.tx);
-      const int8_t* qm[2] = {p.q0, p.q1};
-      const uint8_t* sm[2] = {static_cast<const uint8_t*>(p.s0), static_cast<const uint8_t*>(p.s1)};
       int s = 0;
       uint32_t ph = 0;
       for (int64_t u = u_begin; u < u_end; ++u) {
         const int tile = static_cast<int>(u / p.upt);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.upt) * kUnitRows;
+        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.upt) * L::kRows;
         mbar_wait(&empty[s], ph ^ 1u, p.status);
         uint8_t* st = stages + s * L::kBytes;
         mbar_arrive_expect_tx(&full[s], L::kTxBytes);
-        const int64_t row0 = static_cast<int64_t>(tile) * p.K + k0;
-        for (int m = 0; m < NMAT; ++m) {
-          bulk_load(st + m * L::kQBytes, qm[m] + row0 * kTileN, L::kQBytes, &full[s]);
-          bulk_load(st + L::kSOff + m * L::kSBytes, sm[m] + row0 * (L::kSBytes / kUnitRows), L::kSBytes, &full[s]);
-        }
+        bulk_load(st, p.w + u * L::kWBytes, L::kWBytes, &full[s]);   // block index == unit index
         tma_load_2d(st + L::kXOff, &p.tx, k0, 0, &full[s]);
         if (++s == C::kStages) {
           s = 0;
@@ -188,8 +180,8 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[m][i][j] = 0.f;
-  const int8_t* qm[2] = {p.q0, p.q1};
-  const void* sm[2] = {p.s0, p.s1};
+  constexpr int R = UnitRows<NMAT>::value;
+  const int64_t bbytes = packed_block_bytes(NMAT, sizeof(ST));
 
   for (int k0 = 0; k0 < p.K; k0 += kGK) {
     for (int i = threadIdx.x; i < kGM * kGK; i += 256) {
@@ -204,8 +196,11 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
         const int k = k0 + kk, n = n0 + nn;
         float w = 0.f;
         if (k < p.K && n < p.N) {
-          const int64_t row = static_cast<int64_t>(n / kTileN) * p.K + k;
-          w = static_cast<float>(qm[m][row * kTileN + (n % kTileN)]) * ld_scale<ST>(sm[m], row * 8 + ((n % kTileN) >> 5));
+          const uint8_t* blk = p.w + (static_cast<int64_t>(n / kTileN) * p.upt + k / R) * bbytes;
+          const int rr = k % R, cn = n % kTileN;
+          const int8_t q = reinterpret_cast<const int8_t*>(blk)[(m * R + rr) * kTileN + cn];
+          const ST* sc = reinterpret_cast<const ST*>(blk + NMAT * R * kTileN);
+          w = static_cast<float>(q) * to_f32(sc[(m * R + rr) * 8 + (cn >> 5)]);
         }
         wsm[m][kk][nn] = w;
       }
@@ -255,11 +250,12 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
 template <int T, int NMAT, int EPI, typename XT, typename ST>
 int launch_gemv(Params p, cudaStream_t s) {
   using C = GemvCfg<T, NMAT, XT, ST>;
+  using L = typename C::L;
   auto kern = q80_gemv_kernel<T, NMAT, EPI, XT, ST>;
   int rc = set_smem_once(kern, C::kSmemBytes);
   if (rc) return rc;
   rc = make_tmap_2d(&p.tx, p.x, tma_dtype<XT>(), sizeof(XT), p.T, p.K, static_cast<uint64_t>(p.K) * sizeof(XT), T,
-                    kUnitRows);
+                    L::kRows);
   if (rc) return rc;
   int G = 1;
   rc = coresident_grid(kern, kThreads, C::kSmemBytes, C::kCtasPerSm, p.total_units, &G);
@@ -310,7 +306,8 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
   PYRE_CHECK_ARG(x_dtype == PYRE_F32 || x_dtype == PYRE_BF16, f + ": activation dtype must be f32 or bf16");
   PYRE_CHECK_ARG(scale_dtype == PYRE_F32 || scale_dtype == PYRE_F16, f + ": scale dtype must be f32 or f16");
   PYRE_CHECK_ARG(gemv::tiles_of(N) <= gemv::kMaxTiles, f + ": output width too large");
-  PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || K % 32 == 0, f + ": the input dim must be a multiple of 32");
+  PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || (static_cast<int64_t>(K) * (x_dtype == PYRE_BF16 ? 2 : 4)) % 16 == 0,
+                 f + ": activation rows must be 16-byte multiples");
   PYRE_CHECK_ARG(ws != nullptr, f + ": null workspace");
   PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(ws) % 256 == 0, f + ": workspace must be 256-byte aligned");
   PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0, f + ": activations must be 16-byte aligned");
@@ -323,24 +320,24 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
 using namespace pyre;
 using namespace pyre::ffn;
 
-extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H, const int8_t* qg,
-                                        const void* sg, const int8_t* qu, const void* su, int scale_dtype,
-                                        int W, void* h, int h_dtype, void* workspace, int64_t ws_bytes,
-                                        void* stream) {
+extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H, const void* wgu, int gated,
+                                        int scale_dtype, int W, void* h, int h_dtype, void* workspace,
+                                        int64_t ws_bytes, void* stream) {
   int rc = ffn_check_common(x, x_dtype, T, H, W, scale_dtype, h, workspace, ws_bytes, "pyre_ffn_gateup_silu_q80");
   if (rc) return rc;
-  PYRE_CHECK_ARG(qu != nullptr && su != nullptr, "pyre_ffn_gateup_silu_q80: null up weight");
-  PYRE_CHECK_ARG((qg == nullptr) == (sg == nullptr), "pyre_ffn_gateup_silu_q80: gate q/scale mismatch");
+  PYRE_CHECK_ARG(wgu != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0,
+                 "pyre_ffn_gateup_silu_q80: packed gate/up weights must be non-null and 16-byte aligned");
   PYRE_CHECK_ARG(h_dtype == PYRE_F32 || h_dtype == PYRE_BF16, "pyre_ffn_gateup_silu_q80: h dtype must be f32 or bf16");
-  const bool gated = qg != nullptr;
+  const int R = gated ? kUnitRowsPair : kUnitRowsSingle;
   char* wsc = static_cast<char*>(workspace);
   Params p{};
   p.x = x;
+  p.w = static_cast<const uint8_t*>(wgu);
   p.K = H;
   p.N = W;
   p.T = T;
   p.tiles = tiles_of(W);
-  p.upt = (H + kUnitRows - 1) / kUnitRows;
+  p.upt = (H + R - 1) / R;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = reinterpret_cast<unsigned int*>(wsc + kHdrCntA);
   p.status = reinterpret_cast<int*>(wsc + kHdrStatus);
@@ -349,20 +346,16 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   p.out = h;
   p.out_bf16 = h_dtype == PYRE_BF16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (gated) {
-    p.q0 = qg; p.s0 = sg; p.q1 = qu; p.s1 = su;
-    return dispatch_types<2, EPI_SILU_MUL>(p, x_dtype, scale_dtype, s);
-  }
-  p.q0 = qu; p.s0 = su; p.q1 = nullptr; p.s1 = nullptr;
+  if (gated) return dispatch_types<2, EPI_SILU_MUL>(p, x_dtype, scale_dtype, s);
   return dispatch_types<1, EPI_SILU>(p, x_dtype, scale_dtype, s);
 }
 
-extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const int8_t* qd, const void* sd,
-                                 int scale_dtype, int H, float* out, void* workspace, int64_t ws_bytes,
-                                 pyre_comm_t* comm, void* stream) {
+extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H,
+                                 float* out, void* workspace, int64_t ws_bytes, pyre_comm_t* comm, void* stream) {
   int rc = ffn_check_common(h, h_dtype, T, W, H, scale_dtype, out, workspace, ws_bytes, "pyre_ffn_down_q80");
   if (rc) return rc;
-  PYRE_CHECK_ARG(qd != nullptr && sd != nullptr, "pyre_ffn_down_q80: null weight");
+  PYRE_CHECK_ARG(wd != nullptr && reinterpret_cast<uintptr_t>(wd) % 16 == 0,
+                 "pyre_ffn_down_q80: packed down weights must be non-null and 16-byte aligned");
   if (comm != nullptr) {
     PYRE_CHECK_ARG(comm->hidden == H, "pyre_ffn_down_q80: communicator hidden size differs from H");
     PYRE_CHECK_ARG(T <= comm->max_tokens, "pyre_ffn_down_q80: T exceeds the communicator's max_tokens");
@@ -370,12 +363,12 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   char* wsc = static_cast<char*>(workspace);
   Params p{};
   p.x = h;
-  p.q0 = qd; p.s0 = sd; p.q1 = nullptr; p.s1 = nullptr;
+  p.w = static_cast<const uint8_t*>(wd);
   p.K = W;
   p.N = H;
   p.T = T;
   p.tiles = tiles_of(H);
-  p.upt = (W + kUnitRows - 1) / kUnitRows;
+  p.upt = (W + kUnitRowsSingle - 1) / kUnitRowsSingle;
   p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
   p.counters = reinterpret_cast<unsigned int*>(wsc + kHdrCntB);
   p.status = reinterpret_cast<int*>(wsc + kHdrStatus);

@@ -15,14 +15,10 @@ namespace pyre {
 namespace ffn {
 
 struct alignas(64) DecodeParams {
-  CUtensorMap tx;            // x [T, H], box T x 32
-  CUtensorMap th;            // h [T, W] f32, box T x 32
-  const int8_t* qg;          // gate (nullptr when ungated)
-  const void* sg;
-  const int8_t* qu;
-  const void* su;
-  const int8_t* qd;
-  const void* sd;
+  CUtensorMap tx;            // x [T, H], box T x R_A
+  CUtensorMap th;            // h [T, W] f32, box T x R_B
+  const uint8_t* wgu;        // packed gate/up pair (or up alone when ungated)
+  const uint8_t* wd;         // packed down
   int H, W, T;
   int tilesA, uptA;          // phase A: slabs of W, units of H
   int tilesB, uptB;          // phase B: slabs of H, units of W
@@ -117,38 +113,29 @@ q80_ffn_decode_kernel(const __grid_constant__ DecodeParams p) {
     if (lane == 0) {
       prefetch_tmap(&p.tx);
       prefetch_tmap(&p.th);
-      const int8_t* qa[2] = {NA == 2 ? p.qg : p.qu, p.qu};
-      const uint8_t* sa[2] = {static_cast<const uint8_t*>(NA == 2 ? p.sg : p.su), static_cast<const uint8_t*>(p.su)};
       int s = 0;
       uint32_t ph = 0;
       for (int64_t u = a0; u < a1; ++u) {
         const int tile = static_cast<int>(u / p.uptA);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptA) * kUnitRows;
+        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptA) * LA::kRows;
         mbar_wait(&empty[s], ph ^ 1u, p.status);
         uint8_t* st = stages + s * C::kStageBytes;
         mbar_arrive_expect_tx(&full[s], LA::kTxBytes);
-        const int64_t row0 = static_cast<int64_t>(tile) * p.H + k0;
-        for (int m = 0; m < NA; ++m) {
-          bulk_load(st + m * LA::kQBytes, qa[m] + row0 * kTileN, LA::kQBytes, &full[s]);
-          bulk_load(st + LA::kSOff + m * LA::kSBytes, sa[m] + row0 * (LA::kSBytes / kUnitRows), LA::kSBytes, &full[s]);
-        }
+        bulk_load(st, p.wgu + u * LA::kWBytes, LA::kWBytes, &full[s]);
         tma_load_2d(st + LA::kXOff, &p.tx, k0, 0, &full[s]);
         if (++s == C::kStages) {
           s = 0;
           ph ^= 1u;
         }
       }
-      const uint8_t* sd = static_cast<const uint8_t*>(p.sd);
       for (int64_t u = b0; u < b1; ++u) {
         const int tile = static_cast<int>(u / p.uptB);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptB) * kUnitRows;
+        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptB) * LB::kRows;
         mbar_wait(&empty[s], ph ^ 1u, p.status);
         uint8_t* st = stages + s * C::kStageBytes;
         mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
-        const int64_t row0 = static_cast<int64_t>(tile) * p.W + k0;
-        bulk_load(st, p.qd + row0 * kTileN, LB::kQBytes, &full[s]);
-        bulk_load(st + LB::kSOff, sd + row0 * (LB::kSBytes / kUnitRows), LB::kSBytes, &full[s]);
-        // rows k0..k0+31 of h come from gate/up slab k0 / 256
+        bulk_load(st, p.wd + u * LB::kWBytes, LB::kWBytes, &full[s]);
+        // rows k0..k0+R_B-1 of h come from gate/up slab k0 / 256 (R_B divides 256)
         wait_ready(p.ready + k0 / kTileN, epoch, p.status);
         fence_proxy_async_global();
         tma_load_2d(st + LB::kXOff, &p.th, k0, 0, &full[s]);
@@ -262,10 +249,10 @@ int launch_decode(DecodeParams p, const void* x, int64_t ws_cap, cudaStream_t s)
   int rc = set_smem_once(kern, C::kSmemBytes);
   if (rc) return rc;
   rc = make_tmap_2d(&p.tx, x, tma_dtype<XT>(), sizeof(XT), T, p.H, static_cast<uint64_t>(p.H) * sizeof(XT), T,
-                    kUnitRows);
+                    C::LA::kRows);
   if (rc) return rc;
   rc = make_tmap_2d(&p.th, p.h, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, T, p.W, static_cast<uint64_t>(p.W) * 4, T,
-                    kUnitRows);
+                    C::LB::kRows);
   if (rc) return rc;
   int G = 1;
   rc = coresident_grid(kern, kThreads, C::kSmemBytes, C::kCtasPerSm, p.UA < p.UB ? p.UA : p.UB, &G);
@@ -332,36 +319,37 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   return PYRE_OK;
 }
 
-extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, const int8_t* qg, const void* sg,
-                                   const int8_t* qu, const void* su, const int8_t* qd, const void* sd,
-                                   int scale_dtype, int W, float* out, void* workspace, int64_t ws_bytes,
-                                   pyre_comm_t* comm, void* stream) {
+extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, const void* wgu, int gated,
+                                   const void* wd, int scale_dtype, int W, float* out, void* workspace,
+                                   int64_t ws_bytes, pyre_comm_t* comm, void* stream) {
   int rc = ffn_check_common(x, x_dtype, T, H, W, scale_dtype, out, workspace, ws_bytes, "pyre_ffn_decode_q80");
   if (rc) return rc;
   PYRE_CHECK_ARG(T <= PYRE_FUSED_REDUCE_MAX_T, "pyre_ffn_decode_q80: T must be <= PYRE_FUSED_REDUCE_MAX_T");
   PYRE_CHECK_ARG(H % 32 == 0 && W % 32 == 0, "pyre_ffn_decode_q80: H and W must be multiples of 32");
-  PYRE_CHECK_ARG(qu != nullptr && su != nullptr && qd != nullptr && sd != nullptr, "pyre_ffn_decode_q80: null weight");
-  PYRE_CHECK_ARG((qg == nullptr) == (sg == nullptr), "pyre_ffn_decode_q80: gate q/scale mismatch");
+  PYRE_CHECK_ARG(wgu != nullptr && wd != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(wd) % 16 == 0,
+                 "pyre_ffn_decode_q80: packed weights must be non-null and 16-byte aligned");
   PYRE_CHECK_ARG(gemv::tiles_of(H) <= gemv::kMaxTiles && gemv::tiles_of(W) <= gemv::kMaxTiles,
                  "pyre_ffn_decode_q80: dims too large");
   if (comm != nullptr) {
     PYRE_CHECK_ARG(comm->hidden == H, "pyre_ffn_decode_q80: communicator hidden size differs from H");
     PYRE_CHECK_ARG(T <= comm->max_tokens, "pyre_ffn_decode_q80: T exceeds the communicator's max_tokens");
   }
-  const bool gated = qg != nullptr;
   const int64_t need = decode_ws_bytes(T, H, W, gated ? 2 : 1);
   if (ws_bytes < need)
     return set_error(PYRE_ENOMEM, "pyre_ffn_decode_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   char* wsc = static_cast<char*>(workspace);
   DecodeParams p{};
-  p.qg = qg; p.sg = sg; p.qu = qu; p.su = su; p.qd = qd; p.sd = sd;
+  p.wgu = static_cast<const uint8_t*>(wgu);
+  p.wd = static_cast<const uint8_t*>(wd);
   p.H = H;
   p.W = W;
   p.T = T;
+  const int ra = gated ? kUnitRowsPair : kUnitRowsSingle;
   p.tilesA = tiles_of(W);
-  p.uptA = H / kUnitRows;
+  p.uptA = (H + ra - 1) / ra;
   p.tilesB = tiles_of(H);
-  p.uptB = W / kUnitRows;
+  p.uptB = (W + kUnitRowsSingle - 1) / kUnitRowsSingle;
   p.UA = static_cast<int64_t>(p.tilesA) * p.uptA;
   p.UB = static_cast<int64_t>(p.tilesB) * p.uptB;
   p.h = reinterpret_cast<float*>(wsc + kHeaderBytes);

@@ -11,15 +11,12 @@ using namespace gemv;
 enum Epi : int { EPI_SILU_MUL = 0, EPI_SILU = 1, EPI_STORE = 2, EPI_TP = 3 };
 
 struct alignas(64) Params {
-  CUtensorMap tx;            // activations [T, K], box T x 32
+  CUtensorMap tx;            // activations [T, K], box T x R
   const void* x;
-  const int8_t* q0;          // tiled q [tiles, K, 256]; gate (NMAT == 2) or the single matrix
-  const void* s0;            // tiled scales [tiles, K, 8]
-  const int8_t* q1;          // up (NMAT == 2)
-  const void* s1;
+  const uint8_t* w;          // packed weight group (gate/up pair, or one matrix)
   int K, N, T;
   int tiles;                 // ceil(N / kTileN)
-  int upt;                   // units per tile = K / kUnitRows
+  int upt;                   // units per tile = ceil(K / R)
   int64_t total_units;       // tiles * upt
   int pmax;                  // piece slots per tile in ws
   int64_t ws_cap;            // bytes available for pieces

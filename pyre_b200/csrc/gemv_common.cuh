@@ -1,12 +1,16 @@
 // Building blocks of the Q8_0 decode GEMV kernels (T <= 4 tokens).
 //
-// Work decomposition. A [K, N] weight in the column-slab tiled layout is covered by tiles of
-// 256 output columns; a tile is covered by units of 32 input rows. One unit of one matrix
-// is a contiguous 8 KB int8 run plus 32 x 8 scales; a pipeline stage holds one unit of each
-// matrix the kernel multiplies plus the [T x 32] activation slice.
+// Packed device weight layout. A group of M matrices (M = 1, or M = 2 for gate and up,
+// which share [K, N]) is stored as blocks: for every slab of 256 output columns j and every
+// unit of R = 64 / M input rows u, one contiguous block
+//     [q of matrix 0: R x 256 int8] ... [q of matrix M-1] [scales of matrix 0: R x 8] ...
+// in (j, u) order, K padded to a multiple of R and N to a multiple of 256 with zeros. The
+// int8 values and scales are exactly the reference's Q8_0 blocks (each scale covers 32
+// consecutive output columns of one row). One block is one pipeline stage: the producer
+// moves it with a single bulk copy (~17 KB), plus the [T x R] activation slice.
 //
 // Consumer mapping. 8 consumer warps; lane (rs, cc) owns columns 16cc..16cc+15 and, for
-// pass p, row p*16 + 2*warp + rs of the unit. int8 -> f32 is exact: the byte b becomes the
+// pass p (R / 16 passes), row p*16 + 2*warp + rs of the unit. int8 -> f32 is exact: the byte b becomes the
 // float 0x4B0000uu (2^23 + u, u = b ^ 0x80) minus 2^23 + 128, done for pairs with one
 // byte-permute each and one packed f32x2 add; the block scale is folded into the
 // activation and the products accumulate with packed f32x2 FMA in f32.
@@ -22,12 +26,17 @@ namespace gemv {
 #define PYRE_GEMV_CONSUMER_WARPS 8
 #endif
 constexpr int kTileN = 256;            // output columns per tile (= slab width)
-constexpr int kUnitRows = 32;          // input rows per unit
+constexpr int kUnitRowsPair = 32;      // unit rows of a packed gate/up pair
+constexpr int kUnitRowsSingle = 64;    // unit rows of a packed single matrix
+template <int NMAT>
+struct UnitRows {
+  static constexpr int value = NMAT == 2 ? kUnitRowsPair : kUnitRowsSingle;
+};
 constexpr int kConsumerWarps = PYRE_GEMV_CONSUMER_WARPS;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;   // + one producer warp
-constexpr int kPasses = kUnitRows / (2 * kConsumerWarps);
-static_assert(kPasses >= 1 && kPasses * 2 * kConsumerWarps == kUnitRows, "consumer warps must divide 16");
+constexpr int kRowsPerPass = 2 * kConsumerWarps;
+static_assert(kUnitRowsPair % kRowsPerPass == 0 && kUnitRowsSingle % kRowsPerPass == 0, "consumer warps must divide 16");
 constexpr int kMaxGrid = 1024;
 constexpr int kMaxTiles = 2048;        // N <= 524288
 
@@ -42,16 +51,25 @@ constexpr int64_t kHdrReady = kHdrCntB + kMaxTiles * 4;
 constexpr int64_t kHeaderBytes = 32768;
 static_assert(kHdrReady + kMaxTiles * 4 <= kHeaderBytes, "workspace header overflow");
 
+// One pipeline stage: a packed weight block followed by the activation slice.
 template <int T, int NMAT, typename XT, typename ST>
 struct StageLayout {
-  static constexpr int kQBytes = kUnitRows * kTileN;                                 // 8 KB
-  static constexpr int kSBytes = kUnitRows * 8 * static_cast<int>(sizeof(ST));
-  static constexpr int kXBytes = T * kUnitRows * static_cast<int>(sizeof(XT));
+  static constexpr int kRows = UnitRows<NMAT>::value;
+  static constexpr int kQBytes = kRows * kTileN;                                     // 16 KB / NMAT
+  static constexpr int kSBytes = kRows * 8 * static_cast<int>(sizeof(ST));
   static constexpr int kSOff = NMAT * kQBytes;
-  static constexpr int kXOff = NMAT * (kQBytes + kSBytes);
+  static constexpr int kWBytes = NMAT * (kQBytes + kSBytes);                         // packed block
+  static constexpr int kXOff = kWBytes;
+  static constexpr int kXBytes = T * kRows * static_cast<int>(sizeof(XT));
   static constexpr int kTxBytes = kXOff + kXBytes;
   static constexpr int kBytes = (kTxBytes + 127) / 128 * 128;
 };
+
+// Bytes of one packed block of M matrices with scales of es bytes.
+__host__ __device__ __forceinline__ int64_t packed_block_bytes(int M, int es) {
+  const int R = M == 2 ? kUnitRowsPair : kUnitRowsSingle;
+  return static_cast<int64_t>(M) * R * (kTileN + 8 * es);
+}
 
 __device__ __forceinline__ float silu_f32(float g) { return __fdiv_rn(g, 1.0f + expf(-g)); }
 
@@ -72,11 +90,11 @@ __device__ __forceinline__ void consume_unit(const uint8_t* st, float2 (&acc)[NM
   const ST* ss = reinterpret_cast<const ST*>(st + L::kSOff);
   const XT* xs = reinterpret_cast<const XT*>(st + L::kXOff);
 #pragma unroll
-  for (int pass = 0; pass < kPasses; ++pass) {
-    const int r = pass * (2 * kConsumerWarps) + warp * 2 + rs;
+  for (int pass = 0; pass < L::kRows / kRowsPerPass; ++pass) {
+    const int r = pass * kRowsPerPass + warp * 2 + rs;
     float xv[T];
 #pragma unroll
-    for (int t = 0; t < T; ++t) xv[t] = to_f32(xs[t * kUnitRows + r]);
+    for (int t = 0; t < T; ++t) xv[t] = to_f32(xs[t * L::kRows + r]);
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
       const float sc = to_f32(ss[m * (L::kSBytes / static_cast<int>(sizeof(ST))) + r * 8 + (cc >> 1)]);

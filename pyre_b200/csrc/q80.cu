@@ -5,7 +5,7 @@
 //   absmax == 0 -> 1.0, scale = f32(absmax / 127) (IEEE f32 division),
 //   q = clip(round_half_even(f32(x / scale)), -128, 127).
 // The kernels use __fdiv_rn and rintf, so the build must not use fast-math.
-#include "common.cuh"
+#include "gemv_common.cuh"
 
 namespace pyre {
 namespace {
@@ -91,6 +91,52 @@ __global__ void __launch_bounds__(256) q80_dequantize_kernel(const int8_t* __res
   }
 }
 
+// Plain reference-orientation Q8_0 (q [K, N] int8, scales [K, N/32]) -> packed blocks
+// (see gemv_common.cuh): one thread per 16-byte chunk of a block's int8 part, one per
+// scale entry; rows past K and columns past N become zeros.
+template <typename S>
+__global__ void __launch_bounds__(256) q80_pack_kernel(const int8_t* __restrict__ q0, const S* __restrict__ s0,
+                                                       const int8_t* __restrict__ q1, const S* __restrict__ s1, int M,
+                                                       int K, int N, int upt, int64_t nblocks,
+                                                       uint8_t* __restrict__ out) {
+  const int R = M == 2 ? gemv::kUnitRowsPair : gemv::kUnitRowsSingle;
+  const int64_t bbytes = gemv::packed_block_bytes(M, sizeof(S));
+  const int64_t q_chunks = static_cast<int64_t>(M) * R * (gemv::kTileN / 16);   // per block
+  const int64_t s_items = static_cast<int64_t>(M) * R * 8;                        // per block
+  const int64_t per_block = q_chunks + s_items;
+  const int64_t total = nblocks * per_block;
+  const int nsb = N / 32;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t blk = i / per_block;
+    const int64_t w = i - blk * per_block;
+    const int j = static_cast<int>(blk / upt);
+    const int u = static_cast<int>(blk - static_cast<int64_t>(j) * upt);
+    uint8_t* base = out + blk * bbytes;
+    if (w < q_chunks) {
+      const int m = static_cast<int>(w / (R * 16));
+      const int rr = static_cast<int>((w / 16) % R);
+      const int c16 = static_cast<int>(w % 16);
+      const int k = u * R + rr;
+      const int n = j * gemv::kTileN + c16 * 16;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (k < K && n < N) v = *reinterpret_cast<const int4*>((m == 0 ? q0 : q1) + static_cast<int64_t>(k) * N + n);
+      *reinterpret_cast<int4*>(base + (static_cast<int64_t>(m) * R + rr) * gemv::kTileN + c16 * 16) = v;
+    } else {
+      const int64_t e = w - q_chunks;
+      const int m = static_cast<int>(e / (R * 8));
+      const int rr = static_cast<int>((e / 8) % R);
+      const int sc = static_cast<int>(e % 8);
+      const int k = u * R + rr;
+      const int bc = j * 8 + sc;
+      S v = S(0.f);
+      if (k < K && bc < nsb) v = (m == 0 ? s0 : s1)[static_cast<int64_t>(k) * nsb + bc];
+      S* sbase = reinterpret_cast<S*>(base + static_cast<int64_t>(M) * R * gemv::kTileN);
+      sbase[(static_cast<int64_t>(m) * R + rr) * 8 + sc] = v;
+    }
+  }
+}
+
 int grid_for(int64_t work, int threads) {
   const int64_t want = (work + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -150,5 +196,44 @@ extern "C" int pyre_q80_dequantize(const int8_t* q, const void* scale, int scale
   else
     q80_dequantize_kernel<__half><<<grid, threads, 0, s>>>(q, static_cast<const __half*>(scale), n, out);
   PYRE_LAUNCH_CHECK("q80_dequantize_kernel");
+  return PYRE_OK;
+}
+
+extern "C" int pyre_q80_packed_bytes(int M, int K, int N, int scale_dtype, int64_t* bytes) {
+  using namespace pyre;
+  PYRE_CHECK_ARG(bytes != nullptr, "pyre_q80_packed_bytes: null bytes");
+  PYRE_CHECK_ARG(M == 1 || M == 2, "pyre_q80_packed_bytes: M must be 1 or 2");
+  PYRE_CHECK_ARG(K >= 1 && N >= 32 && N % 32 == 0, "pyre_q80_packed_bytes: need K >= 1 and N a multiple of 32");
+  PYRE_CHECK_ARG(scale_dtype == PYRE_F32 || scale_dtype == PYRE_F16, "pyre_q80_packed_bytes: bad scale dtype");
+  const int R = M == 2 ? gemv::kUnitRowsPair : gemv::kUnitRowsSingle;
+  const int64_t nt = (N + gemv::kTileN - 1) / gemv::kTileN, upt = (K + R - 1) / R;
+  *bytes = nt * upt * gemv::packed_block_bytes(M, scale_dtype == PYRE_F16 ? 2 : 4);
+  return PYRE_OK;
+}
+
+extern "C" int pyre_q80_pack(int M, const int8_t* q0, const void* s0, const int8_t* q1, const void* s1, int K, int N,
+                             int scale_dtype, void* out, void* stream) {
+  using namespace pyre;
+  int64_t bytes = 0;
+  int rc = pyre_q80_packed_bytes(M, K, N, scale_dtype, &bytes);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(q0 != nullptr && s0 != nullptr && out != nullptr, "pyre_q80_pack: null pointer");
+  PYRE_CHECK_ARG(M == 1 || (q1 != nullptr && s1 != nullptr), "pyre_q80_pack: M == 2 needs both matrices");
+  PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(q0) % 16 == 0 && (q1 == nullptr || reinterpret_cast<uintptr_t>(q1) % 16 == 0) &&
+                     reinterpret_cast<uintptr_t>(out) % 16 == 0,
+                 "pyre_q80_pack: q and out must be 16-byte aligned");
+  const int R = M == 2 ? gemv::kUnitRowsPair : gemv::kUnitRowsSingle;
+  const int upt = (K + R - 1) / R;
+  const int64_t nblocks = static_cast<int64_t>((N + gemv::kTileN - 1) / gemv::kTileN) * upt;
+  const int64_t work = nblocks * (static_cast<int64_t>(M) * R * 16 + static_cast<int64_t>(M) * R * 8);
+  const int grid = grid_for(work, 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (scale_dtype == PYRE_F16)
+    q80_pack_kernel<__half><<<grid, 256, 0, s>>>(q0, static_cast<const __half*>(s0), q1, static_cast<const __half*>(s1),
+                                                 M, K, N, upt, nblocks, static_cast<uint8_t*>(out));
+  else
+    q80_pack_kernel<float><<<grid, 256, 0, s>>>(q0, static_cast<const float*>(s0), q1, static_cast<const float*>(s1),
+                                                M, K, N, upt, nblocks, static_cast<uint8_t*>(out));
+  PYRE_LAUNCH_CHECK("q80_pack_kernel");
   return PYRE_OK;
 }

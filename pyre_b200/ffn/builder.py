@@ -22,7 +22,7 @@ import torch
 from .. import _device as D
 from ..engine import DeviceRef, Graph, InferenceSession, Tensor
 from ..quantizer import Q80Weight
-from .op import FfnShardOp
+from .op import FfnShardOp, FfnWeights
 
 
 @dataclass(frozen=True)
@@ -89,7 +89,7 @@ class FfnModel:
                 gate = None
                 up = _as_weight(inputs[1], (H, W))
                 down = _as_weight(inputs[2], (W, H))
-            out = self.op(x.reshape(S, H), gate, up, down)
+            out = self.op.run(x.reshape(S, H), FfnWeights.prepare(gate, up, down))
             return (Tensor(out.reshape(1, S, H)),)
 
 

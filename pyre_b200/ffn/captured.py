@@ -12,13 +12,11 @@ from __future__ import annotations
 
 import torch
 
-from ..quantizer import Q80Weight
-from .op import FfnShardOp
+from .op import FfnShardOp, FfnWeights
 
 
 class CapturedFfn:
-    def __init__(self, op: FfnShardOp, gate: Q80Weight | None, up: Q80Weight, down: Q80Weight, tokens: int,
-                 x_dtype: torch.dtype = torch.bfloat16):
+    def __init__(self, op: FfnShardOp, weights: FfnWeights, tokens: int, x_dtype: torch.dtype = torch.bfloat16):
         if tokens > op.max_tokens:
             raise ValueError("tokens exceeds the op's max_tokens")
         self.op = op
@@ -28,16 +26,16 @@ class CapturedFfn:
         self.out_host = torch.empty((tokens, op.hidden), dtype=torch.float32, pin_memory=True)
         self.x_dev = torch.zeros((tokens, op.hidden), dtype=x_dtype, device=dev)
         self.out_dev = torch.zeros((tokens, op.hidden), dtype=torch.float32, device=dev)
-        self._w = (gate, up, down)
+        self._w = weights
         self.stream = torch.cuda.Stream(device=dev)
         # one eager call on the capture stream first (sets up lazy state, checks arguments)
         with torch.cuda.stream(self.stream):
-            op(self.x_dev, gate, up, down, out=self.out_dev, stream=self.stream)
+            op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
         self.stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
             self.x_dev.copy_(self.x_host, non_blocking=True)
-            op(self.x_dev, gate, up, down, out=self.out_dev, stream=self.stream)
+            op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
             self.out_host.copy_(self.out_dev, non_blocking=True)
 
     @property

@@ -8,18 +8,49 @@ done inside the down-projection's epilogue over NVLink.
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 
 import torch
 
 from .. import _device as D
 from .. import _native as N
-from ..quantizer import Q80Weight
+from ..quantizer import Q80Packed, Q80Weight
 
 
 def workspace_bytes(tokens: int, hidden: int, width: int) -> int:
     out = ctypes.c_int64(0)
     N.call("pyre_ffn_workspace_bytes", int(tokens), int(hidden), int(width), ctypes.byref(out))
     return int(out.value)
+
+
+@dataclass
+class FfnWeights:
+    """One shard's weights in the kernels' packed layout (prepare once, call many times):
+    gate and up packed as a pair (or up alone when ungated), down packed alone."""
+
+    gateup: Q80Packed
+    down: Q80Packed
+    gated: bool
+
+    @property
+    def hidden(self) -> int:
+        return self.gateup.k
+
+    @property
+    def width(self) -> int:
+        return self.gateup.n
+
+    @classmethod
+    def prepare(cls, gate: Q80Weight | None, up: Q80Weight, down: Q80Weight) -> "FfnWeights":
+        H, W = up.shape
+        if gate is not None and (gate.shape != (H, W) or gate.scale.dtype != up.scale.dtype):
+            raise ValueError(f"gate weight must be {(H, W)} with the up weight's scale dtype")
+        if down.shape != (W, H):
+            raise ValueError(f"down weight must be {(W, H)}, got {down.shape}")
+        if down.scale.dtype != up.scale.dtype:
+            raise ValueError("down and up scales must share a dtype")
+        gu = Q80Packed.pack([gate, up] if gate is not None else [up])
+        return cls(gu, Q80Packed.pack(down), gate is not None)
 
 
 class FfnShardOp:
@@ -66,6 +97,12 @@ class FfnShardOp:
 
     def __call__(self, x: torch.Tensor, gate: Q80Weight | None, up: Q80Weight, down: Q80Weight,
                  out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """Convenience form on Q8_0 weights (packs them on every call); prepare an
+        :class:`FfnWeights` once and use :meth:`run` on a hot path."""
+        return self.run(x, FfnWeights.prepare(gate, up, down), out=out, stream=stream)
+
+    def run(self, x: torch.Tensor, w: FfnWeights, out: torch.Tensor | None = None,
+            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         if x.dim() != 2 or x.shape[1] != self.hidden:
             raise ValueError(f"x must be [T, {self.hidden}], got {tuple(x.shape)}")
         T = x.shape[0]
@@ -75,34 +112,24 @@ class FfnShardOp:
             raise ValueError("x must be float32 or bfloat16")
         if not x.is_contiguous():
             x = x.contiguous()
-        if self.gated and gate is None:
-            raise ValueError("gated FFN needs a gate weight")
-        for name, w, shp in (("gate", gate, (self.hidden, self.width)), ("up", up, (self.hidden, self.width)),
-                             ("down", down, (self.width, self.hidden))):
-            if w is None:
-                continue
-            if tuple(w.shape) != shp:
-                raise ValueError(f"{name} weight must be {shp}, got {tuple(w.shape)}")
-        if gate is not None and gate.scale.dtype != up.scale.dtype:
-            raise ValueError("gate and up scales must share a dtype")
-        if down.scale.dtype != up.scale.dtype:
-            raise ValueError("down and up scales must share a dtype")
+        if w.hidden != self.hidden or w.width != self.width:
+            raise ValueError(f"weights are [{w.hidden}, {w.width}], op is [{self.hidden}, {self.width}]")
+        if self.gated != w.gated:
+            raise ValueError("gated op needs gated weights (and ungated op ungated ones)")
         s = D.stream_ptr(stream)
         if out is None:
             out = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
         ws = self.workspace
         comm = ctypes.c_void_p(self.comm.handle if self.comm is not None else 0)
+        gated = 1 if w.gated else 0
+        code = w.gateup.scale_code
         if self.fused and T <= N.PYRE_FUSED_REDUCE_MAX_T:
-            N.call("pyre_ffn_decode_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
-                   D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
-                   D.ptr(up.q), D.ptr(up.scale), D.ptr(down.q), D.ptr(down.scale), up.scale_code, self.width,
-                   D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
+            N.call("pyre_ffn_decode_q80", D.ptr(x), D.dtype_code(x), T, self.hidden, D.ptr(w.gateup.data), gated,
+                   D.ptr(w.down.data), code, self.width, D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
             return out
         h = torch.empty((T, self.width), dtype=self.h_dtype(T), device=x.device)
-        N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), T, self.hidden,
-               D.ptr(gate.q if gate is not None else None), D.ptr(gate.scale if gate is not None else None),
-               D.ptr(up.q), D.ptr(up.scale), up.scale_code, self.width,
-               D.ptr(h), D.dtype_code(h), D.ptr(ws), ws.numel(), s)
-        N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), T, self.width, D.ptr(down.q), D.ptr(down.scale),
-               down.scale_code, self.hidden, D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
+        N.call("pyre_ffn_gateup_silu_q80", D.ptr(x), D.dtype_code(x), T, self.hidden, D.ptr(w.gateup.data), gated,
+               code, self.width, D.ptr(h), D.dtype_code(h), D.ptr(ws), ws.numel(), s)
+        N.call("pyre_ffn_down_q80", D.ptr(h), D.dtype_code(h), T, self.width, D.ptr(w.down.data), code,
+               self.hidden, D.ptr(out), D.ptr(ws), ws.numel(), comm, s)
         return out

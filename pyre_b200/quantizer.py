@@ -9,14 +9,15 @@ with the arithmetic done by the sm_100a kernels of ``libpyre_b200.so``:
 * :func:`quantize_weights_dict` / :func:`dequantize_weights_dict` — ``quantizer.py:70-114``
   (``("q8", q, s, shape)`` tags, ``MIN_QUANTIZE_ELEMS`` threshold).
 
-:class:`Q80Weight` is the GEMV/GEMM operand: the reference's Q8_0 blocks of a ``[K, N]``
-weight (stored ``[in, out]``), laid out in column slabs of 256 (``q [NT, K, 256]`` int8,
-``scale [NT, K, 8]`` f16 by default or f32), N zero-padded to a multiple of 256. Each
-32-row unit of a slab is one contiguous 8 KB run that the kernels stream with bulk
-copies; the int8 values and scales are exactly the reference's.
+:class:`Q80Weight` holds one ``[K, N]`` weight (stored ``[in, out]`` like the reference) as
+its Q8_0 blocks in the reference orientation: ``q [K, N]`` int8 and ``scale [K, N/32]`` (f16
+by default, f32 for the exact-scale variant). :class:`Q80Packed` is the kernels' operand:
+one or two such weights (gate and up) in the packed block layout of ``include/pyre_b200.h``
+(one ~17 KB block per 256-column slab and 64/M-row unit, streamed with one bulk copy).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Tuple
 
@@ -139,20 +140,23 @@ def _numel(v) -> int:
 
 
 SLAB = 256
-SLAB_SCALES = SLAB // BLOCK
 
 
 @dataclass
 class Q80Weight:
-    """A ``[K, N]`` weight in Q8_0, column-slab tiled on the device (see module doc)."""
+    """A ``[K, N]`` weight in Q8_0 on the device: ``q [K, N]`` int8, ``scale [K, N/32]``."""
 
-    q: torch.Tensor       # [NT, K, 256] int8
-    scale: torch.Tensor   # [NT, K, 8] f16 or f32
-    n: int                # logical output width N
+    q: torch.Tensor
+    scale: torch.Tensor
+
+    def __post_init__(self):
+        K, Nn = self.q.shape
+        if Nn % BLOCK or tuple(self.scale.shape) != (K, Nn // BLOCK):
+            raise ValueError("Q80Weight needs q [K, N] with N % 32 == 0 and scale [K, N/32]")
 
     @property
     def shape(self) -> Tuple[int, int]:
-        return (int(self.q.shape[1]), int(self.n))
+        return tuple(self.q.shape)
 
     @property
     def scale_code(self) -> int:
@@ -160,34 +164,7 @@ class Q80Weight:
 
     @property
     def nbytes(self) -> int:
-        """Bytes of the format proper (int8 + one scale per 32 weights, padding excluded)."""
-        K, Nn = self.shape
-        return K * Nn + K * (Nn // BLOCK) * self.scale.element_size()
-
-    @classmethod
-    def from_plain(cls, q: torch.Tensor, s: torch.Tensor) -> "Q80Weight":
-        """From plain ``q [K, N]`` int8 and ``s [K, N/32]`` block scales (device tensors)."""
-        K, Nn = q.shape
-        if Nn % BLOCK or tuple(s.shape) != (K, Nn // BLOCK):
-            raise ValueError("Q80Weight.from_plain: need q [K, N] with N % 32 == 0 and s [K, N/32]")
-        nt = (Nn + SLAB - 1) // SLAB
-        qp = torch.zeros((K, nt * SLAB), dtype=torch.int8, device=q.device)
-        qp[:, :Nn] = q
-        sp = torch.zeros((K, nt * SLAB_SCALES), dtype=s.dtype, device=s.device)
-        sp[:, : Nn // BLOCK] = s
-        return cls(qp.view(K, nt, SLAB).permute(1, 0, 2).contiguous(),
-                   sp.view(K, nt, SLAB_SCALES).permute(1, 0, 2).contiguous(), Nn)
-
-    def plain(self) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Plain ``(q [K, N], s [K, N/32])`` views of the tiled storage (copies)."""
-        nt, K, _ = self.q.shape
-        q = self.q.permute(1, 0, 2).reshape(K, nt * SLAB)[:, : self.n]
-        s = self.scale.permute(1, 0, 2).reshape(K, nt * SLAB_SCALES)[:, : self.n // BLOCK]
-        return q.contiguous(), s.contiguous()
-
-    @property
-    def block_scales(self) -> torch.Tensor:
-        return self.plain()[1]
+        return self.q.numel() + self.scale.numel() * self.scale.element_size()
 
     @classmethod
     def from_float(cls, w, scale_dtype: torch.dtype = torch.float16) -> "Q80Weight":
@@ -208,7 +185,7 @@ class Q80Weight:
         s16 = s if scale_dtype == torch.float16 else None
         N.call("pyre_q80_quantize", D.ptr(t), D.dtype_code(t), K * Nn, D.ptr(q), D.ptr(s32), D.ptr(s16),
                D.stream_ptr())
-        return cls.from_plain(q, s)
+        return cls(q, s)
 
     @classmethod
     def from_tuple(cls, tup, scale_dtype: torch.dtype | None = None) -> "Q80Weight":
@@ -226,27 +203,66 @@ class Q80Weight:
             st = st.to(scale_dtype)
         elif st.dtype not in (torch.float16, torch.float32):
             st = st.to(torch.float32)
-        return cls.from_plain(qt, st)
+        return cls(qt.contiguous(), st.contiguous())
 
     def dequantize(self) -> torch.Tensor:
         K, Nn = self.shape
-        q, s = self.plain()
         out = torch.empty((K, Nn), dtype=torch.float32, device=self.q.device)
-        N.call("pyre_q80_dequantize", D.ptr(q), D.ptr(s), self.scale_code, K * Nn, D.ptr(out), D.stream_ptr())
+        N.call("pyre_q80_dequantize", D.ptr(self.q), D.ptr(self.scale), self.scale_code, K * Nn, D.ptr(out),
+               D.stream_ptr())
         return out
 
     def to_tuple(self) -> tuple:
         """Reference tuple ``("q8", q [n_blocks, 32], scales [n_blocks], shape)`` (device tensors)."""
-        q, s = self.plain()
-        return ("q8", q.reshape(-1, BLOCK), s.reshape(-1), self.shape)
+        return ("q8", self.q.reshape(-1, BLOCK), self.scale.reshape(-1), self.shape)
 
     def cols(self, start: int, end: int) -> "Q80Weight":
         """Columns [start, end) (a gate/up shard); both multiples of 32."""
         if start % BLOCK or end % BLOCK:
             raise ValueError("column shard bounds must be multiples of 32")
-        q, s = self.plain()
-        return Q80Weight.from_plain(q[:, start:end].contiguous(), s[:, start // BLOCK:end // BLOCK].contiguous())
+        return Q80Weight(self.q[:, start:end].contiguous(), self.scale[:, start // BLOCK:end // BLOCK].contiguous())
 
     def rows(self, start: int, end: int) -> "Q80Weight":
         """Rows [start, end) (a down shard)."""
-        return Q80Weight(self.q[:, start:end].contiguous(), self.scale[:, start:end].contiguous(), self.n)
+        return Q80Weight(self.q[start:end].contiguous(), self.scale[start:end].contiguous())
+
+
+@dataclass
+class Q80Packed:
+    """One weight (M = 1) or a gate/up pair (M = 2) in the packed block layout."""
+
+    data: torch.Tensor      # uint8, pyre_q80_packed_bytes() bytes
+    m: int
+    k: int
+    n: int
+    scale_dtype: torch.dtype
+
+    @property
+    def scale_code(self) -> int:
+        return N.PYRE_F16 if self.scale_dtype == torch.float16 else N.PYRE_F32
+
+    @property
+    def nbytes_payload(self) -> int:
+        """Q8_0 bytes of the packed weights (padding excluded)."""
+        es = 2 if self.scale_dtype == torch.float16 else 4
+        return self.m * (self.k * self.n + self.k * (self.n // BLOCK) * es)
+
+    @classmethod
+    def pack(cls, weights) -> "Q80Packed":
+        """Pack one Q80Weight, or a (gate, up) pair sharing shape and scale dtype."""
+        ws = list(weights) if isinstance(weights, (list, tuple)) else [weights]
+        if len(ws) not in (1, 2):
+            raise ValueError("pack one weight or a (gate, up) pair")
+        K, Nn = ws[0].shape
+        for w in ws[1:]:
+            if w.shape != (K, Nn) or w.scale.dtype != ws[0].scale.dtype:
+                raise ValueError("packed matrices must share shape and scale dtype")
+        code = ws[0].scale_code
+        nbytes = ctypes.c_int64(0)
+        N.call("pyre_q80_packed_bytes", len(ws), K, Nn, code, ctypes.byref(nbytes))
+        out = torch.empty(int(nbytes.value), dtype=torch.uint8, device=ws[0].q.device)
+        q1 = ws[1].q if len(ws) == 2 else None
+        s1 = ws[1].scale if len(ws) == 2 else None
+        N.call("pyre_q80_pack", len(ws), D.ptr(ws[0].q), D.ptr(ws[0].scale), D.ptr(q1), D.ptr(s1), K, Nn, code,
+               D.ptr(out), D.stream_ptr())
+        return cls(out, len(ws), K, Nn, ws[0].scale.dtype)

@@ -52,17 +52,21 @@ def test_quantize_argument_checks_need_no_gpu(native_lib):
     assert native_lib.pyre_q80_quantize(None, N.PYRE_F32, 0, None, None, None, None) == N.PYRE_OK
     assert native_lib.pyre_q80_quantize(ctypes.c_void_p(16), 7, 32, ctypes.c_void_p(16),
                                         ctypes.c_void_p(16), None, None) == N.PYRE_EINVAL
-    assert native_lib.pyre_ffn_gateup_silu_q80(None, N.PYRE_F32, 1, 64, None, None, None, None, N.PYRE_F32, 64,
+    assert native_lib.pyre_ffn_gateup_silu_q80(None, N.PYRE_F32, 1, 64, None, 1, N.PYRE_F32, 64,
                                                None, N.PYRE_F32, None, 0, None) == N.PYRE_EINVAL
-    assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 64, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), N.PYRE_F32, 48, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), 1 << 20, None, None) == N.PYRE_EINVAL
+    ws = ctypes.c_void_p(256)
+    assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 64, ctypes.c_void_p(16), N.PYRE_F32, 48,
+                                        ctypes.c_void_p(16), ws, 1 << 20, None, None) == N.PYRE_EINVAL
     assert "multiple of 32" in N.last_error()
-    # decode path needs the input dim on whole 32-row units
-    assert native_lib.pyre_ffn_down_q80(ctypes.c_void_p(16), N.PYRE_F32, 1, 48, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), N.PYRE_F16, 64, ctypes.c_void_p(16),
-                                        ctypes.c_void_p(16), 1 << 20, None, None) == N.PYRE_EINVAL
-    assert "input dim" in N.last_error()
+    # a workspace smaller than the header is refused before any launch
+    assert native_lib.pyre_ffn_decode_q80(ctypes.c_void_p(16), N.PYRE_BF16, 1, 64, ctypes.c_void_p(16), 1,
+                                          ctypes.c_void_p(16), N.PYRE_F16, 64, ctypes.c_void_p(16), ws, 64, None,
+                                          None) == N.PYRE_EINVAL
+    assert "workspace" in N.last_error()
+    b = ctypes.c_int64(0)
+    N.check(native_lib.pyre_q80_packed_bytes(2, 4096, 14336, N.PYRE_F16, ctypes.byref(b)))
+    assert b.value == 56 * 128 * 2 * 32 * (256 + 16)
+    assert native_lib.pyre_q80_packed_bytes(3, 64, 64, N.PYRE_F16, ctypes.byref(b)) == N.PYRE_EINVAL
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):

@@ -5,6 +5,8 @@ import pytest
 import torch
 
 from conftest import GOLDEN
+import sys, os
+sys.path.insert(0, os.path.dirname(__file__))
 from oracle import q80 as oq80
 
 pytestmark = pytest.mark.gpu
@@ -116,3 +118,17 @@ def test_q80weight_tuple_roundtrip_is_reference_bits():
     assert sh == x.shape
     np.testing.assert_array_equal(q2.cpu().numpy(), q)
     np.testing.assert_array_equal(s2.cpu().numpy().view(np.uint32), s.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 64, 256), (1, 100, 800), (2, 96, 512), (2, 40, 352), (1, 4096, 1344)])
+@pytest.mark.parametrize("scale_dtype", [torch.float16, torch.float32])
+def test_pack_kernel_matches_layout(M, K, N, scale_dtype):
+    from test_layout import pack_reference
+    from pyre_b200.quantizer import Q80Packed, Q80Weight
+    g = torch.Generator().manual_seed(K + N + M)
+    ws = [Q80Weight(torch.randint(-128, 128, (K, N), generator=g, dtype=torch.int8).cuda(),
+                    torch.rand((K, N // 32), generator=g).to(scale_dtype).cuda()) for _ in range(M)]
+    packed = Q80Packed.pack(ws)
+    es = np.float16 if scale_dtype == torch.float16 else np.float32
+    ref = pack_reference([w.q.cpu().numpy() for w in ws], [w.scale.cpu().numpy() for w in ws], es)
+    np.testing.assert_array_equal(packed.data.cpu().numpy(), ref)
