@@ -1,6 +1,6 @@
 // Gated-SiLU FFN shard on Q8_0 weights, two-call form: gate/up + SiLU·mul, then down
-// (+ the cross-rank sum). Decode (T <= 4) runs the TMA-fed stream-K GEMV of
-// gemv_common.cuh; larger T runs a SIMT dequant GEMM (placeholder for the tensor-core path).
+// (+ the cross-rank sum). Decode (T <= 4) runs the streaming kernel of ffn_stream.cuh;
+// larger T runs a SIMT dequant GEMM (placeholder for the tensor-core path).
 //
 // Reference semantics (src/ffn/builder.py:37-45, src/orchestrator/root_node.py:972-980):
 //   gate = x @ Wg, up = x @ Wu, h = silu(gate) * up, partial = h @ Wd
@@ -27,137 +27,6 @@ __device__ __forceinline__ float ld_scale(const void* s, int64_t i) {
 template <typename XT>
 __device__ __forceinline__ float ld_x(const void* x, int64_t i) {
   return to_f32(__ldg(static_cast<const XT*>(x) + i));
-}
-
-// Epilogue over the finished tile sums held in shared memory `fin` ([NMAT][T][kTileN]).
-template <int T, int NMAT, int EPI>
-__device__ void tile_epilogue(const Params& p, int tile, const float* fin, uint32_t epoch, int tid) {
-  if constexpr (EPI == EPI_TP) {
-    tp_reduce_tile<T>(p.comm, epoch, tile, fin, static_cast<float*>(p.out), p.N, tid);
-  } else {
-    for (int i = tid; i < T * kTileN; i += kConsumers) {
-      const int t = i / kTileN, cc = i % kTileN;
-      const int col = tile * kTileN + cc;
-      if (col >= p.N) continue;
-      float v;
-      if constexpr (EPI == EPI_SILU_MUL) {
-        v = silu_f32(fin[i]) * fin[T * kTileN + i];
-      } else if constexpr (EPI == EPI_SILU) {
-        v = silu_f32(fin[i]);
-      } else {
-        v = fin[i];
-      }
-      store_out(p.out, p.out_bf16, p.N, t, col, v);
-    }
-  }
-}
-
-#ifndef PYRE_GEMV_STAGES
-#define PYRE_GEMV_STAGES 4
-#endif
-template <int T, int NMAT, typename XT, typename ST>
-struct GemvCfg {
-  using L = StageLayout<T, NMAT, XT, ST>;
-  // T <= 2: two CTAs per SM with a 4-stage ring each; T >= 3 (larger reduction buffers):
-  // one CTA per SM with 5 stages.
-  static constexpr int kCtasPerSm = (T <= 2) ? 2 : 1;
-  static constexpr int kStages = (T <= 2) ? PYRE_GEMV_STAGES : 5;
-  static constexpr int kRedFloats = kConsumerWarps * NMAT * T * kTileN;
-  static constexpr int kFinFloats = NMAT * T * kTileN;
-  static constexpr int kSmemBytes = kStages * L::kBytes + (kRedFloats + kFinFloats) * 4 + 2 * kStages * 8 + 16;
-};
-
-// Decode GEMV over tiled Q8_0 weights.
-//   warp 8 (producer): lane 0 streams, per unit, the int8 run and scales of each matrix
-//     (bulk copies) and the activation slice (tensor-map copy) into an mbarrier ring.
-//   warps 0-7 (consumers): consume_unit() per stage, then per tile reduce_tile(),
-//     fixup_tile() and the epilogue.
-template <int T, int NMAT, int EPI, typename XT, typename ST>
-__global__ void __launch_bounds__(kThreads, (GemvCfg<T, NMAT, XT, ST>::kCtasPerSm))
-q80_gemv_kernel(const __grid_constant__ Params p) {
-  using C = GemvCfg<T, NMAT, XT, ST>;
-  using L = typename C::L;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* stages = smem;
-  float* red = reinterpret_cast<float*>(smem + C::kStages * L::kBytes);
-  float* fin = red + C::kRedFloats;
-  uint64_t* full = reinterpret_cast<uint64_t*>(fin + C::kFinFloats);
-  uint64_t* empty = full + C::kStages;
-  int* s_last = reinterpret_cast<int*>(empty + C::kStages);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int c = blockIdx.x;
-  const int64_t U = p.total_units;
-  const int64_t u_begin = (static_cast<int64_t>(c) * U) / G;
-  const int64_t u_end = (static_cast<int64_t>(c + 1) * U) / G;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < C::kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  uint32_t epoch = 0;
-  if constexpr (EPI == EPI_TP) epoch = comm::epoch_begin(p.comm);
-
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      prefetch_tmap(&p.tx);
-      int s = 0;
-      uint32_t ph = 0;
-      for (int64_t u = u_begin; u < u_end; ++u) {
-        const int tile = static_cast<int>(u / p.upt);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.upt) * L::kRows;
-        mbar_wait(&empty[s], ph ^ 1u, p.status);
-        uint8_t* st = stages + s * L::kBytes;
-        mbar_arrive_expect_tx(&full[s], L::kTxBytes);
-        bulk_load(st, p.w + u * L::kWBytes, L::kWBytes, &full[s]);   // block index == unit index
-        tma_load_2d(st + L::kXOff, &p.tx, k0, 0, &full[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-    }
-  } else {
-    // ---------------- consumers ----------------
-    const int tid = threadIdx.x;
-    const int rs = lane >> 4;
-    const int cc = lane & 15;
-    int s = 0;
-    uint32_t ph = 0;
-    int64_t u = u_begin;
-    while (u < u_end) {
-      const int tile = static_cast<int>(u / p.upt);
-      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.upt;
-      const int64_t seg_end = min(u_end, tile_u0 + p.upt);
-      float2 acc[NMAT][T][8];
-      zero_acc<NMAT, T>(acc);
-      for (; u < seg_end; ++u) {
-        mbar_wait(&full[s], ph, p.status);
-        consume_unit<T, NMAT, XT, ST>(stages + s * L::kBytes, acc, warp, rs, cc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-      reduce_tile<T, NMAT>(acc, red, fin, warp, rs, cc, tid);
-      const int cf = cta_of_unit(tile_u0, U, G);
-      const int cl = cta_of_unit(tile_u0 + p.upt - 1, U, G);
-      if (fixup_tile<T, NMAT>(fin, p.ws, p.counters, p.pmax, tile, c, cf, cl, s_last, tid))
-        tile_epilogue<T, NMAT, EPI>(p, tile, fin, epoch, tid);
-      consumer_sync();
-    }
-  }
-  __syncthreads();
-  if constexpr (EPI == EPI_TP) comm::epoch_end(p.comm, epoch);
 }
 
 // ---- SIMT GEMM for T > 4 --------------------------------------------------------------
@@ -247,36 +116,8 @@ __global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
 
 // ---- host side ------------------------------------------------------------------------
 
-template <int T, int NMAT, int EPI, typename XT, typename ST>
-int launch_gemv(Params p, cudaStream_t s) {
-  using C = GemvCfg<T, NMAT, XT, ST>;
-  using L = typename C::L;
-  auto kern = q80_gemv_kernel<T, NMAT, EPI, XT, ST>;
-  int rc = set_smem_once(kern, C::kSmemBytes);
-  if (rc) return rc;
-  rc = make_tmap_2d(&p.tx, p.x, tma_dtype<XT>(), sizeof(XT), p.T, p.K, static_cast<uint64_t>(p.K) * sizeof(XT), T,
-                    L::kRows);
-  if (rc) return rc;
-  int G = 1;
-  rc = coresident_grid(kern, kThreads, C::kSmemBytes, C::kCtasPerSm, p.total_units, &G);
-  if (rc) return rc;
-  p.pmax = pmax_for(p.tiles, p.upt, G);
-  if (static_cast<int64_t>(p.tiles) * p.pmax * NMAT * T * kTileN * 4 > p.ws_cap)
-    return set_error(PYRE_ENOMEM, "q80_gemv: stream-K workspace too small for this grid");
-  kern<<<G, kThreads, C::kSmemBytes, s>>>(p);
-  PYRE_LAUNCH_CHECK("q80_gemv_kernel");
-  return PYRE_OK;
-}
-
 template <int NMAT, int EPI, typename XT, typename ST>
 int dispatch_T(Params p, cudaStream_t s) {
-  switch (p.T) {
-    case 1: return launch_gemv<1, NMAT, EPI, XT, ST>(p, s);
-    case 2: return launch_gemv<2, NMAT, EPI, XT, ST>(p, s);
-    case 3: return launch_gemv<3, NMAT, EPI, XT, ST>(p, s);
-    case 4: return launch_gemv<4, NMAT, EPI, XT, ST>(p, s);
-    default: break;
-  }
   static_assert(EPI != EPI_TP || NMAT == 1, "TP epilogue is single-matrix");
   dim3 grid((p.N + kGN - 1) / kGN, (p.T + kGM - 1) / kGM);
   constexpr int GEPI = EPI == EPI_TP ? EPI_STORE : EPI;
@@ -328,6 +169,9 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   PYRE_CHECK_ARG(wgu != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0,
                  "pyre_ffn_gateup_silu_q80: packed gate/up weights must be non-null and 16-byte aligned");
   PYRE_CHECK_ARG(h_dtype == PYRE_F32 || h_dtype == PYRE_BF16, "pyre_ffn_gateup_silu_q80: h dtype must be f32 or bf16");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T <= PYRE_FUSED_REDUCE_MAX_T)
+    return ffn_stream_gateup(x, x_dtype, T, H, wgu, gated, scale_dtype, W, h, h_dtype, workspace, ws_bytes, s);
   const int R = gated ? kUnitRowsPair : kUnitRowsSingle;
   char* wsc = static_cast<char*>(workspace);
   Params p{};
@@ -345,7 +189,6 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   p.ws_cap = ws_bytes - kHeaderBytes;
   p.out = h;
   p.out_bf16 = h_dtype == PYRE_BF16;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (gated) return dispatch_types<2, EPI_SILU_MUL>(p, x_dtype, scale_dtype, s);
   return dispatch_types<1, EPI_SILU>(p, x_dtype, scale_dtype, s);
 }
@@ -360,6 +203,9 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
     PYRE_CHECK_ARG(comm->hidden == H, "pyre_ffn_down_q80: communicator hidden size differs from H");
     PYRE_CHECK_ARG(T <= comm->max_tokens, "pyre_ffn_down_q80: T exceeds the communicator's max_tokens");
   }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T <= PYRE_FUSED_REDUCE_MAX_T)
+    return ffn_stream_down(h, h_dtype, T, W, wd, scale_dtype, H, out, workspace, ws_bytes, comm, s);
   char* wsc = static_cast<char*>(workspace);
   Params p{};
   p.x = h;
@@ -376,12 +222,7 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   p.ws_cap = ws_bytes - kHeaderBytes;
   p.out = out;
   p.out_bf16 = 0;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tp = comm != nullptr && comm->world > 1;
-  if (tp && T <= PYRE_FUSED_REDUCE_MAX_T) {
-    p.comm = comm::device_view(comm);
-    return dispatch_types<1, EPI_TP>(p, h_dtype, scale_dtype, s);
-  }
   rc = dispatch_types<1, EPI_STORE>(p, h_dtype, scale_dtype, s);
   if (rc || !tp) return rc;
   return allreduce_sum_f32(comm, out, static_cast<int64_t>(T) * H, s);

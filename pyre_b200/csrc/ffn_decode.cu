@@ -1,307 +1,171 @@
-// One persistent launch per FFN shard call for decode (T <= 4 tokens):
-//   phase A: h[T, W] = silu(x @ Wg) * (x @ Wu)   (stream-K over gate/up slabs)
-//   phase B: out[T, H] = h @ Wd (+ the cross-rank sum over NVLink)
-// Reference semantics as in ffn.cu (src/ffn/builder.py:37-45, root_node.py:956-995).
-//
-// Every CTA first works through its share of the phase-A units, then its share of the
-// phase-B units, through one shared-memory ring. The producer streams phase-B weights as
-// soon as ring slots free up — during the phase-A tail — and only the activation slice of
-// a phase-B unit (rows k0..k0+31 of h) waits for the gate/up slab k0/256 that produces
-// them: the CTA finishing a slab publishes a per-slab ready flag tagged with the call's
-// epoch. Phase A never waits on anything, every CTA is co-resident, so every wait ends.
-#include "ffn_internal.cuh"
+// Host side of the decode-path streaming kernel (ffn_stream.cuh) and the one-launch decode
+// FFN entry point. Reference semantics: src/ffn/builder.py:37-45 and
+// src/orchestrator/root_node.py:956-995.
+#include "ffn_stream.cuh"
 
 namespace pyre {
 namespace ffn {
 
-struct alignas(64) DecodeParams {
-  CUtensorMap tx;            // x [T, H], box T x R_A
-  CUtensorMap th;            // h [T, W] f32, box T x R_B
-  const uint8_t* wgu;        // packed gate/up pair (or up alone when ungated)
-  const uint8_t* wd;         // packed down
-  int H, W, T;
-  int tilesA, uptA;          // phase A: slabs of W, units of H
-  int tilesB, uptB;          // phase B: slabs of H, units of W
-  int64_t UA, UB;
-  int pmaxA, pmaxB;
-  float* h;                  // [T, W]
-  float* out;                // [T, H]
-  float* wsA;
-  float* wsB;
-  unsigned int* cntA;
-  unsigned int* cntB;
-  uint32_t* ready;           // [tilesA]
-  uint32_t* ws_epoch;
-  unsigned int* ws_done;
-  int* status;
-  comm::DevComm comm;
-};
-
-template <int T, int NA, typename XT, typename ST>
-struct DecodeCfg {
-  using LA = StageLayout<T, NA, XT, ST>;
-  using LB = StageLayout<T, 1, float, ST>;
-  static constexpr int kStageBytes = LA::kBytes > LB::kBytes ? LA::kBytes : LB::kBytes;
-  static constexpr int kCtasPerSm = (T <= 2) ? 2 : 1;
-  static constexpr int kStages = (T <= 2) ? 4 : 5;
-  static constexpr int kRedFloats = kConsumerWarps * NA * T * kTileN;
-  static constexpr int kFinFloats = NA * T * kTileN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + (kRedFloats + kFinFloats) * 4 + 2 * kStages * 8 + 16;
-};
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// Bounded wait for a per-slab ready flag (2 s); records PYRE_ETIMEOUT on expiry.
-__device__ __forceinline__ void wait_ready(const uint32_t* flag, uint32_t epoch, int* status) {
-  if (ld_acquire_gpu(flag) == epoch) return;
-  const uint64_t t0 = globaltimer_ns();
-  while (ld_acquire_gpu(flag) != epoch) {
-    if (globaltimer_ns() - t0 > 2000000000ull) {
-      atomicExch(status, PYRE_ETIMEOUT);
-      return;
-    }
-    __nanosleep(20);
-  }
-}
-
-template <int T, int NA, typename XT, typename ST, bool TP>
-__global__ void __launch_bounds__(kThreads, (DecodeCfg<T, NA, XT, ST>::kCtasPerSm))
-q80_ffn_decode_kernel(const __grid_constant__ DecodeParams p) {
-  using C = DecodeCfg<T, NA, XT, ST>;
-  using LA = typename C::LA;
-  using LB = typename C::LB;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* stages = smem;
-  float* red = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
-  float* fin = red + C::kRedFloats;
-  uint64_t* full = reinterpret_cast<uint64_t*>(fin + C::kFinFloats);
-  uint64_t* empty = full + C::kStages;
-  int* s_last = reinterpret_cast<int*>(empty + C::kStages);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int c = blockIdx.x;
-  const int64_t a0 = (static_cast<int64_t>(c) * p.UA) / G, a1 = (static_cast<int64_t>(c + 1) * p.UA) / G;
-  const int64_t b0 = (static_cast<int64_t>(c) * p.UB) / G, b1 = (static_cast<int64_t>(c + 1) * p.UB) / G;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < C::kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  // epoch of this call (tags the per-slab ready flags); published by the last CTA to exit
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
-  uint32_t cepoch = 0;
-  if constexpr (TP) cepoch = comm::epoch_begin(p.comm);
-
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      prefetch_tmap(&p.tx);
-      prefetch_tmap(&p.th);
-      int s = 0;
-      uint32_t ph = 0;
-      for (int64_t u = a0; u < a1; ++u) {
-        const int tile = static_cast<int>(u / p.uptA);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptA) * LA::kRows;
-        mbar_wait(&empty[s], ph ^ 1u, p.status);
-        uint8_t* st = stages + s * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[s], LA::kTxBytes);
-        bulk_load(st, p.wgu + u * LA::kWBytes, LA::kWBytes, &full[s]);
-        tma_load_2d(st + LA::kXOff, &p.tx, k0, 0, &full[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-      for (int64_t u = b0; u < b1; ++u) {
-        const int tile = static_cast<int>(u / p.uptB);
-        const int k0 = static_cast<int>(u - static_cast<int64_t>(tile) * p.uptB) * LB::kRows;
-        mbar_wait(&empty[s], ph ^ 1u, p.status);
-        uint8_t* st = stages + s * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
-        bulk_load(st, p.wd + u * LB::kWBytes, LB::kWBytes, &full[s]);
-        // rows k0..k0+R_B-1 of h come from gate/up slab k0 / 256 (R_B divides 256)
-        wait_ready(p.ready + k0 / kTileN, epoch, p.status);
-        fence_proxy_async_global();
-        tma_load_2d(st + LB::kXOff, &p.th, k0, 0, &full[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-    }
-  } else {
-    // ---------------- consumers ----------------
-    const int tid = threadIdx.x;
-    const int rs = lane >> 4;
-    const int cc = lane & 15;
-    int s = 0;
-    uint32_t ph = 0;
-    // phase A: gate/up + SiLU·mul into h
-    int64_t u = a0;
-    while (u < a1) {
-      const int tile = static_cast<int>(u / p.uptA);
-      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.uptA;
-      const int64_t seg_end = min(a1, tile_u0 + p.uptA);
-      float2 acc[NA][T][8];
-      zero_acc<NA, T>(acc);
-      for (; u < seg_end; ++u) {
-        mbar_wait(&full[s], ph, p.status);
-        consume_unit<T, NA, XT, ST>(stages + s * C::kStageBytes, acc, warp, rs, cc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-      reduce_tile<T, NA>(acc, red, fin, warp, rs, cc, tid);
-      const int cf = cta_of_unit(tile_u0, p.UA, G);
-      const int cl = cta_of_unit(tile_u0 + p.uptA - 1, p.UA, G);
-      if (fixup_tile<T, NA>(fin, p.wsA, p.cntA, p.pmaxA, tile, c, cf, cl, s_last, tid)) {
-        for (int i = tid; i < T * kTileN; i += kConsumers) {
-          const int t = i / kTileN, col = tile * kTileN + (i % kTileN);
-          if (col >= p.W) continue;
-          const float v = (NA == 2) ? silu_f32(fin[i]) * fin[T * kTileN + i] : silu_f32(fin[i]);
-          p.h[static_cast<int64_t>(t) * p.W + col] = v;
-        }
-        __threadfence();
-        fence_proxy_async_global();
-        consumer_sync();
-        if (tid == 0) st_release_gpu(p.ready + tile, epoch);
-      }
-      consumer_sync();
-    }
-    // phase B: down projection (+ cross-rank sum)
-    u = b0;
-    while (u < b1) {
-      const int tile = static_cast<int>(u / p.uptB);
-      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.uptB;
-      const int64_t seg_end = min(b1, tile_u0 + p.uptB);
-      float2 acc[1][T][8];
-      zero_acc<1, T>(acc);
-      for (; u < seg_end; ++u) {
-        mbar_wait(&full[s], ph, p.status);
-        consume_unit<T, 1, float, ST>(stages + s * C::kStageBytes, acc, warp, rs, cc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == C::kStages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-      reduce_tile<T, 1>(acc, red, fin, warp, rs, cc, tid);
-      const int cf = cta_of_unit(tile_u0, p.UB, G);
-      const int cl = cta_of_unit(tile_u0 + p.uptB - 1, p.UB, G);
-      if (fixup_tile<T, 1>(fin, p.wsB, p.cntB, p.pmaxB, tile, c, cf, cl, s_last, tid)) {
-        if constexpr (TP) {
-          tp_reduce_tile<T>(p.comm, cepoch, tile, fin, p.out, p.H, tid);
-        } else {
-          for (int i = tid; i < T * kTileN; i += kConsumers) {
-            const int t = i / kTileN, col = tile * kTileN + (i % kTileN);
-            if (col < p.H) p.out[static_cast<int64_t>(t) * p.H + col] = fin[i];
-          }
-        }
-      }
-      consumer_sync();
-    }
-  }
-  __syncthreads();
-  if constexpr (TP) comm::epoch_end(p.comm, cepoch);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(p.ws_done, 1u);
-    if (prev == gridDim.x - 1) {
-      *reinterpret_cast<volatile unsigned int*>(p.ws_done) = 0u;
-      __threadfence();
-      *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) = epoch;
-    }
-  }
-}
-
 inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
 
-// Workspace of the one-launch decode: header | h [T, W] f32 | pieces A | pieces B.
-int64_t decode_ws_bytes(int T, int H, int W, int na) {
-  return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + align256(pieces_bytes(T, W, na)) +
-         align256(pieces_bytes(T, H, 1));
+int64_t stream_pieces_bytes(int T, int N, int K, int nmat) {
+  const int R = nmat == 2 ? kUnitRowsPair : kUnitRowsSingle;
+  const int64_t tiles = tiles_of(N);
+  const int64_t upt = (K + R - 1) / R;
+  const int64_t cpt = (upt + kChunk - 1) / kChunk;
+  return align256(tiles * cpt * nmat * T * kTileN * 4);
 }
 
-template <int T, int NA, typename XT, typename ST, bool TP>
-int launch_decode(DecodeParams p, const void* x, int64_t ws_cap, cudaStream_t s) {
-  using C = DecodeCfg<T, NA, XT, ST>;
-  auto kern = q80_ffn_decode_kernel<T, NA, XT, ST, TP>;
+// Workspace layouts (after the kHeaderBytes header):
+//   MODE_A / MODE_B : pieces of that phase
+//   MODE_AB         : h [T, W] f32 | pieces A | pieces B
+int64_t decode_ws_bytes(int T, int H, int W, int na) {
+  return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + stream_pieces_bytes(T, W, H, na) +
+         stream_pieces_bytes(T, H, W, 1);
+}
+
+struct StreamArgs {
+  int mode;
+  bool tp;
+  const void* xa;      // phase-A activation [T, KA]
+  int xa_dtype;
+  const void* xb;      // phase-B activation [T, KB] (MODE_B); MODE_AB uses h in the workspace
+  int xb_dtype;
+};
+
+template <int T, int NA, typename XA, typename XB, typename ST, int MODE, bool TP>
+int launch_stream(StreamParams p, const StreamArgs& a, cudaStream_t s) {
+  using C = StreamCfg<T, NA, XA, XB, ST>;
+  auto kern = q80_ffn_stream_kernel<T, NA, XA, XB, ST, MODE, TP>;
   int rc = set_smem_once(kern, C::kSmemBytes);
   if (rc) return rc;
-  rc = make_tmap_2d(&p.tx, x, tma_dtype<XT>(), sizeof(XT), T, p.H, static_cast<uint64_t>(p.H) * sizeof(XT), T,
-                    C::LA::kRows);
-  if (rc) return rc;
-  rc = make_tmap_2d(&p.th, p.h, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, T, p.W, static_cast<uint64_t>(p.W) * 4, T,
-                    C::LB::kRows);
-  if (rc) return rc;
-  int G = 1;
-  rc = coresident_grid(kern, kThreads, C::kSmemBytes, C::kCtasPerSm, p.UA < p.UB ? p.UA : p.UB, &G);
-  if (rc) return rc;
-  p.pmaxA = pmax_for(p.tilesA, p.uptA, G);
-  p.pmaxB = pmax_for(p.tilesB, p.uptB, G);
-  const int64_t needA = align256(static_cast<int64_t>(p.tilesA) * p.pmaxA * NA * T * kTileN * 4);
-  const int64_t needB = align256(static_cast<int64_t>(p.tilesB) * p.pmaxB * T * kTileN * 4);
-  if (needA + needB > ws_cap) return set_error(PYRE_ENOMEM, "pyre_ffn_decode_q80: workspace too small for this grid");
-  p.wsB = reinterpret_cast<float*>(reinterpret_cast<char*>(p.wsA) + needA);
-  kern<<<G, kThreads, C::kSmemBytes, s>>>(p);
-  PYRE_LAUNCH_CHECK("q80_ffn_decode_kernel");
+  if constexpr ((MODE & MODE_A) != 0) {
+    rc = make_tmap_2d(&p.txa, a.xa, tma_dtype<XA>(), sizeof(XA), T, p.KA, static_cast<uint64_t>(p.KA) * sizeof(XA), T,
+                      C::LA::kRows);
+    if (rc) return rc;
+  }
+  if constexpr ((MODE & MODE_B) != 0) {
+    const void* xb = MODE == MODE_AB ? p.outA : a.xb;
+    rc = make_tmap_2d(&p.txb, xb, tma_dtype<XB>(), sizeof(XB), T, p.KB, static_cast<uint64_t>(p.KB) * sizeof(XB), T,
+                      C::LB::kRows);
+    if (rc) return rc;
+  }
+  int occ = 0;
+  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, C::kSmemBytes));
+  if (occ < 1) return set_error(PYRE_ECUDA, "q80_ffn_stream_kernel does not fit on an SM");
+  if (occ > C::kCtasPerSm) occ = C::kCtasPerSm;
+  int64_t g = static_cast<int64_t>(occ) * sm_count();   // co-resident (tensor-parallel waits)
+  const int64_t chunks = static_cast<int64_t>(p.ncA) + p.ncB;
+  if (g > chunks) g = chunks;
+  if (g < 1) g = 1;
+  kern<<<static_cast<int>(g), kThreads, C::kSmemBytes, s>>>(p);
+  PYRE_LAUNCH_CHECK("q80_ffn_stream_kernel");
   return PYRE_OK;
 }
 
-template <int T, int NA, typename XT, typename ST>
-int decode_tp(DecodeParams p, const void* x, int64_t cap, bool tp, cudaStream_t s) {
-  return tp ? launch_decode<T, NA, XT, ST, true>(p, x, cap, s) : launch_decode<T, NA, XT, ST, false>(p, x, cap, s);
+template <int T, int NA, typename XA, typename XB, typename ST>
+int stream_mode(StreamParams p, const StreamArgs& a, cudaStream_t s) {
+  switch (a.mode) {
+    case MODE_A: return launch_stream<T, NA, XA, XB, ST, MODE_A, false>(p, a, s);
+    case MODE_B:
+      return a.tp ? launch_stream<T, NA, XA, XB, ST, MODE_B, true>(p, a, s)
+                  : launch_stream<T, NA, XA, XB, ST, MODE_B, false>(p, a, s);
+    default:
+      return a.tp ? launch_stream<T, NA, XA, XB, ST, MODE_AB, true>(p, a, s)
+                  : launch_stream<T, NA, XA, XB, ST, MODE_AB, false>(p, a, s);
+  }
 }
 
+// Type dispatch. MODE_A: XA = x dtype; MODE_B: XB = x dtype (NA unused, 1);
+// MODE_AB: XA = x dtype, XB = f32 (h).
 template <int T, int NA>
-int decode_types(DecodeParams p, const void* x, int x_dtype, int scale_dtype, int64_t cap, bool tp, cudaStream_t s) {
-  if (x_dtype == PYRE_BF16) {
-    if (scale_dtype == PYRE_F16) return decode_tp<T, NA, __nv_bfloat16, __half>(p, x, cap, tp, s);
-    return decode_tp<T, NA, __nv_bfloat16, float>(p, x, cap, tp, s);
+int stream_types(StreamParams p, const StreamArgs& a, int scale_dtype, cudaStream_t s) {
+  const bool f16s = scale_dtype == PYRE_F16;
+  if (a.mode == MODE_B) {
+    if (a.xb_dtype == PYRE_BF16)
+      return f16s ? stream_mode<T, 1, float, __nv_bfloat16, __half>(p, a, s)
+                  : stream_mode<T, 1, float, __nv_bfloat16, float>(p, a, s);
+    return f16s ? stream_mode<T, 1, float, float, __half>(p, a, s) : stream_mode<T, 1, float, float, float>(p, a, s);
   }
-  if (scale_dtype == PYRE_F16) return decode_tp<T, NA, float, __half>(p, x, cap, tp, s);
-  return decode_tp<T, NA, float, float>(p, x, cap, tp, s);
+  if (a.xa_dtype == PYRE_BF16)
+    return f16s ? stream_mode<T, NA, __nv_bfloat16, float, __half>(p, a, s)
+                : stream_mode<T, NA, __nv_bfloat16, float, float>(p, a, s);
+  return f16s ? stream_mode<T, NA, float, float, __half>(p, a, s) : stream_mode<T, NA, float, float, float>(p, a, s);
 }
 
 template <int NA>
-int decode_T(DecodeParams p, const void* x, int x_dtype, int scale_dtype, int64_t cap, bool tp, cudaStream_t s) {
+int stream_T(StreamParams p, const StreamArgs& a, int scale_dtype, cudaStream_t s) {
   switch (p.T) {
-    case 1: return decode_types<1, NA>(p, x, x_dtype, scale_dtype, cap, tp, s);
-    case 2: return decode_types<2, NA>(p, x, x_dtype, scale_dtype, cap, tp, s);
-    case 3: return decode_types<3, NA>(p, x, x_dtype, scale_dtype, cap, tp, s);
-    case 4: return decode_types<4, NA>(p, x, x_dtype, scale_dtype, cap, tp, s);
-    default: return set_error(PYRE_EINVAL, "pyre_ffn_decode_q80: T must be in [1, 4]");
+    case 1: return stream_types<1, NA>(p, a, scale_dtype, s);
+    case 2: return stream_types<2, NA>(p, a, scale_dtype, s);
+    case 3: return stream_types<3, NA>(p, a, scale_dtype, s);
+    case 4: return stream_types<4, NA>(p, a, scale_dtype, s);
+    default: return set_error(PYRE_EINVAL, "streaming FFN kernel: T must be in [1, 4]");
   }
 }
 
-// Two-call workspace need (ffn.cu): header + the larger of the two piece regions.
-int64_t twocall_ws_bytes(int T, int H, int W) {
-  if (T > PYRE_FUSED_REDUCE_MAX_T) return kHeaderBytes;
-  const int64_t a = pieces_bytes(T, W, 2), b = pieces_bytes(T, H, 1);
-  return kHeaderBytes + (a > b ? a : b);
+void fill_phase(StreamParams& p, bool phase_b, int K, int N, int nmat) {
+  const int R = nmat == 2 ? kUnitRowsPair : kUnitRowsSingle;
+  const int tiles = tiles_of(N), upt = (K + R - 1) / R, cpt = (upt + kChunk - 1) / kChunk;
+  if (!phase_b) {
+    p.KA = K; p.NA = N; p.tilesA = tiles; p.uptA = upt; p.cptA = cpt; p.ncA = tiles * cpt;
+  } else {
+    p.KB = K; p.NB = N; p.tilesB = tiles; p.uptB = upt; p.cptB = cpt; p.ncB = tiles * cpt;
+  }
+}
+
+void fill_header(StreamParams& p, char* wsc) {
+  p.cntA = reinterpret_cast<unsigned int*>(wsc + kHdrCntA);
+  p.cntB = reinterpret_cast<unsigned int*>(wsc + kHdrCntB);
+  p.ready = reinterpret_cast<uint32_t*>(wsc + kHdrReady);
+  p.next = reinterpret_cast<unsigned int*>(wsc + kHdrNext);
+  p.ws_epoch = reinterpret_cast<uint32_t*>(wsc + kHdrEpoch);
+  p.ws_done = reinterpret_cast<unsigned int*>(wsc + kHdrDone);
+  p.status = reinterpret_cast<int*>(wsc + kHdrStatus);
 }
 
 }  // namespace ffn
+
+// Streaming-kernel forms of the two-call entry points (T <= 4), used by ffn.cu.
+int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, int scale_dtype, int W,
+                      void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s) {
+  using namespace ffn;
+  const int na = gated ? 2 : 1;
+  if (ws_bytes < kHeaderBytes + stream_pieces_bytes(T, W, H, na))
+    return set_error(PYRE_ENOMEM, "pyre_ffn_gateup_silu_q80: workspace smaller than pyre_ffn_workspace_bytes()");
+  char* wsc = static_cast<char*>(workspace);
+  StreamParams p{};
+  p.T = T;
+  p.wa = static_cast<const uint8_t*>(wgu);
+  fill_phase(p, false, H, W, na);
+  p.outA = h;
+  p.outA_bf16 = h_dtype == PYRE_BF16;
+  p.wsA = reinterpret_cast<float*>(wsc + kHeaderBytes);
+  fill_header(p, wsc);
+  StreamArgs a{MODE_A, false, x, x_dtype, nullptr, PYRE_F32};
+  return gated ? stream_T<2>(p, a, scale_dtype, s) : stream_T<1>(p, a, scale_dtype, s);
+}
+
+int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,
+                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s) {
+  using namespace ffn;
+  if (ws_bytes < kHeaderBytes + stream_pieces_bytes(T, H, W, 1))
+    return set_error(PYRE_ENOMEM, "pyre_ffn_down_q80: workspace smaller than pyre_ffn_workspace_bytes()");
+  const bool tp = comm != nullptr && comm->world > 1;
+  PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, "pyre_ffn_down_q80: H too large for the fused reduce");
+  char* wsc = static_cast<char*>(workspace);
+  StreamParams p{};
+  p.T = T;
+  p.wb = static_cast<const uint8_t*>(wd);
+  fill_phase(p, true, W, H, 1);
+  p.outB = out;
+  p.wsB = reinterpret_cast<float*>(wsc + kHeaderBytes);
+  fill_header(p, wsc);
+  if (tp) p.comm = comm::device_view(comm);
+  StreamArgs a{MODE_B, tp, nullptr, PYRE_F32, h, h_dtype};
+  return stream_T<1>(p, a, scale_dtype, s);
+}
+
 }  // namespace pyre
 
 using namespace pyre;
@@ -310,10 +174,9 @@ using namespace pyre::ffn;
 extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   PYRE_CHECK_ARG(bytes != nullptr, "pyre_ffn_workspace_bytes: null bytes");
   PYRE_CHECK_ARG(T >= 1 && H >= 1 && W >= 1, "pyre_ffn_workspace_bytes: sizes must be positive");
-  int64_t need = twocall_ws_bytes(T, H, W);
+  int64_t need = kHeaderBytes;
   if (T <= PYRE_FUSED_REDUCE_MAX_T) {
-    const int64_t d = decode_ws_bytes(T, H, W, 2);
-    if (d > need) need = d;
+    need = decode_ws_bytes(T, H, W, 2);   // covers the two-call forms too
   }
   *bytes = need;
   return PYRE_OK;
@@ -329,42 +192,32 @@ extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, con
   PYRE_CHECK_ARG(wgu != nullptr && wd != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(wd) % 16 == 0,
                  "pyre_ffn_decode_q80: packed weights must be non-null and 16-byte aligned");
-  PYRE_CHECK_ARG(gemv::tiles_of(H) <= gemv::kMaxTiles && gemv::tiles_of(W) <= gemv::kMaxTiles,
-                 "pyre_ffn_decode_q80: dims too large");
+  PYRE_CHECK_ARG(tiles_of(H) <= kMaxTiles && tiles_of(W) <= kMaxTiles, "pyre_ffn_decode_q80: dims too large");
+  const bool tp = comm != nullptr && comm->world > 1;
   if (comm != nullptr) {
     PYRE_CHECK_ARG(comm->hidden == H, "pyre_ffn_decode_q80: communicator hidden size differs from H");
     PYRE_CHECK_ARG(T <= comm->max_tokens, "pyre_ffn_decode_q80: T exceeds the communicator's max_tokens");
+    PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, "pyre_ffn_decode_q80: H too large for the fused reduce");
   }
-  const int64_t need = decode_ws_bytes(T, H, W, gated ? 2 : 1);
+  const int na = gated ? 2 : 1;
+  const int64_t need = decode_ws_bytes(T, H, W, na);
   if (ws_bytes < need)
     return set_error(PYRE_ENOMEM, "pyre_ffn_decode_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   char* wsc = static_cast<char*>(workspace);
-  DecodeParams p{};
-  p.wgu = static_cast<const uint8_t*>(wgu);
-  p.wd = static_cast<const uint8_t*>(wd);
-  p.H = H;
-  p.W = W;
+  StreamParams p{};
   p.T = T;
-  const int ra = gated ? kUnitRowsPair : kUnitRowsSingle;
-  p.tilesA = tiles_of(W);
-  p.uptA = (H + ra - 1) / ra;
-  p.tilesB = tiles_of(H);
-  p.uptB = (W + kUnitRowsSingle - 1) / kUnitRowsSingle;
-  p.UA = static_cast<int64_t>(p.tilesA) * p.uptA;
-  p.UB = static_cast<int64_t>(p.tilesB) * p.uptB;
-  p.h = reinterpret_cast<float*>(wsc + kHeaderBytes);
-  p.out = out;
+  p.wa = static_cast<const uint8_t*>(wgu);
+  p.wb = static_cast<const uint8_t*>(wd);
+  fill_phase(p, false, H, W, na);
+  fill_phase(p, true, W, H, 1);
+  p.outA = wsc + kHeaderBytes;   // h [T, W] f32
+  p.outA_bf16 = 0;
+  p.outB = out;
   p.wsA = reinterpret_cast<float*>(wsc + kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4));
-  p.wsB = nullptr;
-  p.cntA = reinterpret_cast<unsigned int*>(wsc + kHdrCntA);
-  p.cntB = reinterpret_cast<unsigned int*>(wsc + kHdrCntB);
-  p.ready = reinterpret_cast<uint32_t*>(wsc + kHdrReady);
-  p.ws_epoch = reinterpret_cast<uint32_t*>(wsc + kHdrEpoch);
-  p.ws_done = reinterpret_cast<unsigned int*>(wsc + kHdrDone);
-  p.status = reinterpret_cast<int*>(wsc + kHdrStatus);
-  const bool tp = comm != nullptr && comm->world > 1;
+  p.wsB = reinterpret_cast<float*>(reinterpret_cast<char*>(p.wsA) + stream_pieces_bytes(T, W, H, na));
+  fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);
-  const int64_t cap = ws_bytes - (kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4));
+  StreamArgs a{MODE_AB, tp, x, x_dtype, nullptr, PYRE_F32};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return gated ? decode_T<2>(p, x, x_dtype, scale_dtype, cap, tp, s) : decode_T<1>(p, x, x_dtype, scale_dtype, cap, tp, s);
+  return gated ? stream_T<2>(p, a, scale_dtype, s) : stream_T<1>(p, a, scale_dtype, s);
 }

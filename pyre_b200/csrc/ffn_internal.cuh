@@ -68,6 +68,44 @@ __device__ void tp_reduce_tile(const comm::DevComm& c, uint32_t epoch, int tile,
   }
 }
 
+// Split form of tp_reduce_tile for kernels that schedule work dynamically (the chunk to CTA
+// map differs between ranks, so a CTA must never block on a peer while it still holds
+// unprocessed work): tp_push_tile() pushes and flags without waiting; tp_finish_tile()
+// waits for every peer's flag of the tile and sums, called after all work is drained.
+template <int T>
+__device__ void tp_push_tile(const comm::DevComm& c, uint32_t epoch, int tile, const float* fin, int tid) {
+  const int slot = epoch & 1u;
+  const int n = T * kTileN;
+  for (int peer = 0; peer < c.world; ++peer) {
+    float* dst = comm::fused_slot(c, peer, slot, c.rank) + static_cast<int64_t>(tile) * n;
+    for (int i = tid; i < n; i += kConsumers) dst[i] = fin[i];
+  }
+  __threadfence_system();
+  consumer_sync();
+  if (tid < c.world) st_release_sys(comm::fused_flag(c, tid, slot, c.rank, tile), epoch);
+}
+
+template <int T>
+__device__ void tp_finish_tile(const comm::DevComm& c, uint32_t epoch, int tile, float* out, int N, int tid) {
+  const int slot = epoch & 1u;
+  const int n = T * kTileN;
+  if (tid < c.world) {
+    if (!wait_flag_eq(comm::fused_flag(c, c.rank, slot, tid, tile), epoch, c.timeout_ns))
+      atomicExch(c.status, PYRE_ETIMEOUT);
+  }
+  consumer_sync();
+  for (int i = tid; i < n; i += kConsumers) {
+    const int t = i / kTileN, cc = i % kTileN;
+    const int col = tile * kTileN + cc;
+    if (col >= N) continue;
+    float acc = 0.f;
+    for (int src = 0; src < c.world; ++src)
+      acc += __ldcg(comm::fused_slot(c, c.rank, slot, src) + static_cast<int64_t>(tile) * n + i);
+    out[static_cast<int64_t>(t) * N + col] = acc;
+  }
+  consumer_sync();
+}
+
 template <typename K>
 int set_smem_once(K kern, int bytes) {
   return set_smem_limit(reinterpret_cast<const void*>(kern), bytes);
@@ -94,5 +132,10 @@ int coresident_grid(K kern, int threads, int smem, int want_per_sm, int64_t unit
 // Argument checks shared by the FFN entry points (defined in ffn.cu).
 int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
                      const void* ws, int64_t ws_bytes, const char* fn);
+// Streaming-kernel forms of the two-call entry points for T <= 4 (defined in ffn_decode.cu).
+int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, int scale_dtype, int W,
+                      void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s);
+int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,
+                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s);
 
 }  // namespace pyre

@@ -45,6 +45,7 @@ constexpr int kMaxTiles = 2048;        // N <= 524288
 constexpr int64_t kHdrEpoch = 0;
 constexpr int64_t kHdrDone = 4;
 constexpr int64_t kHdrStatus = 8;
+constexpr int64_t kHdrNext = 16;       // two u32 chunk counters (dynamic scheduling)
 constexpr int64_t kHdrCntA = 1024;
 constexpr int64_t kHdrCntB = kHdrCntA + kMaxTiles * 4;
 constexpr int64_t kHdrReady = kHdrCntB + kMaxTiles * 4;

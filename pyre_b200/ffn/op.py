@@ -91,6 +91,11 @@ class FfnShardOp:
         wait ran out); read after synchronising the stream."""
         return int(self.workspace[8:12].view(torch.int32).item())
 
+    def reset(self) -> None:
+        """Zero the scratch (status, counters, flags). Needed after a call that reported
+        PYRE_ETIMEOUT: the kernels stop early then and leave their counters part-way."""
+        self.workspace.zero_()
+
     def h_dtype(self, tokens: int) -> torch.dtype:
         # decode keeps the intermediate in f32; larger T stores bf16 (tensor-core operand)
         return torch.float32 if tokens <= N.PYRE_FUSED_REDUCE_MAX_T else torch.bfloat16
