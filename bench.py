@@ -358,7 +358,7 @@ def run_ours(args):
                        "weight_sets": n_sets, "l2": f"inputs larger than L2: {n_sets} rotating weight sets per rank",
                        "parallelism": f"tp{world}", "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
             "roofline": {"bound": "hbm",
-                         "kernel": "q80_ffn_decode_kernel (gate/up + SiLU\u00b7mul + down [+ NVLink reduce], one launch), rank 0 shard",
+                         "kernel": "q80_ffn_stream_kernel (gate/up + SiLU\u00b7mul + down [+ NVLink reduce], one launch, chunk-scheduled), rank 0 shard",
                          "achieved": round(k_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
                          "peak_kind": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": int(k_bytes), "avg_launch_us": round(k_avg * 1e3, 3),

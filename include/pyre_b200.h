@@ -45,6 +45,7 @@ extern "C" {
 #define PYRE_ECUDA     2  /* a CUDA runtime/driver call failed                          */
 #define PYRE_ETIMEOUT  3  /* a bounded device-side wait on a peer ran out               */
 #define PYRE_ENOMEM    4  /* caller-supplied workspace too small / allocation failed    */
+#define PYRE_ERANGE    5  /* device status: an FFN partial sum was not finite or >= 2^30 */
 
 /* ---- element types ----------------------------------------------------------------- */
 #define PYRE_F32   0

@@ -15,6 +15,7 @@ PYRE_EINVAL = 1
 PYRE_ECUDA = 2
 PYRE_ETIMEOUT = 3
 PYRE_ENOMEM = 4
+PYRE_ERANGE = 5
 
 PYRE_F32 = 0
 PYRE_BF16 = 1

@@ -8,20 +8,17 @@ namespace ffn {
 
 inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
 
-int64_t stream_pieces_bytes(int T, int N, int K, int nmat) {
-  const int R = nmat == 2 ? kUnitRowsPair : kUnitRowsSingle;
-  const int64_t tiles = tiles_of(N);
-  const int64_t upt = (K + R - 1) / R;
-  const int64_t cpt = (upt + kChunk - 1) / kChunk;
-  return align256(tiles * cpt * nmat * T * kTileN * 4);
+// Fixed-point slab accumulators of one phase: [tiles(N), nmat, T, 256] int64.
+int64_t stream_acc_bytes(int T, int N, int nmat) {
+  return align256(static_cast<int64_t>(tiles_of(N)) * nmat * T * kTileN * 8);
 }
 
 // Workspace layouts (after the kHeaderBytes header):
-//   MODE_A / MODE_B : pieces of that phase
-//   MODE_AB         : h [T, W] f32 | pieces A | pieces B
+//   MODE_A / MODE_B : accumulators of that phase
+//   MODE_AB         : h [T, W] f32 | accumulators A | accumulators B
 int64_t decode_ws_bytes(int T, int H, int W, int na) {
-  return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + stream_pieces_bytes(T, W, H, na) +
-         stream_pieces_bytes(T, H, W, 1);
+  return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + stream_acc_bytes(T, W, na) +
+         stream_acc_bytes(T, H, 1);
 }
 
 struct StreamArgs {
@@ -51,14 +48,23 @@ int launch_stream(StreamParams p, const StreamArgs& a, cudaStream_t s) {
     if (rc) return rc;
   }
   int occ = 0;
-  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, C::kSmemBytes));
+  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kStreamThreads, C::kSmemBytes));
   if (occ < 1) return set_error(PYRE_ECUDA, "q80_ffn_stream_kernel does not fit on an SM");
   if (occ > C::kCtasPerSm) occ = C::kCtasPerSm;
   int64_t g = static_cast<int64_t>(occ) * sm_count();   // co-resident (tensor-parallel waits)
   const int64_t chunks = static_cast<int64_t>(p.ncA) + p.ncB;
   if (g > chunks) g = chunks;
   if (g < 1) g = 1;
-  kern<<<static_cast<int>(g), kThreads, C::kSmemBytes, s>>>(p);
+  if constexpr (MODE == MODE_AB) {
+    // Lead of phase A over phase B in the queue, in groups. A phase-A slab becomes usable
+    // several microseconds after its last chunk is streamed (count, read-back, release under
+    // full HBM load), so a phase-B chunk queued a round or two after its rows blocks its
+    // producer; measured on the 7B decode shape, queueing all of phase A first is faster.
+    static_assert((kChunk * C::LB::kRows) % kTileN == 0, "a phase-B chunk must cover whole phase-A slabs");
+    p.spg = kChunk * C::LB::kRows / kTileN;
+    p.slack = p.cptB;
+  }
+  kern<<<static_cast<int>(g), kStreamThreads, C::kSmemBytes, s>>>(p);
   PYRE_LAUNCH_CHECK("q80_ffn_stream_kernel");
   return PYRE_OK;
 }
@@ -131,7 +137,7 @@ int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu,
                       void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s) {
   using namespace ffn;
   const int na = gated ? 2 : 1;
-  if (ws_bytes < kHeaderBytes + stream_pieces_bytes(T, W, H, na))
+  if (ws_bytes < kHeaderBytes + stream_acc_bytes(T, W, na))
     return set_error(PYRE_ENOMEM, "pyre_ffn_gateup_silu_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   char* wsc = static_cast<char*>(workspace);
   StreamParams p{};
@@ -140,7 +146,7 @@ int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu,
   fill_phase(p, false, H, W, na);
   p.outA = h;
   p.outA_bf16 = h_dtype == PYRE_BF16;
-  p.wsA = reinterpret_cast<float*>(wsc + kHeaderBytes);
+  p.accA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
   fill_header(p, wsc);
   StreamArgs a{MODE_A, false, x, x_dtype, nullptr, PYRE_F32};
   return gated ? stream_T<2>(p, a, scale_dtype, s) : stream_T<1>(p, a, scale_dtype, s);
@@ -149,7 +155,7 @@ int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu,
 int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,
                     void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s) {
   using namespace ffn;
-  if (ws_bytes < kHeaderBytes + stream_pieces_bytes(T, H, W, 1))
+  if (ws_bytes < kHeaderBytes + stream_acc_bytes(T, H, 1))
     return set_error(PYRE_ENOMEM, "pyre_ffn_down_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   const bool tp = comm != nullptr && comm->world > 1;
   PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, "pyre_ffn_down_q80: H too large for the fused reduce");
@@ -159,7 +165,7 @@ int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, in
   p.wb = static_cast<const uint8_t*>(wd);
   fill_phase(p, true, W, H, 1);
   p.outB = out;
-  p.wsB = reinterpret_cast<float*>(wsc + kHeaderBytes);
+  p.accB = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
   fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);
   StreamArgs a{MODE_B, tp, nullptr, PYRE_F32, h, h_dtype};
@@ -213,8 +219,8 @@ extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, con
   p.outA = wsc + kHeaderBytes;   // h [T, W] f32
   p.outA_bf16 = 0;
   p.outB = out;
-  p.wsA = reinterpret_cast<float*>(wsc + kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4));
-  p.wsB = reinterpret_cast<float*>(reinterpret_cast<char*>(p.wsA) + stream_pieces_bytes(T, W, H, na));
+  p.accA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4));
+  p.accB = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(p.accA) + stream_acc_bytes(T, W, na));
   fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);
   StreamArgs a{MODE_AB, tp, x, x_dtype, nullptr, PYRE_F32};

@@ -6,15 +6,28 @@
 //
 // Scheduling. A phase's work is its packed weight blocks (one 256-column slab x R rows
 // each, see gemv_common.cuh), grouped per slab into chunks of kChunk consecutive blocks.
-// The producer lane of every CTA takes chunks from a global atomic counter — all phase-A
-// chunks first, then phase-B chunks — so faster SMs simply take more chunks (per-SM memory
-// bandwidth on this part is not uniform). Each chunk's partial sums go to a fixed slot
-// [slab][chunk]; the CTA finishing the last chunk of a slab adds the slots in chunk order
-// (deterministic) and runs the epilogue. In MODE_AB the epilogue of a phase-A slab
-// publishes a ready flag tagged with the call's epoch, and the producer waits for the flag
-// of the slab holding rows k0.. of h before it loads that h slice for a phase-B block.
-// Phase A never waits on phase B, all phase-A chunks are taken before any phase-B chunk,
-// and every wait is bounded, so no wait can last forever.
+// The producer lane of every CTA takes chunks from one global atomic counter, so faster SMs
+// simply take more chunks (per-SM memory bandwidth on this part is not uniform).
+//
+// Slab sums. Each chunk's partial sums are added into the slab's accumulator as 64-bit
+// fixed point (value * 2^32, |value| < 2^30) with integer atomics: integer addition is
+// associative, so the sums are bit-identical whatever CTA ran which chunk and in what
+// order, and the adds are fire-and-forget. The consumers hand each finished chunk to a
+// helper warp, which counts it for its slab (release); the helper that counts a slab's last
+// chunk reads the accumulator back, clears it for the next call and runs the slab epilogue
+// (SiLU-mul and h store, or the output store / cross-rank push) while its consumers stream on.
+//
+// MODE_AB queue. Phase-B chunk column c (chunk c of every output slab) reads rows
+// [c*512, c*512+512) of h, which phase-A slabs [c*spg, c*spg+spg) produce (group c). The
+// queue is: groups 0..slack-1 of phase A, then for each later group g its phase-A chunks
+// followed by phase-B column g-slack, then the last `slack` phase-B columns. Phase B thus
+// runs alongside phase A instead of after it, each phase-B column comes about `slack`
+// groups after the rows it reads, and the tail is short chunks of both phases. The epilogue
+// of a phase-A slab publishes a ready flag tagged with the call's epoch; the producer waits
+// for the flag of the slab holding rows k0.. of h before it loads that h slice.
+// No deadlock: every chunk depends only on phase-A chunks earlier in the queue, chunks are
+// taken in queue order by running CTAs, and a CTA's stages are consumed in order, so the
+// earliest unfinished chunk can always proceed. Every wait is bounded besides.
 #pragma once
 
 #include "ffn_internal.cuh"
@@ -36,15 +49,16 @@ struct alignas(64) StreamParams {
   int KA, NA, tilesA, uptA, cptA;   // phase A: K, N, slabs, blocks per slab, chunks per slab
   int KB, NB, tilesB, uptB, cptB;
   int ncA, ncB;                     // chunks in each phase
+  int spg, slack;                   // MODE_AB queue: phase-A slabs per group, groups of lead
   void* outA;                // [T, NA]: h
   int outA_bf16;
   float* outB;               // [T, NB]
-  float* wsA;                // [tilesA, cptA, NMAT_A * T * 256]
-  float* wsB;                // [tilesB, cptB, T * 256]
+  unsigned long long* accA;  // [tilesA, NMAT_A, T, 256] fixed-point slab sums (zero between calls)
+  unsigned long long* accB;  // [tilesB, T, 256]
   unsigned int* cntA;        // [tilesA] finished chunks
   unsigned int* cntB;
   uint32_t* ready;           // [tilesA] per-slab ready flags (MODE_AB)
-  unsigned int* next;        // [2] chunk counters of phase A and B
+  unsigned int* next;        // queue position counter
   uint32_t* ws_epoch;
   unsigned int* ws_done;
   int* status;
@@ -52,6 +66,13 @@ struct alignas(64) StreamParams {
 };
 
 constexpr int kMaxOwnedTiles = 64;   // tensor-parallel: slabs one CTA may finish (H <= 16384)
+
+// Warp roles: kConsumerWarps consumers, one producer, kHelperWarps helpers.
+constexpr int kHelperWarps = 1;
+constexpr int kHelpers = kHelperWarps * 32;
+constexpr int kStreamThreads = kThreads + kHelpers;
+constexpr int kJobs = 4;             // finished chunks queued from the consumers to the helpers
+static_assert(kHelpers == 32, "the slab read-back maps one helper lane to column pairs");
 
 template <int T, int NA, typename XA, typename XB, typename ST>
 struct StreamCfg {
@@ -61,9 +82,8 @@ struct StreamCfg {
   static constexpr int kCtasPerSm = (T <= 2) ? 2 : 1;
   static constexpr int kStages = (T <= 2) ? 4 : 5;
   static constexpr int kRedFloats = kConsumerWarps * NA * T * kTileN;
-  static constexpr int kFinFloats = NA * T * kTileN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + (kRedFloats + kFinFloats) * 4 + 2 * kStages * 8 +
-                                    kStages * 16 + 16 + (kMaxOwnedTiles + 1) * 4;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kRedFloats * 4 + 2 * kStages * 8 + kStages * 16 +
+                                    2 * kJobs * 8 + kJobs * 16 + 16 + (kMaxOwnedTiles + 1) * 4;
 };
 
 __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
@@ -99,44 +119,124 @@ struct StageMeta {
   int phase, tile, chunk, last;
 };
 
-// Sums the chunk slots of a slab after its last chunk arrived; returns true in the CTA
-// that must run the slab epilogue (the sums are then in fin).
+// A finished chunk handed from the consumers to the helper warps (end = no more chunks).
+struct Job {
+  int phase, tile, chunk, end;
+};
+
+__device__ __forceinline__ void helper_sync() { named_bar(2, kHelpers); }
+
+// Fixed-point slab sums: 2^32 scale; partials are limited to |v| < 2^30, so a slab sum of
+// up to 2^32 partials cannot leave int64 (the quantum, 2^-32, is far below f32 rounding of
+// the values an FFN produces).
+constexpr float kFixScale = 4294967296.0f;            // 2^32
+constexpr float kFixInv = 2.3283064365386963e-10f;    // 2^-32
+constexpr float kFixLimit = 1073741824.0f;            // 2^30
+
+// Sums acc over the two row lanes and all consumer warps (in warp order) and adds the
+// chunk's partial [NMAT][T][kTileN] into the slab accumulator. A partial that is not finite
+// or not below 2^30 in magnitude is added as 0 and flags PYRE_ERANGE.
+// red: kConsumerWarps * NMAT * T * kTileN floats.
 template <int T, int NMAT>
-__device__ __forceinline__ bool chunk_fixup(float* fin, float* ws, unsigned int* cnt, int cpt, int tile, int chunk,
-                                            int* s_last, int tid) {
-  constexpr int kItems = NMAT * T * kTileN;
-  if (cpt == 1) return true;
-  float* slot = ws + (static_cast<int64_t>(tile) * cpt + chunk) * kItems;
-  for (int i = tid; i < kItems; i += kConsumers) __stcg(slot + i, fin[i]);
-  __threadfence();
-  consumer_sync();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(cnt + tile, 1u);
-    *s_last = (prev == static_cast<unsigned>(cpt - 1));
+__device__ __forceinline__ void reduce_to_acc(float2 (&acc)[NMAT][T][8], float* red, unsigned long long* accum,
+                                              int* status, int warp, int rs, int cc, int tid) {
+#pragma unroll
+  for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 v = acc[m][t][i];
+        v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
+        v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
+        acc[m][t][i] = v;
+      }
+  if (rs == 0) {
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        float4* dst = reinterpret_cast<float4*>(red + static_cast<int64_t>(warp) * NMAT * T * kTileN +
+                                                (m * T + t) * kTileN + cc * 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_float4(acc[m][t][2 * i].x, acc[m][t][2 * i].y, acc[m][t][2 * i + 1].x, acc[m][t][2 * i + 1].y);
+      }
   }
   consumer_sync();
-  if (!*s_last) return false;
-  __threadfence();
-  const float* base = ws + static_cast<int64_t>(tile) * cpt * kItems;
+  constexpr int kItems = NMAT * T * kTileN;
   for (int i = tid; i < kItems; i += kConsumers) {
     float v = 0.f;
-    for (int pc0 = 0; pc0 < cpt; pc0 += 16) {
-      float pv[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) pv[j] = (pc0 + j < cpt) ? __ldcg(base + static_cast<int64_t>(pc0 + j) * kItems + i) : 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (pc0 + j < cpt) v += pv[j];
+    for (int w = 0; w < kConsumerWarps; ++w) v += red[w * kItems + i];
+    if (!(fabsf(v) < kFixLimit)) {
+      atomicCAS(status, PYRE_OK, PYRE_ERANGE);
+      v = 0.f;
     }
-    fin[i] = v;
+    atomicAdd(accum + i, static_cast<unsigned long long>(__float2ll_rn(v * kFixScale)));
   }
-  consumer_sync();
-  if (tid == 0) cnt[tile] = 0u;
+  consumer_sync();   // red is rewritten at the next chunk's end
+}
+
+// Helper-warp read-back of a finished slab accumulator: for this lane's column pairs,
+// returns the sums of the M rows at row offsets off[m] (in floats of the [.., kTileN] grid)
+// as f32 and clears them. kPairs column pairs per call, lane-strided.
+template <int M, int kPairs>
+__device__ __forceinline__ void take_acc(unsigned long long* base, const int (&off)[M], int pair0, float2 (&out)[kPairs][M]) {
+  ulonglong2 v[kPairs][M];
+#pragma unroll
+  for (int k = 0; k < kPairs; ++k)
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      v[k][m] = __ldcg(reinterpret_cast<const ulonglong2*>(base + off[m]) + pair0 + k * 32);
+#pragma unroll
+  for (int k = 0; k < kPairs; ++k)
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      __stcg(reinterpret_cast<ulonglong2*>(base + off[m]) + pair0 + k * 32, make_ulonglong2(0ull, 0ull));
+      out[k][m] = make_float2(__ll2float_rn(static_cast<long long>(v[k][m].x)) * kFixInv,
+                              __ll2float_rn(static_cast<long long>(v[k][m].y)) * kFixInv);
+    }
+}
+
+// Queue position -> chunk for MODE_AB (see the scheduling note above). Returns false past
+// the end; tile may be >= tilesA for the padding slabs of a short last group (skipped).
+__host__ __device__ __forceinline__ bool ab_item(const StreamParams& p, int pos, int& phase, int& tile, int& chunk) {
+  const int sA = p.spg * p.cptA, sB = p.tilesB, G = p.cptB, D = min(p.slack, G);
+  int g, j;
+  if (pos < D * sA) {
+    g = pos / sA;
+    j = pos - g * sA;
+  } else {
+    const int q = pos - D * sA;
+    const int mid = (G - D) * (sA + sB);
+    if (q < mid) {
+      const int k = q / (sA + sB);
+      j = q - k * (sA + sB);
+      if (j >= sA) {
+        phase = 1;
+        chunk = k;
+        tile = j - sA;
+        return true;
+      }
+      g = D + k;
+    } else {
+      const int r = q - mid;
+      if (r >= D * sB) return false;
+      phase = 1;
+      chunk = G - D + r / sB;
+      tile = r - (r / sB) * sB;
+      return true;
+    }
+  }
+  phase = 0;
+  tile = g * p.spg + j / p.cptA;
+  chunk = j - (j / p.cptA) * p.cptA;
   return true;
 }
 
 template <int T, int NA, typename XA, typename XB, typename ST, int MODE, bool TP>
-__global__ void __launch_bounds__(kThreads, (StreamCfg<T, NA, XA, XB, ST>::kCtasPerSm))
+__global__ void __launch_bounds__(kStreamThreads, (StreamCfg<T, NA, XA, XB, ST>::kCtasPerSm))
 q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
   using C = StreamCfg<T, NA, XA, XB, ST>;
   using LA = typename C::LA;
@@ -146,11 +246,13 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
   float* red = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
-  float* fin = red + C::kRedFloats;
-  uint64_t* full = reinterpret_cast<uint64_t*>(fin + C::kFinFloats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + C::kRedFloats);
   uint64_t* empty = full + C::kStages;
-  StageMeta* meta = reinterpret_cast<StageMeta*>(empty + C::kStages);
-  int* s_last = reinterpret_cast<int*>(meta + C::kStages);
+  uint64_t* job_full = empty + C::kStages;
+  uint64_t* job_empty = job_full + kJobs;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(job_empty + kJobs);
+  Job* jobs = reinterpret_cast<Job*>(meta + C::kStages);
+  int* s_last = reinterpret_cast<int*>(jobs + kJobs);
   int* owned = s_last + 4;           // [0]: count, then slab ids (tensor-parallel finish)
 
   const int warp = threadIdx.x >> 5;
@@ -159,6 +261,10 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
     for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kConsumerWarps);
+    }
+    for (int i = 0; i < kJobs; ++i) {
+      mbar_init(&job_full[i], kConsumerWarps);
+      mbar_init(&job_empty[i], 1);
     }
     owned[0] = 0;
     fence_mbar_init();
@@ -176,8 +282,8 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       if constexpr (kHasB) prefetch_tmap(&p.txb);
       int s = 0;
       uint32_t ph = 0;
-      // Failure handling: after any wait runs out (here or in another CTA, seen through the
-      // status word) the producer issues no more copies, still tries to hand the consumers
+      // Failure handling: after any wait runs out (here or in another CTA, seen as
+      // PYRE_ETIMEOUT in the status word) the producer issues no more copies, still tries to hand the consumers
       // their end marker, and waits (bounded) for the copies it already issued, so that no
       // copy into this CTA's shared memory is in flight when it exits.
       bool ok = true;
@@ -195,68 +301,72 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
           ph ^= 1u;
         }
       };
-      auto failed = [&]() { return *reinterpret_cast<volatile int*>(p.status) != PYRE_OK; };
-      if constexpr (kHasA) {
-        while (ok) {
-          if (failed()) {
-            ok = false;
-            break;
-          }
-          const int ch = static_cast<int>(atomicAdd(p.next, 1u));
-          if (ch >= p.ncA) break;
-          const int tile = ch / p.cptA, chunk = ch - tile * p.cptA;
-          const int u0 = chunk * kChunk;
-          const int u1 = min(u0 + kChunk, p.uptA);
-          for (int u = u0; u < u1; ++u) {
-            if (!acquire()) {
-              ok = false;
-              break;
+      auto failed = [&]() { return *reinterpret_cast<volatile int*>(p.status) == PYRE_ETIMEOUT; };
+      // issues the stages of one chunk; false once a wait ran out
+      auto issue_chunk = [&](int phase, int tile, int chunk) -> bool {
+        if (phase == 0) {
+          if constexpr (kHasA) {
+            const int u0 = chunk * kChunk;
+            const int u1 = min(u0 + kChunk, p.uptA);
+            for (int u = u0; u < u1; ++u) {
+              if (!acquire()) return false;
+              meta[s] = StageMeta{0, tile, chunk, u + 1 == u1};
+              uint8_t* st = stages + s * C::kStageBytes;
+              mbar_arrive_expect_tx(&full[s], LA::kTxBytes);
+              bulk_load(st, p.wa + (static_cast<int64_t>(tile) * p.uptA + u) * LA::kWBytes, LA::kWBytes, &full[s]);
+              tma_load_2d(st + LA::kXOff, &p.txa, u * LA::kRows, 0, &full[s]);
+              issue_done();
             }
-            meta[s] = StageMeta{0, tile, chunk, u + 1 == u1};
-            uint8_t* st = stages + s * C::kStageBytes;
-            mbar_arrive_expect_tx(&full[s], LA::kTxBytes);
-            bulk_load(st, p.wa + (static_cast<int64_t>(tile) * p.uptA + u) * LA::kWBytes, LA::kWBytes, &full[s]);
-            tma_load_2d(st + LA::kXOff, &p.txa, u * LA::kRows, 0, &full[s]);
-            issue_done();
           }
-        }
-      }
-      if constexpr (kHasB) {
-        while (ok) {
-          if (failed()) {
-            ok = false;
-            break;
-          }
-          const int ch = static_cast<int>(atomicAdd(p.next + 1, 1u));
-          if (ch >= p.ncB) break;
-          const int tile = ch / p.cptB, chunk = ch - tile * p.cptB;
-          const int u0 = chunk * kChunk;
-          const int u1 = min(u0 + kChunk, p.uptB);
-          for (int u = u0; u < u1; ++u) {
-            if (!acquire()) {
-              ok = false;
-              break;
-            }
-            meta[s] = StageMeta{1, tile, chunk, u + 1 == u1};
-            uint8_t* st = stages + s * C::kStageBytes;
-            mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
-            bulk_load(st, p.wb + (static_cast<int64_t>(tile) * p.uptB + u) * LB::kWBytes, LB::kWBytes, &full[s]);
-            const int k0 = u * LB::kRows;
-            bool rdy = true;
-            if constexpr (MODE == MODE_AB) {
-              // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256)
-              rdy = wait_ready(p.ready + k0 / kTileN, epoch, p.status);
-              fence_proxy_async_global();
-            }
-            // issued even when the flag wait ran out, so the stage's byte count completes
-            tma_load_2d(st + LB::kXOff, &p.txb, k0, 0, &full[s]);
-            issue_done();
-            if (!rdy) {
-              ok = false;
-              break;
+        } else {
+          if constexpr (kHasB) {
+            const int u0 = chunk * kChunk;
+            const int u1 = min(u0 + kChunk, p.uptB);
+            for (int u = u0; u < u1; ++u) {
+              if (!acquire()) return false;
+              meta[s] = StageMeta{1, tile, chunk, u + 1 == u1};
+              uint8_t* st = stages + s * C::kStageBytes;
+              mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
+              bulk_load(st, p.wb + (static_cast<int64_t>(tile) * p.uptB + u) * LB::kWBytes, LB::kWBytes, &full[s]);
+              const int k0 = u * LB::kRows;
+              bool rdy = true;
+              if constexpr (MODE == MODE_AB) {
+                // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256)
+                rdy = wait_ready(p.ready + k0 / kTileN, epoch, p.status);
+                fence_proxy_async_global();
+              }
+              // issued even when the flag wait ran out, so the stage's byte count completes
+              tma_load_2d(st + LB::kXOff, &p.txb, k0, 0, &full[s]);
+              issue_done();
+              if (!rdy) return false;
             }
           }
         }
+        return true;
+      };
+      while (ok) {
+        if (failed()) {
+          ok = false;
+          break;
+        }
+        const int pos = static_cast<int>(atomicAdd(p.next, 1u));
+        int phase, tile, chunk;
+        if constexpr (MODE == MODE_AB) {
+          if (!ab_item(p, pos, phase, tile, chunk)) break;
+          if (phase == 0 && tile >= p.tilesA) continue;
+        } else if constexpr (MODE == MODE_A) {
+          if (pos >= p.ncA) break;
+          phase = 0;
+          tile = pos / p.cptA;
+          chunk = pos - tile * p.cptA;
+        } else {
+          if (pos >= p.ncB) break;
+          // chunk-major, like the MODE_AB queue
+          phase = 1;
+          chunk = pos / p.tilesB;
+          tile = pos - chunk * p.tilesB;
+        }
+        ok = issue_chunk(phase, tile, chunk);
       }
       // end marker for the consumers
       if (acquire()) {
@@ -268,13 +378,30 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
           if ((issued >> i) & 1u) mbar_wait(&full[i], (par >> i) & 1u, nullptr, 500000000ull);
       }
     }
-  } else {
+  } else if (warp < kConsumerWarps) {
     // ---------------- consumers ----------------
+    // Stream stages into register accumulators; at the end of each chunk add it into its
+    // slab accumulator and queue it for the helper warp, which counts it and runs the slab
+    // epilogue while the consumers go on with the next chunk.
     const int tid = threadIdx.x;
     const int rs = lane >> 4;
     const int cc = lane & 15;
     int s = 0;
     uint32_t ph = 0;
+    int jb = 0;
+    uint32_t jph = 0;
+    auto post_job = [&](const Job& job) {
+      // every warp waits for the slot so that no arrival runs a phase ahead of the helpers
+      if (lane == 0) mbar_wait(&job_empty[jb], jph ^ 1u, p.status);
+      __syncwarp();
+      if (tid == 0) jobs[jb] = job;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&job_full[jb]);
+      if (++jb == kJobs) {
+        jb = 0;
+        jph ^= 1u;
+      }
+    };
     float2 acc[NA][T][8];
     zero_acc<NA, T>(acc);
     while (true) {
@@ -296,57 +423,143 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
         ph ^= 1u;
       }
       if (!m.last) continue;
-      // a chunk is complete: reduce it, fix up its slab, run the slab epilogue
       if (kHasA && m.phase == 0) {
-        reduce_tile<T, NA>(acc, red, fin, warp, rs, cc, tid);
-        zero_acc<NA, T>(acc);
-        if (chunk_fixup<T, NA>(fin, p.wsA, p.cntA, p.cptA, m.tile, m.chunk, s_last, tid)) {
-          for (int i = tid; i < T * kTileN; i += kConsumers) {
-            const int t = i / kTileN, col = m.tile * kTileN + (i % kTileN);
-            if (col >= p.NA) continue;
-            const float v = (NA == 2) ? silu_f32(fin[i]) * fin[T * kTileN + i] : silu_f32(fin[i]);
-            store_out(p.outA, p.outA_bf16, p.NA, t, col, v);
-          }
-          if constexpr (MODE == MODE_AB) {
-            __threadfence();
-            fence_proxy_async_global();
-            consumer_sync();
-            if (tid == 0) st_release_gpu(p.ready + m.tile, epoch);
-          }
-        }
+        reduce_to_acc<T, NA>(acc, red, p.accA + static_cast<int64_t>(m.tile) * (NA * T * kTileN), p.status, warp, rs,
+                             cc, tid);
       } else if constexpr (kHasB) {
         float2(&acc1)[1][T][8] = reinterpret_cast<float2(&)[1][T][8]>(acc);
-        reduce_tile<T, 1>(acc1, red, fin, warp, rs, cc, tid);
-        zero_acc<NA, T>(acc);
-        if (chunk_fixup<T, 1>(fin, p.wsB, p.cntB, p.cptB, m.tile, m.chunk, s_last, tid)) {
-          if constexpr (TP) {
-            tp_push_tile<T>(p.comm, cepoch, m.tile, fin, tid);
-            if (tid == 0) owned[1 + owned[0]++] = m.tile;
-          } else {
-            for (int i = tid; i < T * kTileN; i += kConsumers) {
-              const int t = i / kTileN, col = m.tile * kTileN + (i % kTileN);
-              if (col < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col] = fin[i];
+        reduce_to_acc<T, 1>(acc1, red, p.accB + static_cast<int64_t>(m.tile) * (T * kTileN), p.status, warp, rs, cc,
+                            tid);
+      }
+      zero_acc<NA, T>(acc);
+      post_job(Job{m.phase, m.tile, m.chunk, 0});
+    }
+    post_job(Job{0, 0, 0, 1});
+  } else {
+    // ---------------- helpers ----------------
+    // Per finished chunk: count it for its slab (release); the CTA that counts a slab's
+    // last chunk reads the slab sums back and runs the slab epilogue.
+    const int htid = threadIdx.x - (kThreads);
+    int jb = 0;
+    uint32_t jph = 0;
+    while (true) {
+      if (!mbar_wait(&job_full[jb], jph, p.status, 8000000000ull)) break;
+      const Job job = jobs[jb];
+      helper_sync();
+      if (htid == 0) mbar_arrive(&job_empty[jb]);
+      if (++jb == kJobs) {
+        jb = 0;
+        jph ^= 1u;
+      }
+      if (job.end) break;
+      const bool isA = kHasA && job.phase == 0;
+      const int cpt = isA ? p.cptA : p.cptB;
+      if (htid == 0) {
+        // the consumers' accumulator adds are ordered before this (barrier, then mbarrier
+        // release/acquire); the fence makes them visible GPU-wide before the count
+        unsigned int* cnt = (isA ? p.cntA : p.cntB) + job.tile;
+        __threadfence();
+        const unsigned prev = atomicAdd(cnt, 1u);
+        const int last = prev == static_cast<unsigned>(cpt - 1);
+        if (last) {
+          __threadfence();
+          *cnt = 0u;      // every chunk of the slab has counted: reset for the next call
+        }
+        *s_last = last;
+      }
+      helper_sync();
+      const int last = *s_last;
+      helper_sync();    // s_last is rewritten for the next job
+      if (!last) continue;
+      if (isA) {
+        if constexpr (kHasA) {
+          // h[t, col] for this slab: lane owns column pairs lane, lane + 32, .. (kTileN / 64)
+          constexpr int kPairs = kTileN / 64;
+          unsigned long long* base = p.accA + static_cast<int64_t>(job.tile) * (NA * T * kTileN);
+#pragma unroll 1
+          for (int t = 0; t < T; ++t) {
+            int off[NA];
+#pragma unroll
+            for (int m = 0; m < NA; ++m) off[m] = (m * T + t) * kTileN;
+            float2 gu[kPairs][NA];
+            take_acc<NA, kPairs>(base, off, htid, gu);
+#pragma unroll
+            for (int k = 0; k < kPairs; ++k) {
+              const int col = job.tile * kTileN + 2 * (htid + 32 * k);
+              const float2 g = gu[k][0];
+              float h0 = silu_f32(g.x), h1 = silu_f32(g.y);
+              if constexpr (NA == 2) {
+                h0 *= gu[k][1].x;
+                h1 *= gu[k][1].y;
+              }
+              if (col < p.NA) store_out(p.outA, p.outA_bf16, p.NA, t, col, h0);
+              if (col + 1 < p.NA) store_out(p.outA, p.outA_bf16, p.NA, t, col + 1, h1);
+            }
+          }
+          if constexpr (MODE == MODE_AB) {
+            // h is read next by other CTAs' TMA (async proxy): proxy fence per writer, then
+            // one cumulative release of the slab's flag
+            fence_proxy_async_global();
+            helper_sync();
+            if (htid == 0) {
+              __threadfence();
+              st_release_gpu(p.ready + job.tile, epoch);
             }
           }
         }
+      } else {
+        if constexpr (kHasB) {
+          constexpr int kPairs = kTileN / 64;
+          unsigned long long* base = p.accB + static_cast<int64_t>(job.tile) * (T * kTileN);
+          const int slotp = TP ? static_cast<int>(cepoch & 1u) : 0;
+#pragma unroll 1
+          for (int t = 0; t < T; ++t) {
+            const int off[1] = {t * kTileN};
+            float2 v[kPairs][1];
+            take_acc<1, kPairs>(base, off, htid, v);
+#pragma unroll
+            for (int k = 0; k < kPairs; ++k) {
+              const int c = 2 * (htid + 32 * k);
+              if constexpr (TP) {
+                for (int peer = 0; peer < p.comm.world; ++peer) {
+                  float* dst = comm::fused_slot(p.comm, peer, slotp, p.comm.rank) +
+                               static_cast<int64_t>(job.tile) * (T * kTileN) + t * kTileN + c;
+                  *reinterpret_cast<float2*>(dst) = v[k][0];
+                }
+              } else {
+                const int col = job.tile * kTileN + c;
+                if (col < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col] = v[k][0].x;
+                if (col + 1 < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col + 1] = v[k][0].y;
+              }
+            }
+          }
+          if constexpr (TP) {
+            __threadfence_system();
+            helper_sync();
+            if (htid < p.comm.world)
+              st_release_sys(comm::fused_flag(p.comm, htid, slotp, p.comm.rank, job.tile), cepoch);
+            if (htid == 0) owned[1 + owned[0]++] = job.tile;
+          }
+        }
       }
-      consumer_sync();
-    }
-    if constexpr (TP) {
-      // every chunk of this CTA is done: now wait for the peers of the slabs it finished
-      const int n_owned = owned[0];
-      for (int i = 0; i < n_owned; ++i) tp_finish_tile<T>(p.comm, cepoch, owned[1 + i], p.outB, p.NB, tid);
     }
   }
   __syncthreads();
-  if constexpr (TP) comm::epoch_end(p.comm, cepoch);
+  if constexpr (TP) {
+    // every chunk of this CTA is done: now wait for the peers of the slabs it finished
+    if (warp < kConsumerWarps) {
+      const int n_owned = owned[0];
+      for (int i = 0; i < n_owned; ++i) tp_finish_tile<T>(p.comm, cepoch, owned[1 + i], p.outB, p.NB, threadIdx.x);
+    }
+    __syncthreads();
+    comm::epoch_end(p.comm, cepoch);
+  }
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(p.ws_done, 1u);
     if (prev == gridDim.x - 1) {
-      // last CTA: reset the chunk counters and publish the epoch for the next call
+      // last CTA: reset the queue counter and publish the epoch for the next call
       p.next[0] = 0u;
-      p.next[1] = 0u;
       *reinterpret_cast<volatile unsigned int*>(p.ws_done) = 0u;
       __threadfence();
       *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) = epoch;

@@ -86,7 +86,35 @@ def test_ffn_deterministic_and_workspace_reuse():
     hdr = op.workspace[:32768].view(torch.int32)
     assert int(hdr[0]) == 5                                  # call epoch: one per call
     assert int(hdr[2]) == 0                                  # status word
-    assert int(hdr[256:256 + 2 * 2048].abs().sum()) == 0     # stream-K counters reset
+    assert int(hdr[4]) == 0                                  # chunk queue position reset
+    assert int(hdr[256:256 + 2 * 2048].abs().sum()) == 0     # per-slab chunk counters reset
+    # after the h buffer ([2, 3072] f32) come the fixed-point slab accumulators: cleared
+    acc = op.workspace[32768 + 2 * 3072 * 4:]
+    assert int(acc.count_nonzero()) == 0
+
+
+def test_ffn_range_status_and_reset():
+    """A partial sum outside the fixed-point range (here from an infinite input) is added as 0
+    and flagged PYRE_ERANGE in the status word; reset() clears it and the op keeps working."""
+    from pyre_b200 import _native as N
+    from pyre_b200.ffn import FfnShardOp
+    rng = np.random.default_rng(12)
+    g, gf = make_weight((512, 768), rng, torch.float16)
+    u, uf = make_weight((512, 768), rng, torch.float16)
+    d, df = make_weight((768, 512), rng, torch.float16)
+    op = FfnShardOp(512, 768, max_tokens=1)
+    bad = torch.zeros((1, 512), device="cuda")
+    bad[0, 7] = float("inf")
+    op(bad, g, u, d)
+    torch.cuda.synchronize()
+    assert op.status() == N.PYRE_ERANGE
+    op.reset()
+    assert op.status() == N.PYRE_OK
+    x = rng.standard_normal((1, 512)).astype(np.float32)
+    out = op(torch.from_numpy(x).cuda(), g, u, d)
+    torch.cuda.synchronize()
+    assert op.status() == N.PYRE_OK
+    assert rel_err(out.cpu().numpy(), offn.ffn_shard_f64(x, gf, uf, df)) < TOL_F32
 
 
 def test_gated_golden_from_reference_builder():
