@@ -124,6 +124,25 @@ PYRE_API int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H,
                                  float* out, void* workspace, int64_t ws_bytes,
                                  pyre_comm_t* comm, void* stream);
 
+/* No counterpart in the reference: this library's own entry point for callers that cannot
+ * allocate device memory (a host program that binds only this C ABI with no CUDA allocator
+ * of its own, or a runtime whose device memory all belongs to its own pool, where a
+ * cudaMalloc fails or synchronises the device mid-serving).
+ * Same computation, inputs and outputs as pyre_ffn_decode_q80 on one GPU (no communicator),
+ * but the scratch is a static device array of PYRE_NOALLOC_SCRATCH_BYTES inside the library,
+ * so the call allocates nothing. Limits and rules:
+ *   - sizes whose workspace (pyre_ffn_workspace_bytes) exceeds PYRE_NOALLOC_SCRATCH_BYTES are
+ *     rejected with PYRE_EINVAL;
+ *   - every GPU that loads the library holds the array until the process exits;
+ *   - the first call on a device looks up the array's address on that device (with that
+ *     device current); make it before any stream capture;
+ *   - calls on one device share the array: each call clears it on its stream first, and
+ *     calls that overlap on the GPU race (serialise them on one stream). */
+#define PYRE_NOALLOC_SCRATCH_BYTES (4 << 20)
+PYRE_API int pyre_ffn_decode_q80_noalloc(const void* x, int x_dtype, int T, int H,
+                                         const void* wgu, int gated, const void* wd, int scale_dtype,
+                                         int W, float* out, void* stream);
+
 /* out[T, H] = h @ Wd   (src/ffn/builder.py:44), and with comm != NULL also the sum of
  * that partial over every rank of comm (src/orchestrator/root_node.py:582-594 and
  * :982-995, `ffn_out += partial`), in rank order 0..world-1 on every rank. For

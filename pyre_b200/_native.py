@@ -16,6 +16,7 @@ PYRE_ECUDA = 2
 PYRE_ETIMEOUT = 3
 PYRE_ENOMEM = 4
 PYRE_ERANGE = 5
+PYRE_NOALLOC_SCRATCH_BYTES = 4 << 20
 
 PYRE_F32 = 0
 PYRE_BF16 = 1
@@ -54,6 +55,7 @@ _SIGNATURES = {
     "pyre_ffn_gateup_silu_q80": [_vp, _i, _i, _i, _vp, _i, _i, _i, _vp, _i, _vp, _c_i64, _vp],
     "pyre_ffn_down_q80": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
     "pyre_ffn_decode_q80": [_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
+    "pyre_ffn_decode_q80_noalloc": [_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _vp],
     "pyre_comm_buffer_bytes": [_i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_comm_alloc": [_c_i64, ctypes.POINTER(_vp), _vp],
     "pyre_comm_free": [_vp],
