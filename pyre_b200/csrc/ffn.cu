@@ -1,6 +1,6 @@
 // Gated-SiLU FFN shard on Q8_0 weights, two-call form: gate/up + SiLU·mul, then down
 // (+ the cross-rank sum). Decode (T <= 4) runs the streaming kernel of ffn_stream.cuh;
-// larger T runs a SIMT dequant GEMM (placeholder for the tensor-core path).
+// larger T runs the tensor-core GEMM of gemm_tc.cu.
 //
 // Reference semantics (src/ffn/builder.py:37-45, src/orchestrator/root_node.py:972-980):
 //   gate = x @ Wg, up = x @ Wu, h = silu(gate) * up, partial = h @ Wd
@@ -10,131 +10,12 @@
 //
 // Weights are in the packed block layout of gemv_common.cuh (gate and up interleaved per
 // block for the gated form).
-#include <algorithm>
-
 #include "ffn_internal.cuh"
 
 namespace pyre {
 namespace ffn {
 
 using namespace gemv;
-
-template <typename ST>
-__device__ __forceinline__ float ld_scale(const void* s, int64_t i) {
-  return to_f32(__ldg(static_cast<const ST*>(s) + i));
-}
-
-template <typename XT>
-__device__ __forceinline__ float ld_x(const void* x, int64_t i) {
-  return to_f32(__ldg(static_cast<const XT*>(x) + i));
-}
-
-// ---- SIMT GEMM for T > 4 --------------------------------------------------------------
-// CTA tile: 64 tokens x 64 columns, K step 32. Weights are dequantized into shared
-// memory as f32; each thread owns a 4x4 block of outputs per matrix.
-constexpr int kGM = 64, kGN = 64, kGK = 32;
-
-template <int NMAT, int EPI, typename XT, typename ST>
-__global__ void __launch_bounds__(256) q80_gemm_simt_kernel(const Params p) {
-  __shared__ float xs[kGK][kGM + 4];
-  __shared__ float wsm[NMAT][kGK][kGN + 4];
-  const int tx = threadIdx.x & 15;   // column group
-  const int ty = threadIdx.x >> 4;   // token group
-  const int n0 = blockIdx.x * kGN;
-  const int t0 = blockIdx.y * kGM;
-  float acc[NMAT][4][4];
-#pragma unroll
-  for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[m][i][j] = 0.f;
-  constexpr int R = UnitRows<NMAT>::value;
-  const int64_t bbytes = packed_block_bytes(NMAT, sizeof(ST));
-
-  for (int k0 = 0; k0 < p.K; k0 += kGK) {
-    for (int i = threadIdx.x; i < kGM * kGK; i += 256) {
-      const int tt = i / kGK, kk = i % kGK;
-      const int t = t0 + tt, k = k0 + kk;
-      xs[kk][tt] = (t < p.T && k < p.K) ? ld_x<XT>(p.x, static_cast<int64_t>(t) * p.K + k) : 0.f;
-    }
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m) {
-      for (int i = threadIdx.x; i < kGK * kGN; i += 256) {
-        const int kk = i / kGN, nn = i % kGN;
-        const int k = k0 + kk, n = n0 + nn;
-        float w = 0.f;
-        if (k < p.K && n < p.N) {
-          const uint8_t* blk = p.w + (static_cast<int64_t>(n / kTileN) * p.upt + k / R) * bbytes;
-          const int rr = k % R, cn = n % kTileN;
-          const int8_t q = reinterpret_cast<const int8_t*>(blk)[(m * R + rr) * kTileN + cn];
-          const ST* sc = reinterpret_cast<const ST*>(blk + NMAT * R * kTileN);
-          w = static_cast<float>(q) * to_f32(sc[(m * R + rr) * 8 + (cn >> 5)]);
-        }
-        wsm[m][kk][nn] = w;
-      }
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int kk = 0; kk < kGK; ++kk) {
-      float a[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty * 4 + i];
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        float b[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) b[j] = wsm[m][kk][tx * 4 + j];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[m][i][j] = fmaf(a[i], b[j], acc[m][i][j]);
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty * 4 + i;
-    if (t >= p.T) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n >= p.N) continue;
-      float v;
-      if constexpr (EPI == EPI_SILU_MUL) {
-        v = silu_f32(acc[0][i][j]) * acc[NMAT - 1][i][j];
-      } else if constexpr (EPI == EPI_SILU) {
-        v = silu_f32(acc[0][i][j]);
-      } else {
-        v = acc[0][i][j];
-      }
-      store_out(p.out, p.out_bf16, p.N, t, n, v);
-    }
-  }
-}
-
-// ---- host side ------------------------------------------------------------------------
-
-template <int NMAT, int EPI, typename XT, typename ST>
-int dispatch_T(Params p, cudaStream_t s) {
-  static_assert(EPI != EPI_TP || NMAT == 1, "TP epilogue is single-matrix");
-  dim3 grid((p.N + kGN - 1) / kGN, (p.T + kGM - 1) / kGM);
-  constexpr int GEPI = EPI == EPI_TP ? EPI_STORE : EPI;
-  q80_gemm_simt_kernel<NMAT, GEPI, XT, ST><<<grid, 256, 0, s>>>(p);
-  PYRE_LAUNCH_CHECK("q80_gemm_simt_kernel");
-  return PYRE_OK;
-}
-
-template <int NMAT, int EPI>
-int dispatch_types(Params p, int x_dtype, int scale_dtype, cudaStream_t s) {
-  if (x_dtype == PYRE_BF16) {
-    if (scale_dtype == PYRE_F16) return dispatch_T<NMAT, EPI, __nv_bfloat16, __half>(p, s);
-    return dispatch_T<NMAT, EPI, __nv_bfloat16, float>(p, s);
-  }
-  if (scale_dtype == PYRE_F16) return dispatch_T<NMAT, EPI, float, __half>(p, s);
-  return dispatch_T<NMAT, EPI, float, float>(p, s);
-}
 
 }  // namespace ffn
 
@@ -172,25 +53,10 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_gateup(x, x_dtype, T, H, wgu, gated, scale_dtype, W, h, h_dtype, workspace, ws_bytes, s);
-  const int R = gated ? kUnitRowsPair : kUnitRowsSingle;
   char* wsc = static_cast<char*>(workspace);
-  Params p{};
-  p.x = x;
-  p.w = static_cast<const uint8_t*>(wgu);
-  p.K = H;
-  p.N = W;
-  p.T = T;
-  p.tiles = tiles_of(W);
-  p.upt = (H + R - 1) / R;
-  p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
-  p.counters = reinterpret_cast<unsigned int*>(wsc + kHdrCntA);
-  p.status = reinterpret_cast<int*>(wsc + kHdrStatus);
-  p.ws = reinterpret_cast<float*>(wsc + kHeaderBytes);
-  p.ws_cap = ws_bytes - kHeaderBytes;
-  p.out = h;
-  p.out_bf16 = h_dtype == PYRE_BF16;
-  if (gated) return dispatch_types<2, EPI_SILU_MUL>(p, x_dtype, scale_dtype, s);
-  return dispatch_types<1, EPI_SILU>(p, x_dtype, scale_dtype, s);
+  return ffn_gemm_tc(x, x_dtype, T, H, wgu, gated ? 2 : 1, gated ? EPI_SILU_MUL : EPI_SILU, scale_dtype, W, h,
+                     h_dtype == PYRE_BF16, wsc + kHeaderBytes, ws_bytes - kHeaderBytes,
+                     reinterpret_cast<int*>(wsc + kHdrStatus), s);
 }
 
 extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H,
@@ -207,23 +73,9 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_down(h, h_dtype, T, W, wd, scale_dtype, H, out, workspace, ws_bytes, comm, s);
   char* wsc = static_cast<char*>(workspace);
-  Params p{};
-  p.x = h;
-  p.w = static_cast<const uint8_t*>(wd);
-  p.K = W;
-  p.N = H;
-  p.T = T;
-  p.tiles = tiles_of(H);
-  p.upt = (W + kUnitRowsSingle - 1) / kUnitRowsSingle;
-  p.total_units = static_cast<int64_t>(p.tiles) * p.upt;
-  p.counters = reinterpret_cast<unsigned int*>(wsc + kHdrCntB);
-  p.status = reinterpret_cast<int*>(wsc + kHdrStatus);
-  p.ws = reinterpret_cast<float*>(wsc + kHeaderBytes);
-  p.ws_cap = ws_bytes - kHeaderBytes;
-  p.out = out;
-  p.out_bf16 = 0;
+  rc = ffn_gemm_tc(h, h_dtype, T, W, wd, 1, EPI_STORE, scale_dtype, H, out, 0, wsc + kHeaderBytes,
+                   ws_bytes - kHeaderBytes, reinterpret_cast<int*>(wsc + kHdrStatus), s);
   const bool tp = comm != nullptr && comm->world > 1;
-  rc = dispatch_types<1, EPI_STORE>(p, h_dtype, scale_dtype, s);
   if (rc || !tp) return rc;
   return allreduce_sum_f32(comm, out, static_cast<int64_t>(T) * H, s);
 }

@@ -180,9 +180,13 @@ using namespace pyre::ffn;
 extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   PYRE_CHECK_ARG(bytes != nullptr, "pyre_ffn_workspace_bytes: null bytes");
   PYRE_CHECK_ARG(T >= 1 && H >= 1 && W >= 1, "pyre_ffn_workspace_bytes: sizes must be positive");
-  int64_t need = kHeaderBytes;
-  if (T <= PYRE_FUSED_REDUCE_MAX_T) {
-    need = decode_ws_bytes(T, H, W, 2);   // covers the two-call forms too
+  // decode (T <= 4, also the two-call forms) and, for larger T, the bf16 copy of f32
+  // activations that the tensor-core GEMM reads
+  const int td = T < PYRE_FUSED_REDUCE_MAX_T ? T : PYRE_FUSED_REDUCE_MAX_T;
+  int64_t need = decode_ws_bytes(td, H, W, 2);
+  if (T > PYRE_FUSED_REDUCE_MAX_T) {
+    const int64_t stage = kHeaderBytes + align256(static_cast<int64_t>(T) * (H > W ? H : W) * 2);
+    if (stage > need) need = stage;
   }
   *bytes = need;
   return PYRE_OK;

@@ -133,6 +133,8 @@ int coresident_grid(K kern, int threads, int smem, int want_per_sm, int64_t unit
 int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
                      const void* ws, int64_t ws_bytes, const char* fn);
 // Streaming-kernel forms of the two-call entry points for T <= 4 (defined in ffn_decode.cu).
+int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
+                void* out, int out_bf16, void* staging, int64_t staging_bytes, int* status, cudaStream_t s);
 int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, int scale_dtype, int W,
                       void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s);
 int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,

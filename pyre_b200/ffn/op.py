@@ -76,7 +76,7 @@ class FfnShardOp:
         self.gated = gated
         self.comm = comm
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        wsb = workspace_bytes(min(self.max_tokens, N.PYRE_FUSED_REDUCE_MAX_T), self.hidden, self.width)
+        wsb = workspace_bytes(self.max_tokens, self.hidden, self.width)
         self.workspace = torch.zeros(wsb, dtype=torch.uint8, device=self.device)
         self.fused = fused
 
