@@ -25,7 +25,8 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
   PYRE_CHECK_ARG(x != nullptr && out != nullptr, f + ": null input/output");
   PYRE_CHECK_ARG(T >= 1 && K >= 1 && N >= 32, f + ": sizes must be positive (N >= 32)");
   PYRE_CHECK_ARG(N % 32 == 0, f + ": output width must be a multiple of 32 (Q8_0 blocks run along it)");
-  PYRE_CHECK_ARG(x_dtype == PYRE_F32 || x_dtype == PYRE_BF16, f + ": activation dtype must be f32 or bf16");
+  PYRE_CHECK_ARG(x_dtype == PYRE_F32 || x_dtype == PYRE_BF16 || (x_dtype == PYRE_F16 && T > PYRE_FUSED_REDUCE_MAX_T),
+                 f + ": activation dtype must be f32 or bf16 (or f16 for T > PYRE_FUSED_REDUCE_MAX_T)");
   PYRE_CHECK_ARG(scale_dtype == PYRE_F32 || scale_dtype == PYRE_F16, f + ": scale dtype must be f32 or f16");
   PYRE_CHECK_ARG(gemv::tiles_of(N) <= gemv::kMaxTiles, f + ": output width too large");
   PYRE_CHECK_ARG(T > PYRE_FUSED_REDUCE_MAX_T || (static_cast<int64_t>(K) * (x_dtype == PYRE_BF16 ? 2 : 4)) % 16 == 0,
@@ -49,14 +50,16 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   if (rc) return rc;
   PYRE_CHECK_ARG(wgu != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0,
                  "pyre_ffn_gateup_silu_q80: packed gate/up weights must be non-null and 16-byte aligned");
-  PYRE_CHECK_ARG(h_dtype == PYRE_F32 || h_dtype == PYRE_BF16, "pyre_ffn_gateup_silu_q80: h dtype must be f32 or bf16");
+  PYRE_CHECK_ARG(h_dtype == PYRE_F32 || h_dtype == PYRE_BF16 || (h_dtype == PYRE_F16 && T > PYRE_FUSED_REDUCE_MAX_T),
+                 "pyre_ffn_gateup_silu_q80: h dtype must be f32 or bf16 (or f16 for T > PYRE_FUSED_REDUCE_MAX_T)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_gateup(x, x_dtype, T, H, wgu, gated, scale_dtype, W, h, h_dtype, workspace, ws_bytes, s);
   char* wsc = static_cast<char*>(workspace);
+  const int64_t stage = ffn_gemm_staging_bytes(T, H, W);
   return ffn_gemm_tc(x, x_dtype, T, H, wgu, gated ? 2 : 1, gated ? EPI_SILU_MUL : EPI_SILU, scale_dtype, W, h,
-                     h_dtype == PYRE_BF16, wsc + kHeaderBytes, ws_bytes - kHeaderBytes,
-                     reinterpret_cast<int*>(wsc + kHdrStatus), s);
+                     h_dtype, wsc + kHeaderBytes, stage, wsc + kHeaderBytes + stage, ws_bytes - kHeaderBytes - stage,
+                     reinterpret_cast<unsigned int*>(wsc + kHdrCntA), reinterpret_cast<int*>(wsc + kHdrStatus), s);
 }
 
 extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H,
@@ -73,8 +76,10 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_down(h, h_dtype, T, W, wd, scale_dtype, H, out, workspace, ws_bytes, comm, s);
   char* wsc = static_cast<char*>(workspace);
-  rc = ffn_gemm_tc(h, h_dtype, T, W, wd, 1, EPI_STORE, scale_dtype, H, out, 0, wsc + kHeaderBytes,
-                   ws_bytes - kHeaderBytes, reinterpret_cast<int*>(wsc + kHdrStatus), s);
+  const int64_t stage = ffn_gemm_staging_bytes(T, H, W);
+  rc = ffn_gemm_tc(h, h_dtype, T, W, wd, 1, EPI_STORE, scale_dtype, H, out, PYRE_F32, wsc + kHeaderBytes, stage,
+                   wsc + kHeaderBytes + stage, ws_bytes - kHeaderBytes - stage,
+                   reinterpret_cast<unsigned int*>(wsc + kHdrCntA), reinterpret_cast<int*>(wsc + kHdrStatus), s);
   const bool tp = comm != nullptr && comm->world > 1;
   if (rc || !tp) return rc;
   return allreduce_sum_f32(comm, out, static_cast<int64_t>(T) * H, s);

@@ -185,8 +185,9 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   const int td = T < PYRE_FUSED_REDUCE_MAX_T ? T : PYRE_FUSED_REDUCE_MAX_T;
   int64_t need = decode_ws_bytes(td, H, W, 2);
   if (T > PYRE_FUSED_REDUCE_MAX_T) {
-    const int64_t stage = kHeaderBytes + align256(static_cast<int64_t>(T) * (H > W ? H : W) * 2);
-    if (stage > need) need = stage;
+    const int64_t pg = ffn_gemm_partial_bytes(T, W, 2), pd = ffn_gemm_partial_bytes(T, H, 1);
+    const int64_t gemm = kHeaderBytes + ffn_gemm_staging_bytes(T, H, W) + (pg > pd ? pg : pd);
+    if (gemm > need) need = gemm;
   }
   *bytes = need;
   return PYRE_OK;

@@ -134,7 +134,14 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
                      const void* ws, int64_t ws_bytes, const char* fn);
 // Streaming-kernel forms of the two-call entry points for T <= 4 (defined in ffn_decode.cu).
 int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
-                void* out, int out_bf16, void* staging, int64_t staging_bytes, int* status, cudaStream_t s);
+                void* out, int out_dtype, void* staging, int64_t staging_bytes, void* partial, int64_t partial_bytes,
+                unsigned int* counters, int* status, cudaStream_t s);
+int64_t ffn_gemm_partial_bytes(int T, int N, int nmat);
+// Workspace regions of the T > 4 path after the header: f16 staging of the activations,
+// then split-K partial tiles.
+inline int64_t ffn_gemm_staging_bytes(int T, int H, int W) {
+  return (static_cast<int64_t>(T) * (H > W ? H : W) * 2 + 255) / 256 * 256;
+}
 int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, int scale_dtype, int W,
                       void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s);
 int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,

@@ -1,5 +1,5 @@
 // sm_100a tensor-core (tcgen05) building blocks: tensor-memory allocation, shared-memory
-// matrix descriptors, the instruction descriptor of a bf16 x bf16 -> f32 MMA, MMA issue and
+// matrix descriptors, the instruction descriptor of an f16 x f16 -> f32 MMA, MMA issue and
 // completion, and tensor-memory loads. Written against the PTX ISA for tcgen05; the field
 // positions of the descriptors follow the sm_100 descriptor formats.
 #pragma once
@@ -58,13 +58,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
-// Instruction descriptor, kind::f16: D f32, A and B bf16, A K-major, B MN-major, M x N.
+// Instruction descriptor, kind::f16: D f32, A and B f16, A K-major, B MN-major, M x N.
 template <int M, int N>
-__host__ __device__ constexpr uint32_t idesc_bf16_f32_kmaj_mnmaj() {
+__host__ __device__ constexpr uint32_t idesc_f16_f32_kmaj_mnmaj() {
   static_assert(M == 128 && N % 16 == 0 && N >= 16 && N <= 256, "M = 128, N in [16, 256] step 16");
   return (1u << 4)                                   // D format f32
-         | (1u << 7)                                 // A format bf16
-         | (1u << 10)                                // B format bf16
+         | (0u << 7)                                 // A format f16
+         | (0u << 10)                                // B format f16
          | (0u << 15)                                // A K-major
          | (1u << 16)                                // B MN-major
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
@@ -72,7 +72,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_kmaj_mnmaj() {
 }
 
 // D[tmem] (+)= A[smem] * B[smem]; accumulate == 0 overwrites D. Issued by one thread.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"

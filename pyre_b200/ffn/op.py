@@ -97,8 +97,9 @@ class FfnShardOp:
         self.workspace.zero_()
 
     def h_dtype(self, tokens: int) -> torch.dtype:
-        # decode keeps the intermediate in f32; larger T stores bf16 (tensor-core operand)
-        return torch.float32 if tokens <= N.PYRE_FUSED_REDUCE_MAX_T else torch.bfloat16
+        # decode keeps the intermediate in f32; larger T stores f16, the tensor-core operand
+        # type of the down GEMM
+        return torch.float32 if tokens <= N.PYRE_FUSED_REDUCE_MAX_T else torch.float16
 
     def __call__(self, x: torch.Tensor, gate: Q80Weight | None, up: Q80Weight, down: Q80Weight,
                  out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:

@@ -240,3 +240,25 @@ def test_decode_repeated_calls_and_status():
     for it, o in enumerate(outs):
         assert torch.equal(o, first[it % 3])
     assert op.status() == 0
+
+
+def test_prefill_split_k_deterministic():
+    """The tensor-core path (T > 4) splits K across CTAs when the tiles alone leave SMs idle;
+    the partial tiles are added in split order, so repeated calls are bit-identical and leave
+    the split counters at zero."""
+    from pyre_b200.ffn import FfnShardOp
+    rng = np.random.default_rng(13)
+    g, gd = make_weight((1024, 2048), rng, torch.float16)
+    u, ud = make_weight((1024, 2048), rng, torch.float16)
+    d, dd = make_weight((2048, 1024), rng, torch.float16)
+    op = FfnShardOp(1024, 2048, max_tokens=200)
+    x = bf16_round(rng.standard_normal((200, 1024)).astype(np.float32))
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    outs = [op(xt, g, u, d).clone() for _ in range(3)]
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    hdr = op.workspace[:32768].view(torch.int32)
+    assert int(hdr[2]) == 0
+    assert int(hdr[256:256 + 2048].abs().sum()) == 0
+    assert rel_err(outs[0].cpu().numpy(), offn.ffn_shard_f64(x, gd, ud, dd)) < TOL_BF16
