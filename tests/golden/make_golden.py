@@ -14,6 +14,15 @@ Run in a container that has the reference checkout (read-only) at /root/referenc
                          3-shard case on Q8_0-roundtripped weights.
 * partition_golden.json— reference ``AdaptivePartitioner`` / ``detect_drift``
                          (src/orchestrator/cluster.py:217-403) on fixed timing traces.
+* attn_golden.npz      — reference ``build_ulysses_attention_graph`` (src/attention/
+                         builder.py:27-65) through the numpy MAX stand-in, and
+                         ``RootNode._compute_attention`` / ``_compute_attention_decode``
+                         (src/orchestrator/root_node.py:250-314, :1009-1031) with the Mojo
+                         kernel module replaced by the numpy restatement of
+                         pyre_kernels.mojo in oracle/kernels.py (the compiled module is
+                         never loaded). These pin the reference's attention orchestration:
+                         concatenation order, layout, RoPE position, clipping, GQA, scale,
+                         causal and padding masks.
 
 Only this script touches /root/reference; tests read the fixtures.
 """
@@ -178,6 +187,102 @@ def make_partition() -> None:
     print("partition_golden.json written")
 
 
+class _KernelShim:
+    """Stands in for the pyre_kernels module: same call signatures (outputs written into
+    the ``result`` array), arithmetic from oracle/kernels.py."""
+
+    def __init__(self):
+        sys.path.insert(0, str(HERE.parent.parent))
+        from oracle import kernels
+        self.k = kernels
+
+    def softmax(self, x, out):
+        with np.errstate(invalid="ignore", over="ignore"):
+            out[...] = self.k.softmax(x)
+        return out
+
+    def apply_rope(self, x, out, theta, start_pos, frac):
+        out[...] = self.k.apply_rope(x, float(theta), int(start_pos), float(frac))
+        return out
+
+    def rms_norm(self, x, w, out):
+        out[...] = self.k.rms_norm(x, w)
+        return out
+
+    def apply_v_norm(self, v, out):
+        v64 = v.astype(np.float64)
+        out[...] = (v64 / np.sqrt(np.sum(v64 * v64, axis=-1, keepdims=True) / v.shape[-1] + 1e-6)).astype(np.float32)
+        return out
+
+    def matmul_f32(self, a, b, out):
+        out[...] = (a.astype(np.float32) @ b.astype(np.float32)).astype(np.float32)
+        return out
+
+
+def make_attention() -> None:
+    import types
+    import src.orchestrator.root_node as rn
+    from src.attention.builder import ShardSpec, build_ulysses_attention_graph
+    from max.engine import InferenceSession
+    from max.graph import DeviceRef
+    from max.driver import CPU
+
+    rn._PYRE_KERNELS = _KernelShim()
+    out = {}
+    # (1) QKV projection graph: 2 seq shards, GQA 8 q heads / 2 kv heads, hd 16
+    H, nq, nkv, hd, S = 64, 8, 2, 16, 10
+    rng = np.random.default_rng(21)
+    x = bf16_round(rng.standard_normal((1, S, H)).astype(np.float32))
+    wq = bf16_round(rng.standard_normal((H, nq * hd)).astype(np.float32) * 0.1)
+    wk = bf16_round(rng.standard_normal((H, nkv * hd)).astype(np.float32) * 0.1)
+    wv = bf16_round(rng.standard_normal((H, nkv * hd)).astype(np.float32) * 0.1)
+    for i, (a, b) in enumerate(((0, 6), (6, 10))):
+        shard = ShardSpec(0, nq * hd, a, b, nq, nkv, 0, 0)
+        g = build_ulysses_attention_graph(shard, H, nq, nkv, hd, DeviceRef.CPU(), full_q_weights=True)
+        model = InferenceSession(devices=[CPU()]).load(g)
+        q, k, v = (t.to_numpy() for t in model.execute(np.ascontiguousarray(x[:, a:b]), wq, wk, wv))
+        out[f"proj{i}__q"], out[f"proj{i}__k"], out[f"proj{i}__v"] = q, k, v
+    out["proj__x"], out["proj__wq"], out["proj__wk"], out["proj__wv"] = x, wq, wk, wv
+    out["proj__dims"] = np.array([H, nq, nkv, hd, S], dtype=np.int64)
+
+    # (2) prefill attention over 2 nodes: seq-concatenated, and head-concatenated (GQA split)
+    cfg = types.SimpleNamespace(head_dim=hd, n_heads=nq, n_kv_heads=nkv, rope_theta=10000.0)
+    fake = types.SimpleNamespace(config=cfg, worker_ids=[1], _apply_rope=rn.RootNode._apply_rope,
+                                 _softmax=rn.RootNode._softmax, _apply_v_norm=rn.RootNode._apply_v_norm)
+    cases = [("seq_rope1", False, 1.0, False), ("seq_rope05_vnorm", False, 0.5, True), ("head_rope1", True, 1.0, False)]
+    for ci, (name, by_head, frac, vn) in enumerate(cases):
+        rng = np.random.default_rng(40 + ci)
+        if by_head:   # each node holds all S positions of half the heads
+            parts = [tuple((rng.standard_normal((1, S, n, hd)) * 3).astype(np.float32) for n in (nq // 2, nkv // 2, nkv // 2))
+                     for _ in range(2)]
+        else:         # each node holds a slice of the sequence with all heads
+            parts = [tuple((rng.standard_normal((1, s, n, hd)) * 3).astype(np.float32) for n in (nq, nkv, nkv))
+                     for s in (6, 4)]
+        all_qkv = {0: parts[0], 1: parts[1]}
+        props = {"rope_fraction": frac, "use_v_norm": vn}
+        with np.errstate(invalid="ignore", over="ignore"):
+            attn = rn.RootNode._compute_attention(fake, all_qkv, 0, None, None, props, by_head)
+        for i in range(2):
+            for j, t in enumerate("qkv"):
+                out[f"{name}__n{i}_{t}"] = parts[i][j]
+        out[f"{name}__attn"] = attn
+        out[f"{name}__cfg"] = np.array([int(by_head), int(vn)], dtype=np.int64)
+        out[f"{name}__frac"] = np.array(frac, dtype=np.float64)
+
+    # (3) decode attention over a cache with a padded prefill (positions 5..7 masked)
+    rng = np.random.default_rng(33)
+    t = 12
+    q = (rng.standard_normal((1, nq, 1, hd)) * 2).astype(np.float32)
+    k = (rng.standard_normal((1, nkv, t, hd)) * 2).astype(np.float32)
+    v = (rng.standard_normal((1, nkv, t, hd)) * 2).astype(np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        dec = rn.RootNode._compute_attention_decode(q, k, v, 0, prefill_real=5, prefill_max_seq=8)
+    out["decode__q"], out["decode__k"], out["decode__v"], out["decode__attn"] = q, k, v, dec
+    out["decode__mask"] = np.array([5, 8], dtype=np.int64)
+    np.savez_compressed(HERE / "attn_golden.npz", **out)
+    print("attn_golden.npz written")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -192,6 +297,7 @@ def main() -> None:
     with contextlib.redirect_stdout(io.StringIO()):
         make_partition()
     print("partition_golden.json written")
+    make_attention()
 
 
 if __name__ == "__main__":
