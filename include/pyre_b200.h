@@ -182,6 +182,53 @@ PYRE_API int pyre_comm_check(pyre_comm_t* comm, int* status, void* stream);
  * all-gather through peer memory), rank order 0..world-1. n <= max_tokens * hidden. */
 PYRE_API int pyre_allreduce_sum_f32(pyre_comm_t* comm, float* buf, int64_t n, void* stream);
 
+/* ---- attention path ------------------------------------------------------------------
+ * out[T, N] (f32) = x[T, K] @ W, W a packed single Q8_0 matrix [K, N] (pyre_q80_pack with
+ * M = 1): the Q, K, V and O projections of src/attention/builder.py:56-58 (x @ Wq ...) and
+ * root_node.py:866-897 (matmul_f32 of the normed token with the projection weights), on the
+ * Q8_0 weights a reference worker holds. x: f32 or bf16 (f16 too for T > 4). workspace:
+ * zero-initialised, pyre_ffn_workspace_bytes(T, K, N) bytes. */
+PYRE_API int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N,
+                             float* out, void* workspace, int64_t ws_bytes, void* stream);
+
+/* out[r, :] = f32(x[r, :] * rstd_r * w) with rstd_r = 1 / sqrt(mean(x[r, :]^2) + eps), the sum
+ * of squares in f64 (pyre_kernels.mojo:18-35; the reference uses eps = 1e-6). x, out: f32
+ * [rows, H]; w: f32 [H]. */
+PYRE_API int pyre_rms_norm(const float* x, int rows, int H, const float* w, double eps, float* out, void* stream);
+
+/* Softmax over the last axis of an f32 [rows, cols] matrix, max initialised to -1e10 and
+ * exp(x - max) * (1 / sum) (pyre_kernels.mojo:39-58). */
+PYRE_API int pyre_softmax_rows(const float* x, int64_t rows, int cols, float* out, void* stream);
+
+/* RoPE + clip + KV-cache append for T new tokens at positions start_pos..start_pos+T-1
+ * (pyre_kernels.mojo:62-96 apply_rope, root_node.py:283-290 and :905-929): q [T, nq, hd] and
+ * k, v [T, nkv, hd] f32 with row strides q_stride / kv_stride elements (one fused QKV
+ * projection output can be passed as three offset pointers). q and k are rotated over the
+ * first int(hd * rope_fraction) dims with freq_i = 1 / theta^(2i/dims) (f64, as the
+ * reference), q, k and v clipped to +-1000; q_out f16 [nq, T, hd]; k, v appended to the f16
+ * caches [nkv, max_t, hd]. */
+PYRE_API int pyre_rope_kv_append(const float* q, const float* k, const float* v, int64_t q_stride,
+                                 int64_t kv_stride, int T, int nq, int nkv, int hd, int start_pos, double theta,
+                                 double rope_fraction, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                                 int max_t, void* stream);
+
+/* Causal prefill attention over positions 0..T-1 of the caches (root_node.py:292-307:
+ * GQA q head h -> kv head h / (nq / nkv), q k^T / sqrt(hd), -inf above the diagonal, softmax,
+ * probs @ v), f16 operands, f32 accumulation. q: f16 [nq, T, hd] (pyre_rope_kv_append);
+ * out: f32 [T, nq * hd]. hd: 64 or 128. */
+PYRE_API int pyre_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int T, int nq,
+                               int nkv, int hd, int max_t, float* out, void* stream);
+
+/* Decode attention of one query token over cache positions 0..t-1 (root_node.py:1009-1031):
+ * positions in [mask_lo, mask_hi) are masked (the reference's padded prefill). q: f16
+ * [nq, hd]; out: f32 [nq * hd]. Split over the cache (flash-decoding), chunks combined in
+ * order (deterministic). workspace: zero-initialised once, pyre_attn_decode_workspace_bytes
+ * bytes, reused call after call on one stream. nq / nkv <= 8, hd 64 or 128. */
+PYRE_API int pyre_attn_decode_workspace_bytes(int nq, int nkv, int hd, int t, int64_t* bytes);
+PYRE_API int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int t, int nq,
+                              int nkv, int hd, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
+                              int64_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

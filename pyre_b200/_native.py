@@ -66,6 +66,14 @@ _SIGNATURES = {
     "pyre_comm_set_timeout_ns": [_vp, ctypes.c_uint64],
     "pyre_comm_check": [_vp, ctypes.POINTER(_i), _vp],
     "pyre_allreduce_sum_f32": [_vp, _vp, _c_i64, _vp],
+    "pyre_q80_linear": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp],
+    "pyre_rms_norm": [_vp, _i, _i, _vp, ctypes.c_double, _vp, _vp],
+    "pyre_softmax_rows": [_vp, _c_i64, _i, _vp, _vp],
+    "pyre_rope_kv_append": [_vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _i, ctypes.c_double, ctypes.c_double,
+                            _vp, _vp, _vp, _i, _vp],
+    "pyre_attn_prefill": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp],
+    "pyre_attn_decode_workspace_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
+    "pyre_attn_decode": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _c_i64, _vp],
 }
 
 _lock = threading.Lock()

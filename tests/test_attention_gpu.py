@@ -1,0 +1,167 @@
+"""Attention-path kernels on the GPU against the attention oracle (oracle/attention.py,
+oracle/kernels.py), which is pinned to the reference's own code by tests/test_attention_oracle.py.
+
+Tolerances (max |out - ref| / max |ref|): RMSNorm and softmax 1e-6 (f32 / f64 arithmetic like
+the reference); the Q8_0 projections 1e-4 (f32 path, T <= 4) and 1e-2 (f16 tensor-core path);
+RoPE + clip 2e-3 (the rotated values are stored as f16); attention 5e-3 (f16 q/k/v and
+probabilities, f32 accumulation). The path's budget is 2e-2.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import attention as OA
+from oracle import kernels as OK
+from oracle import q80 as oq80
+
+pytestmark = pytest.mark.gpu
+
+TOL_ATTN = 5e-3
+
+
+def rel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def test_rms_norm_and_softmax():
+    from pyre_b200.attention import rms_norm, softmax
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((7, 4096)) * 3).astype(np.float32)
+    w = rng.standard_normal(4096).astype(np.float32)
+    got = rms_norm(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()).cpu().numpy()
+    assert rel(got, OK.rms_norm(x, w)) < 1e-6
+    s = (rng.standard_normal((5, 37, 129)) * 4).astype(np.float32)
+    s[0, 0, 5:] = -np.inf
+    got = softmax(torch.from_numpy(s).cuda()).cpu().numpy()
+    assert rel(got, OK.softmax(s)) < 1e-6
+
+
+@pytest.mark.parametrize("T", [1, 3, 37])
+def test_q80_linear(T):
+    from pyre_b200.attention import Q80Linear
+    from pyre_b200.quantizer import Q80Weight
+    rng = np.random.default_rng(T)
+    w = (rng.standard_normal((576, 384)) * 0.05).astype(np.float32)
+    q, s, sh = oq80.quantize_q80(w)
+    s = s.astype(np.float16).astype(np.float32)
+    wd = oq80.dequantize_q80(q, s, sh)
+    lin = Q80Linear(Q80Weight.from_tuple(("q8", q, s, sh), scale_dtype=torch.float16), max_tokens=T)
+    x = rng.standard_normal((T, 576)).astype(np.float32)
+    out = lin(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = x.astype(np.float64) @ wd.astype(np.float64)
+    assert rel(out, ref) < (1e-4 if T <= 4 else 1e-2)
+
+
+def _qkv(rng, T, nq, nkv, hd, scale=2.0):
+    q = (rng.standard_normal((T, nq * hd)) * scale).astype(np.float32)
+    k = (rng.standard_normal((T, nkv * hd)) * scale).astype(np.float32)
+    v = (rng.standard_normal((T, nkv * hd)) * scale).astype(np.float32)
+    return q, k, v
+
+
+def _as4(x, T, n, hd):
+    return x.reshape(1, T, n, hd)
+
+
+@pytest.mark.parametrize("T,nq,nkv,hd,frac,theta", [(70, 8, 2, 64, 1.0, 1e4), (130, 4, 4, 128, 1.0, 1e6),
+                                                     (200, 32, 8, 128, 1.0, 5e5), (65, 6, 2, 64, 0.5, 1e4)])
+def test_prefill_attention_vs_oracle(T, nq, nkv, hd, frac, theta):
+    from pyre_b200.attention import AttentionOp
+    rng = np.random.default_rng(T + nq)
+    q, k, v = _qkv(rng, T, nq, nkv, hd)
+    op = AttentionOp(nq, nkv, hd, max_t=T + 8, rope_theta=theta, rope_fraction=frac)
+    out = op.prefill(*(torch.from_numpy(a).cuda() for a in (q, k, v))).cpu().numpy()
+    ref = OA.compute_attention([(_as4(q, T, nq, hd), _as4(k, T, nkv, hd), _as4(v, T, nkv, hd))], nq, nkv, frac, theta)
+    assert rel(out, ref[0]) < TOL_ATTN
+    # the cache holds the rotated, clipped keys (f16)
+    kr = np.clip(OK.apply_rope(_as4(k, T, nkv, hd).transpose(0, 2, 1, 3), theta, 0, frac), -1000, 1000)[0]
+    assert rel(op.cache.k[:, :T].float().cpu().numpy(), kr) < 2e-3
+
+
+def test_prefill_golden_cases():
+    """The reference's own prefill attention cases (sequence- and head-concatenated nodes)."""
+    from pyre_b200.attention import AttentionOp
+    z = np.load(GOLDEN / "attn_golden.npz")
+    _, nq, nkv, hd, _ = (int(v) for v in z["proj__dims"])
+    for name in ("seq_rope1", "head_rope1"):
+        by_head = bool(z[f"{name}__cfg"][0])
+        axis = 2 if by_head else 1
+        q, k, v = (np.concatenate([z[f"{name}__n{i}_{t}"] for i in range(2)], axis=axis) for t in "qkv")
+        T = q.shape[1]
+        # The golden heads have hd = 16; the kernels take 64 or 128. Zero-pad each head to 64:
+        # rope_fraction 16/64 rotates exactly the pairs (i, i + 8), i < 8, with the golden's
+        # freq_i = 1 / theta^(2i/16); padded dims add nothing to q.k or to the output, and q is
+        # doubled so that 1/sqrt(64) scales the scores like the golden's 1/sqrt(16).
+        pad = 64 - hd
+        op = AttentionOp(nq, nkv, 64, max_t=T, rope_theta=10000.0, rope_fraction=float(hd) / 64.0)
+        qp, kp, vp = (np.concatenate([a, np.zeros(a.shape[:-1] + (pad,), np.float32)], axis=-1) for a in (q, k, v))
+        qp = qp * 2.0
+        out = op.prefill(*(torch.from_numpy(np.ascontiguousarray(a.reshape(T, -1))).cuda() for a in (qp, kp, vp)))
+        out = out.cpu().numpy()
+        out = out.reshape(T, nq, 64)[:, :, :hd].reshape(T, nq * hd)
+        assert rel(out, z[f"{name}__attn"][0]) < TOL_ATTN, name
+
+
+@pytest.mark.parametrize("nq,nkv,hd,t0", [(8, 2, 64, 37), (32, 8, 128, 300), (4, 4, 128, 1)])
+def test_decode_steps_vs_oracle(nq, nkv, hd, t0):
+    """Prefill t0 tokens, then decode 4 tokens one by one; each step equals the oracle's
+    decode step on the same cache."""
+    from pyre_b200.attention import AttentionOp
+    rng = np.random.default_rng(nq * hd + t0)
+    op = AttentionOp(nq, nkv, hd, max_t=t0 + 8, rope_theta=1e6)
+    q, k, v = _qkv(rng, t0, nq, nkv, hd)
+    op.prefill(*(torch.from_numpy(a).cuda() for a in (q, k, v)))
+    kc = np.clip(OK.apply_rope(_as4(k, t0, nkv, hd).transpose(0, 2, 1, 3), 1e6, 0, 1.0), -1000, 1000)
+    vc = np.clip(_as4(v, t0, nkv, hd).transpose(0, 2, 1, 3), -1000, 1000)
+    for step in range(4):
+        qn, kn, vn = _qkv(rng, 1, nq, nkv, hd)
+        out = op.decode(*(torch.from_numpy(a).cuda() for a in (qn, kn, vn))).cpu().numpy()
+        ref, kc, vc = OA.decode_step(qn.reshape(1, nq, 1, hd), kn.reshape(1, nkv, 1, hd), vn.reshape(1, nkv, 1, hd),
+                                     kc, vc, 1.0, 1e6)
+        assert rel(out, ref[0]) < TOL_ATTN, step
+
+
+def test_decode_padding_mask_golden():
+    """The reference's decode case with a padded prefill (positions 5..7 masked)."""
+    from pyre_b200 import _device as D, _native as N
+    z = np.load(GOLDEN / "attn_golden.npz")
+    q, k, v = z["decode__q"], z["decode__k"], z["decode__v"]
+    lo, hi = (int(x) for x in z["decode__mask"])
+    nq, nkv, t, hd = q.shape[1], k.shape[1], k.shape[2], q.shape[3]
+    pad = 64 - hd   # dot products and weighted sums are unchanged by zero padding of hd
+    qh = torch.from_numpy(np.pad(q[0, :, 0], ((0, 0), (0, pad)))).cuda().half().contiguous()
+    kh = torch.from_numpy(np.pad(k[0], ((0, 0), (0, 0), (0, pad)))).cuda().half().contiguous()
+    vh = torch.from_numpy(np.pad(v[0], ((0, 0), (0, 0), (0, pad)))).cuda().half().contiguous()
+    b = ctypes.c_int64(0)
+    N.call("pyre_attn_decode_workspace_bytes", nq, nkv, 64, t, ctypes.byref(b))
+    ws = torch.zeros(b.value, dtype=torch.uint8, device="cuda")
+    out = torch.empty(nq * 64, device="cuda")
+    # the golden's scale is 1/sqrt(16): scale q by sqrt(64)/sqrt(16) so 1/sqrt(64) gives the same
+    qh = (qh.float() * 2.0).half()
+    N.call("pyre_attn_decode", D.ptr(qh), D.ptr(kh), D.ptr(vh), t, nq, nkv, 64, t, lo, hi, D.ptr(out), D.ptr(ws),
+           ws.numel(), D.stream_ptr())
+    got = out.reshape(nq, 64)[:, :hd].reshape(-1).cpu().numpy()
+    assert rel(got, z["decode__attn"][0, 0]) < TOL_ATTN
+
+
+def test_ulysses_builder_projection():
+    """build_ulysses_attention_graph through the session, on the reference's golden shards."""
+    from pyre_b200.attention import ShardSpec, build_ulysses_attention_graph
+    from pyre_b200.engine import DeviceRef, InferenceSession
+    z = np.load(GOLDEN / "attn_golden.npz")
+    H, nq, nkv, hd, S = (int(v) for v in z["proj__dims"])
+    for i, (a, b) in enumerate(((0, 6), (6, 10))):
+        g = build_ulysses_attention_graph(ShardSpec(0, nq * hd, a, b, nq, nkv, 0, 0), H, nq, nkv, hd,
+                                          DeviceRef.GPU(0), full_q_weights=True)
+        q, k, v = InferenceSession().load(g).execute(np.ascontiguousarray(z["proj__x"][:, a:b]), z["proj__wq"],
+                                                     z["proj__wk"], z["proj__wv"])
+        for t, got in zip("qkv", (q, k, v)):
+            ref = z[f"proj{i}__{t}"]
+            assert got.shape == ref.shape
+            # weights go through Q8_0 (as on a reference worker): budget 2e-2
+            assert rel(got.to_numpy(), ref) < 2e-2
