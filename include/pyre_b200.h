@@ -229,6 +229,29 @@ PYRE_API int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const 
                               int nkv, int hd, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
                               int64_t ws_bytes, void* stream);
 
+/* ---- Ulysses sequence parallelism over NVLink (one process per GPU, P <= 16) ----------
+ * Replaces the gather of every node's q/k/v at the root over TCP and the full-sequence
+ * attention there (src/orchestrator/root_node.py:250-314; Ulysses mode :110): rank r owns
+ * tokens [r*S/P, (r+1)*S/P) and heads [r*nq/P, ..) / [r*nkv/P, ..). Each rank allocates one
+ * buffer of pyre_ulysses_buffer_bytes() with pyre_comm_alloc() (zeroed) and maps its peers'
+ * (pyre_comm_open_peer); bufs[i] is rank i's buffer as seen from this process. Per call,
+ * on one stream: pyre_ulysses_rope_scatter (RoPE at the tokens' global positions, clip, and
+ * NVLink stores of every head into its owner's buffer), pyre_ulysses_barrier(phase 0),
+ * pyre_ulysses_attention (causal attention of the owned heads over the whole sequence, each
+ * output row stored into its token owner's buffer), pyre_ulysses_barrier(phase 1), then
+ * pyre_ulysses_finish (sync, status, and the rank's [S/P, nq*hd] f32 output). Barrier waits
+ * are bounded by timeout_ns and report PYRE_ETIMEOUT through pyre_ulysses_finish. */
+PYRE_API int pyre_ulysses_buffer_bytes(int S, int P, int nq, int nkv, int hd, int64_t* bytes);
+PYRE_API int pyre_ulysses_rope_scatter(void* const* bufs, int rank, int P, const float* q, const float* k,
+                                       const float* v, int64_t q_stride, int64_t kv_stride, int S, int nq, int nkv,
+                                       int hd, double theta, double rope_fraction, void* stream);
+PYRE_API int pyre_ulysses_barrier(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd, int phase,
+                                  uint64_t timeout_ns, void* stream);
+PYRE_API int pyre_ulysses_attention(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd,
+                                    void* stream);
+PYRE_API int pyre_ulysses_finish(void* local_buf, int P, int S, int nq, int nkv, int hd, float* out, int* status,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,12 @@ _SIGNATURES = {
     "pyre_attn_prefill": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp],
     "pyre_attn_decode_workspace_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_attn_decode": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _c_i64, _vp],
+    "pyre_ulysses_buffer_bytes": [_i, _i, _i, _i, _i, ctypes.POINTER(_c_i64)],
+    "pyre_ulysses_rope_scatter": [_vp, _i, _i, _vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, ctypes.c_double,
+                                  ctypes.c_double, _vp],
+    "pyre_ulysses_barrier": [_vp, _i, _i, _i, _i, _i, _i, _i, ctypes.c_uint64, _vp],
+    "pyre_ulysses_attention": [_vp, _i, _i, _i, _i, _i, _i, _vp],
+    "pyre_ulysses_finish": [_vp, _i, _i, _i, _i, _i, _vp, ctypes.POINTER(_i), _vp],
 }
 
 _lock = threading.Lock()

@@ -293,6 +293,10 @@ struct PrefillParams {
   float* out;          // [T, nq * hd]
   int T, nq, nkv, max_t;
   float scale_log2;    // log2(e) / sqrt(hd)
+  // Ulysses output scatter (scatter != 0): row t goes to rank t / rows_per_rank, into its
+  // [rows_per_rank, nq_total * hd] f32 buffer at head column head_off + h
+  int scatter, rows_per_rank, head_off, nq_total;
+  float* out_peers[16];
 };
 
 template <int HD>
@@ -437,16 +441,24 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillParams p
     l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
   }
   const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  const int64_t ld = static_cast<int64_t>(p.nq) * HD;
+  float* dst0 = nullptr;
+  float* dst1 = nullptr;
+  if (!p.scatter) {
+    const int64_t ld = static_cast<int64_t>(p.nq) * HD;
+    dst0 = p.out + row0 * ld + static_cast<int64_t>(h) * HD;
+    dst1 = p.out + row1 * ld + static_cast<int64_t>(h) * HD;
+  } else {
+    // NVLink peer stores into the owning rank's output rows
+    const int64_t ld = static_cast<int64_t>(p.nq_total) * HD;
+    const int64_t hc = static_cast<int64_t>(p.head_off + h) * HD;
+    if (row0 < p.T) dst0 = p.out_peers[row0 / p.rows_per_rank] + (row0 % p.rows_per_rank) * ld + hc;
+    if (row1 < p.T) dst1 = p.out_peers[row1 / p.rows_per_rank] + (row1 % p.rows_per_rank) * ld + hc;
+  }
 #pragma unroll
   for (int j = 0; j < HD / 8; ++j) {
     const int d = j * 8 + (lane & 3) * 2;
-    if (row0 < p.T)
-      *reinterpret_cast<float2*>(p.out + row0 * ld + static_cast<int64_t>(h) * HD + d) =
-          make_float2(o[j][0] * i0, o[j][1] * i0);
-    if (row1 < p.T)
-      *reinterpret_cast<float2*>(p.out + row1 * ld + static_cast<int64_t>(h) * HD + d) =
-          make_float2(o[j][2] * i1, o[j][3] * i1);
+    if (row0 < p.T) *reinterpret_cast<float2*>(dst0 + d) = make_float2(o[j][0] * i0, o[j][1] * i0);
+    if (row1 < p.T) *reinterpret_cast<float2*>(dst1 + d) = make_float2(o[j][2] * i1, o[j][3] * i1);
   }
 }
 
@@ -544,6 +556,26 @@ extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, cons
   return PYRE_OK;
 }
 
+namespace pyre {
+namespace attn {
+int launch_prefill(PrefillParams p, int hd, cudaStream_t s) {
+  dim3 grid((p.T + kPM - 1) / kPM, p.nq);
+  int rc;
+  if (hd == 64) {
+    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<64>), PrefillSmem<64>::kBytes);
+    if (rc) return rc;
+    attn_prefill_kernel<64><<<grid, 128, PrefillSmem<64>::kBytes, s>>>(p);
+  } else {
+    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<128>), PrefillSmem<128>::kBytes);
+    if (rc) return rc;
+    attn_prefill_kernel<128><<<grid, 128, PrefillSmem<128>::kBytes, s>>>(p);
+  }
+  PYRE_LAUNCH_CHECK("attn_prefill_kernel");
+  return PYRE_OK;
+}
+}  // namespace attn
+}  // namespace pyre
+
 extern "C" int pyre_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int T, int nq,
                                  int nkv, int hd, int max_t, float* out, void* stream) {
   PYRE_CHECK_ARG(q && k_cache && v_cache && out, "pyre_attn_prefill: null pointer");
@@ -562,18 +594,223 @@ extern "C" int pyre_attn_prefill(const uint16_t* q, const uint16_t* k_cache, con
   p.nkv = nkv;
   p.max_t = max_t;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
-  dim3 grid((T + kPM - 1) / kPM, nq);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (hd == 64) {
-    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<64>), PrefillSmem<64>::kBytes);
-    if (rc) return rc;
-    attn_prefill_kernel<64><<<grid, 128, PrefillSmem<64>::kBytes, s>>>(p);
-  } else {
-    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<128>), PrefillSmem<128>::kBytes);
-    if (rc) return rc;
-    attn_prefill_kernel<128><<<grid, 128, PrefillSmem<128>::kBytes, s>>>(p);
+  return launch_prefill(p, hd, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// Ulysses sequence parallelism inside one box (P ranks, one GPU each). Rank r owns tokens
+// [r*S/P, (r+1)*S/P) and, for attention, q heads [r*nq/P, ..) and kv heads [r*nkv/P, ..).
+// Every rank holds one buffer (allocated with pyre_comm_alloc, mapped by its peers):
+//   qf  f16 [nq/P, S, hd]      rotated queries of the owned heads, whole sequence
+//   kf  f16 [nkv/P, S, hd]     KV cache of the owned kv heads, whole sequence
+//   vf  f16 [nkv/P, S, hd]
+//   ao  f32 [S/P, nq*hd]       attention output of the owned tokens, all heads
+//   flags u32 [2][16], epoch, status (the last two only used locally)
+// The QKV "all-gather" is fused into RoPE: each rank rotates its tokens and stores every
+// head straight into the owner's qf / kf / vf over NVLink. The output "scatter" is fused
+// into the attention epilogue, which stores each row into the owner's ao. A flag barrier
+// (release / acquire at system scope, bounded waits) separates the phases.
+namespace pyre {
+namespace attn {
+
+constexpr int kUlyMaxWorld = 16;
+
+struct UlyLayout {
+  int64_t q, k, v, ao, flags, epoch, status, total;
+};
+
+inline int64_t a256(int64_t b) { return (b + 255) / 256 * 256; }
+
+UlyLayout uly_layout(int S, int P, int nq, int nkv, int hd) {
+  UlyLayout L{};
+  L.q = 0;
+  L.k = L.q + a256(static_cast<int64_t>(nq / P) * S * hd * 2);
+  L.v = L.k + a256(static_cast<int64_t>(nkv / P) * S * hd * 2);
+  L.ao = L.v + a256(static_cast<int64_t>(nkv / P) * S * hd * 2);
+  L.flags = L.ao + a256(static_cast<int64_t>(S / P) * nq * hd * 4);
+  L.epoch = L.flags + 2 * kUlyMaxWorld * 4;
+  L.status = L.epoch + 4;
+  L.total = a256(L.status + 4);
+  return L;
+}
+
+struct UlyPeers {
+  char* buf[kUlyMaxWorld];
+};
+
+__global__ void __launch_bounds__(256) ulysses_rope_scatter_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, int64_t q_stride,
+    int64_t kv_stride, int S_local, int seq_off, int S, int nq, int nkv, int hd, double theta, int dims, int P,
+    UlyPeers peers, int64_t off_q, int64_t off_k, int64_t off_v) {
+  __shared__ float cs[kRopeMaxHalf], sn[kRopeMaxHalf];
+  const int t = blockIdx.x;
+  const int pos = seq_off + t;
+  const int half = dims >= 2 ? dims / 2 : 0;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    const double freq = 1.0 / pow(theta, static_cast<double>(2 * j) / static_cast<double>(dims));
+    const double ang = static_cast<double>(pos) * freq;
+    cs[j] = static_cast<float>(cos(ang));
+    sn[j] = static_cast<float>(sin(ang));
   }
-  PYRE_LAUNCH_CHECK("attn_prefill_kernel");
+  __syncthreads();
+  const int qpr = nq / P, kpr = nkv / P;
+  for (int e = threadIdx.x; e < (nq + nkv) * hd; e += blockDim.x) {
+    const int hh = e / hd, i = e - hh * hd;
+    const bool is_q = hh < nq;
+    const int h = is_q ? hh : hh - nq;
+    const float* src = is_q ? q + t * q_stride + static_cast<int64_t>(h) * hd : k + t * kv_stride + static_cast<int64_t>(h) * hd;
+    float r;
+    if (i < 2 * half) {
+      const int jj = i < half ? i : i - half;
+      const float x1 = src[jj], x2 = src[jj + half];
+      r = i < half ? x1 * cs[jj] - x2 * sn[jj] : x1 * sn[jj] + x2 * cs[jj];
+    } else {
+      r = src[i];
+    }
+    const __half hv = __float2half_rn(fminf(fmaxf(r, -1000.f), 1000.f));
+    const int owner = is_q ? h / qpr : h / kpr;
+    const int hl = is_q ? h - owner * qpr : h - owner * kpr;
+    __half* dst = reinterpret_cast<__half*>(peers.buf[owner] + (is_q ? off_q : off_k));
+    dst[(static_cast<int64_t>(hl) * S + pos) * hd + i] = hv;
+  }
+  for (int e = threadIdx.x; e < nkv * hd; e += blockDim.x) {
+    const int h = e / hd, i = e - h * hd;
+    const float x = v[t * kv_stride + static_cast<int64_t>(h) * hd + i];
+    const int owner = h / kpr, hl = h - owner * kpr;
+    __half* dst = reinterpret_cast<__half*>(peers.buf[owner] + off_v);
+    dst[(static_cast<int64_t>(hl) * S + pos) * hd + i] = __float2half_rn(fminf(fmaxf(x, -1000.f), 1000.f));
+  }
+}
+
+// Phase barrier: publish this rank's flag to every peer (after a system-scope fence that
+// orders the preceding kernels' peer stores), then wait (bounded) for every peer's flag.
+// The epoch of a call is the local epoch word + 1; phase 1 stores it back.
+__global__ void ulysses_barrier_kernel(UlyPeers peers, int rank, int P, int phase, int64_t off_flags,
+                                       int64_t off_epoch, int64_t off_status, uint64_t timeout_ns) {
+  char* mine = peers.buf[rank];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(mine + off_epoch) + 1u;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < P) {
+    uint32_t* f = reinterpret_cast<uint32_t*>(peers.buf[threadIdx.x] + off_flags) + phase * kUlyMaxWorld + rank;
+    st_release_sys(f, epoch);
+  }
+  if (threadIdx.x < P) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + off_flags) + phase * kUlyMaxWorld + threadIdx.x;
+    if (!wait_flag_eq(f, epoch, timeout_ns)) atomicExch(reinterpret_cast<int*>(mine + off_status), PYRE_ETIMEOUT);
+  }
+  __syncthreads();
+  if (phase == 1 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(mine + off_epoch) = epoch;
+}
+
+int uly_peers(void* const* bufs, int P, UlyPeers* out) {
+  PYRE_CHECK_ARG(bufs != nullptr && P >= 1 && P <= kUlyMaxWorld, "Ulysses: 1..16 ranks and their buffers");
+  for (int i = 0; i < P; ++i) {
+    PYRE_CHECK_ARG(bufs[i] != nullptr, "Ulysses: null peer buffer");
+    out->buf[i] = static_cast<char*>(bufs[i]);
+  }
+  return PYRE_OK;
+}
+
+int uly_check_shape(int S, int P, int nq, int nkv, int hd) {
+  PYRE_CHECK_ARG(P >= 1 && P <= kUlyMaxWorld && S >= P && S % P == 0, "Ulysses: S must be a multiple of P");
+  PYRE_CHECK_ARG(nq % P == 0 && nkv % P == 0 && nq % nkv == 0, "Ulysses: head counts must divide by P (and nq by nkv)");
+  PYRE_CHECK_ARG(hd == 64 || hd == 128, "Ulysses: head dim must be 64 or 128");
+  return PYRE_OK;
+}
+
+}  // namespace attn
+}  // namespace pyre
+
+extern "C" int pyre_ulysses_buffer_bytes(int S, int P, int nq, int nkv, int hd, int64_t* bytes) {
+  PYRE_CHECK_ARG(bytes != nullptr, "pyre_ulysses_buffer_bytes: null bytes");
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  *bytes = uly_layout(S, P, nq, nkv, hd).total;
+  return PYRE_OK;
+}
+
+extern "C" int pyre_ulysses_rope_scatter(void* const* bufs, int rank, int P, const float* q, const float* k,
+                                         const float* v, int64_t q_stride, int64_t kv_stride, int S, int nq, int nkv,
+                                         int hd, double theta, double rope_fraction, void* stream) {
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(q && k && v && rank >= 0 && rank < P, "pyre_ulysses_rope_scatter: bad arguments");
+  PYRE_CHECK_ARG(q_stride >= static_cast<int64_t>(nq) * hd && kv_stride >= static_cast<int64_t>(nkv) * hd,
+                 "pyre_ulysses_rope_scatter: row strides smaller than the heads");
+  const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
+  PYRE_CHECK_ARG(dims <= hd && theta > 0.0, "pyre_ulysses_rope_scatter: bad RoPE parameters");
+  UlyPeers peers{};
+  rc = uly_peers(bufs, P, &peers);
+  if (rc) return rc;
+  const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
+  const int S_local = S / P;
+  ulysses_rope_scatter_kernel<<<S_local, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, k, v, q_stride, kv_stride, S_local, rank * S_local, S, nq, nkv, hd, theta, dims < 2 ? 0 : dims, P, peers,
+      L.q, L.k, L.v);
+  PYRE_LAUNCH_CHECK("ulysses_rope_scatter_kernel");
+  return PYRE_OK;
+}
+
+extern "C" int pyre_ulysses_barrier(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd, int phase,
+                                    uint64_t timeout_ns, void* stream) {
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(rank >= 0 && rank < P && (phase == 0 || phase == 1), "pyre_ulysses_barrier: bad rank or phase");
+  UlyPeers peers{};
+  rc = uly_peers(bufs, P, &peers);
+  if (rc) return rc;
+  const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
+  ulysses_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peers, rank, P, phase, L.flags, L.epoch,
+                                                                            L.status, timeout_ns);
+  PYRE_LAUNCH_CHECK("ulysses_barrier_kernel");
+  return PYRE_OK;
+}
+
+extern "C" int pyre_ulysses_attention(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd,
+                                      void* stream) {
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(rank >= 0 && rank < P, "pyre_ulysses_attention: bad rank");
+  UlyPeers peers{};
+  rc = uly_peers(bufs, P, &peers);
+  if (rc) return rc;
+  const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
+  PrefillParams p{};
+  char* mine = peers.buf[rank];
+  p.q = reinterpret_cast<const __half*>(mine + L.q);
+  p.kc = reinterpret_cast<const __half*>(mine + L.k);
+  p.vc = reinterpret_cast<const __half*>(mine + L.v);
+  p.out = nullptr;
+  p.T = S;
+  p.nq = nq / P;
+  p.nkv = nkv / P;
+  p.max_t = S;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  p.scatter = 1;
+  p.rows_per_rank = S / P;
+  p.head_off = rank * (nq / P);
+  p.nq_total = nq;
+  for (int i = 0; i < P; ++i) p.out_peers[i] = reinterpret_cast<float*>(peers.buf[i] + L.ao);
+  return launch_prefill(p, hd, static_cast<cudaStream_t>(stream));
+}
+
+// Synchronises the stream, returns and clears this rank's status word (PYRE_OK or
+// PYRE_ETIMEOUT), and copies its [S/P, nq*hd] attention output into out (device memory).
+extern "C" int pyre_ulysses_finish(void* local_buf, int P, int S, int nq, int nkv, int hd, float* out, int* status,
+                                   void* stream) {
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(local_buf != nullptr && status != nullptr, "pyre_ulysses_finish: null pointer");
+  const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
+  char* mine = static_cast<char*>(local_buf);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (out != nullptr)
+    PYRE_CUDA_TRY(cudaMemcpyAsync(out, mine + L.ao, static_cast<size_t>(S / P) * nq * hd * 4, cudaMemcpyDeviceToDevice, s));
+  int st = 0;
+  PYRE_CUDA_TRY(cudaMemcpyAsync(&st, mine + L.status, 4, cudaMemcpyDeviceToHost, s));
+  PYRE_CUDA_TRY(cudaStreamSynchronize(s));
+  *status = st;
+  if (st != PYRE_OK) PYRE_CUDA_TRY(cudaMemset(mine + L.status, 0, 4));
   return PYRE_OK;
 }
