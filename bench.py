@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
+    ap.add_argument("--no-attention", action="store_true", help="skip the attention measurements")
     return ap.parse_args()
 
 
@@ -97,6 +98,87 @@ def cpu_reference_leg(tokens: int, budget_s: float, steps: int | None = None):
         "sample": f"{len(times)} reference-worker FFN calls (Q8_0 dequantize + f32 gated FFN, numpy BLAS "
                   f"with {cores} threads) on the full 4096x14336 shard at T={tokens}; median {step * 1e3:.1f} ms/call",
         "cpu_model": platform.processor() or platform.machine(),
+    }
+
+
+# ---------------------------------------------------------------------------------------
+# attention path (rank-local): decode attention over a 7B-shape KV cache, causal prefill
+# ---------------------------------------------------------------------------------------
+
+def attention_bench(dev, stream, hbm, tf_burst):
+    """Mistral-7B attention shape (32 q heads, 8 kv heads, head_dim 128, RoPE theta 1e6).
+    Decode: one token per layer over a t = 2175 cache (the mean cache length of a
+    2048-token prompt plus 256 generated tokens), RoPE + append + flash-decoding, 16 layers'
+    caches rotating (151 MB > L2). Prefill: causal attention of a 2048-token prompt."""
+    import torch
+    from pyre_b200.attention import AttentionOp
+    nq, nkv, hd, t, layers = 32, 8, 128, 2175, 16
+    gen = torch.Generator(device=dev).manual_seed(3)
+    ops = [AttentionOp(nq, nkv, hd, max_t=t, rope_theta=1e6, device=dev) for _ in range(layers)]
+    for o in ops:
+        o.cache.k.normal_(generator=gen)
+        o.cache.v.normal_(generator=gen)
+    q1 = torch.randn((1, nq * hd), generator=gen, device=dev)
+    k1 = torch.randn((1, nkv * hd), generator=gen, device=dev)
+    v1 = torch.randn((1, nkv * hd), generator=gen, device=dev)
+
+    def decode_all():
+        for o in ops:
+            o.cache.length = t - 1
+            o.decode(q1, k1, v1, stream=stream)
+
+    with torch.cuda.stream(stream):
+        decode_all()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        decode_all()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            g.replay()
+    e1.record(stream)
+    stream.synchronize()
+    dec_us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
+    kv_bytes = 2 * nkv * t * hd * 2
+    del g, ops
+
+    S = 2048
+    op = AttentionOp(nq, nkv, hd, max_t=S, rope_theta=1e6, device=dev)
+    qs = torch.randn((S, nq * hd), generator=gen, device=dev)
+    ks = torch.randn((S, nkv * hd), generator=gen, device=dev)
+    vs = torch.randn((S, nkv * hd), generator=gen, device=dev)
+
+    def prefill_once():
+        op.reset()
+        op.prefill(qs, ks, vs, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            prefill_once()
+    reps = 10
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            prefill_once()
+    e1.record(stream)
+    stream.synchronize()
+    pf_ms = e0.elapsed_time(e1) / reps
+    flops = 2 * 2 * hd * nq * S * S / 2          # causal: half of q k^T and of p v
+    return {
+        "shape": "Mistral-7B attention: 32 q heads, 8 kv heads, head_dim 128, f16 KV cache",
+        "decode": {"cache_len": t, "us_per_layer": round(dec_us, 2), "kv_bytes_per_layer": kv_bytes,
+                   "gbs": round(kv_bytes / (dec_us * 1e-6) / 1e9, 1),
+                   "frac_of_hbm": round(kv_bytes / (dec_us * 1e-6) / 1e9 / hbm, 4),
+                   "launches_per_layer": 2, "l2": f"{layers} layers' caches rotating"},
+        "prefill": {"tokens": S, "ms": round(pf_ms, 4), "tflops": round(flops / (pf_ms * 1e-3) / 1e12, 1),
+                    "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / tf_burst, 4),
+                    "kernel": "attn_prefill_kernel (f16 mma.sync, online softmax) + rope_append_kernel"},
     }
 
 
@@ -332,6 +414,9 @@ def run_ours(args):
         pf_ms = p0.elapsed_time(p1) / n_pf
         prefill = {"tokens": TP, "ms_per_step": pf_ms}
 
+    attn = None if args.no_attention else attention_bench(dev, stream, hbm, tf_burst)
+    barrier()
+
     # max over ranks
     vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(k_ms), prefill["ms_per_step"] if prefill else 0.0],
                         dtype=torch.float64, device=dev)
@@ -377,6 +462,8 @@ def run_ours(args):
                               "tok_s": round(args.prefill_tokens / (pf_ms * 1e-3), 1),
                               "tflops": round(flops / (pf_ms * 1e-3) / 1e12, 2),
                               "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / (tf_burst * world), 4)}
+        if attn:
+            res["attention"] = attn
         if not args.no_cpu:
             _, cpu = cpu_reference_leg(T, args.cpu_seconds)
             res["cpu_baseline"] = cpu

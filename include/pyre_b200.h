@@ -100,7 +100,9 @@ PYRE_API int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes);
  * h[T, W] = silu(x @ Wu)                 (ungated, src/ffn/builder.py:47-49; gated == 0)
  * x: [T, H] of x_dtype (PYRE_F32 or PYRE_BF16), 16-byte aligned rows. wgu: gate and up
  * [H, W] packed together (M = 2), or up alone (M = 1) when gated == 0, scales of
- * scale_dtype. h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16). silu(g) = g / (1 + exp(-g))
+ * scale_dtype. h: [T, W] of h_dtype (PYRE_F32 or PYRE_BF16; also PYRE_F16 for
+ * T > PYRE_FUSED_REDUCE_MAX_T, where the tensor-core GEMM takes f16 operands and flags
+ * PYRE_ERANGE in the workspace status word for values beyond f16). silu(g) = g / (1 + exp(-g))
  * as in pyre_kernels.silu_mul (src/kernels/mojo/pyre_kernels.mojo:121-129).
  * workspace: zero-initialised device memory of at least pyre_ffn_workspace_bytes();
  * it is left zeroed where it must start at zero, so it can be reused call after call on
@@ -200,17 +202,23 @@ PYRE_API int pyre_rms_norm(const float* x, int rows, int H, const float* w, doub
  * exp(x - max) * (1 / sum) (pyre_kernels.mojo:39-58). */
 PYRE_API int pyre_softmax_rows(const float* x, int64_t rows, int cols, float* out, void* stream);
 
+/* Host function: the RoPE table of pyre_kernels.mojo:86-89 for positions 0..n_pos-1, as f32
+ * [n_pos, dims/2, 2] (cos, sin) with dims = int(hd * rope_fraction), freq_i =
+ * 1 / theta^(2i/dims) and the angle pos * freq_i in f64 (C library pow / cos / sin), cast to
+ * f32. host_out holds n_pos * (dims/2) * 2 floats; the caller copies it to the device. */
+PYRE_API int pyre_rope_table(double theta, double rope_fraction, int hd, int n_pos, float* host_out);
+
 /* RoPE + clip + KV-cache append for T new tokens at positions start_pos..start_pos+T-1
  * (pyre_kernels.mojo:62-96 apply_rope, root_node.py:283-290 and :905-929): q [T, nq, hd] and
  * k, v [T, nkv, hd] f32 with row strides q_stride / kv_stride elements (one fused QKV
  * projection output can be passed as three offset pointers). q and k are rotated over the
- * first int(hd * rope_fraction) dims with freq_i = 1 / theta^(2i/dims) (f64, as the
- * reference), q, k and v clipped to +-1000; q_out f16 [nq, T, hd]; k, v appended to the f16
- * caches [nkv, max_t, hd]. */
+ * first int(hd * rope_fraction) dims with the device copy of pyre_rope_table (covering the
+ * positions used), q, k and v clipped to +-1000; q_out f16 [nq, T, hd]; k, v appended to the
+ * f16 caches [nkv, max_t, hd]. */
 PYRE_API int pyre_rope_kv_append(const float* q, const float* k, const float* v, int64_t q_stride,
-                                 int64_t kv_stride, int T, int nq, int nkv, int hd, int start_pos, double theta,
-                                 double rope_fraction, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
-                                 int max_t, void* stream);
+                                 int64_t kv_stride, int T, int nq, int nkv, int hd, int start_pos,
+                                 const float* rope_table, double rope_fraction, uint16_t* q_out, uint16_t* k_cache,
+                                 uint16_t* v_cache, int max_t, void* stream);
 
 /* Causal prefill attention over positions 0..T-1 of the caches (root_node.py:292-307:
  * GQA q head h -> kv head h / (nq / nkv), q k^T / sqrt(hd), -inf above the diagonal, softmax,
@@ -244,7 +252,7 @@ PYRE_API int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const 
 PYRE_API int pyre_ulysses_buffer_bytes(int S, int P, int nq, int nkv, int hd, int64_t* bytes);
 PYRE_API int pyre_ulysses_rope_scatter(void* const* bufs, int rank, int P, const float* q, const float* k,
                                        const float* v, int64_t q_stride, int64_t kv_stride, int S, int nq, int nkv,
-                                       int hd, double theta, double rope_fraction, void* stream);
+                                       int hd, const float* rope_table, double rope_fraction, void* stream);
 PYRE_API int pyre_ulysses_barrier(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd, int phase,
                                   uint64_t timeout_ns, void* stream);
 PYRE_API int pyre_ulysses_attention(void* const* bufs, int rank, int P, int S, int nq, int nkv, int hd,

@@ -69,13 +69,14 @@ _SIGNATURES = {
     "pyre_q80_linear": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp],
     "pyre_rms_norm": [_vp, _i, _i, _vp, ctypes.c_double, _vp, _vp],
     "pyre_softmax_rows": [_vp, _c_i64, _i, _vp, _vp],
-    "pyre_rope_kv_append": [_vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _i, ctypes.c_double, ctypes.c_double,
+    "pyre_rope_table": [ctypes.c_double, ctypes.c_double, _i, _i, _vp],
+    "pyre_rope_kv_append": [_vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _i, _vp, ctypes.c_double,
                             _vp, _vp, _vp, _i, _vp],
     "pyre_attn_prefill": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp],
     "pyre_attn_decode_workspace_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_attn_decode": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _c_i64, _vp],
     "pyre_ulysses_buffer_bytes": [_i, _i, _i, _i, _i, ctypes.POINTER(_c_i64)],
-    "pyre_ulysses_rope_scatter": [_vp, _i, _i, _vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, ctypes.c_double,
+    "pyre_ulysses_rope_scatter": [_vp, _i, _i, _vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _vp,
                                   ctypes.c_double, _vp],
     "pyre_ulysses_barrier": [_vp, _i, _i, _i, _i, _i, _i, _i, ctypes.c_uint64, _vp],
     "pyre_ulysses_attention": [_vp, _i, _i, _i, _i, _i, _i, _vp],

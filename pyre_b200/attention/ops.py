@@ -77,6 +77,18 @@ def softmax(x: torch.Tensor, stream=None) -> torch.Tensor:
     return out
 
 
+def rope_table(theta: float, rope_fraction: float, head_dim: int, n_pos: int, device) -> torch.Tensor:
+    """cos/sin of pos * freq_i for positions 0..n_pos-1 (pyre_kernels.mojo:86-89: freq_i =
+    1 / theta^(2i/dims) and the angle in f64, cast to f32), as f32 [n_pos, dims/2, 2] on the
+    device; an empty tensor when nothing is rotated."""
+    dims = int(float(head_dim) * float(rope_fraction))
+    half = dims // 2 if dims >= 2 else 0
+    host = torch.empty((max(n_pos, 1), max(half, 1), 2), dtype=torch.float32)
+    N.call("pyre_rope_table", float(theta), float(rope_fraction), int(head_dim), int(n_pos),
+           ctypes.c_void_p(host.data_ptr()))
+    return host.to(device)
+
+
 class KVCache:
     """One layer's K and V cache, f16 ``[n_kv, max_t, hd]`` (values clipped to +-1000)."""
 
@@ -100,6 +112,7 @@ class AttentionOp:
         self.nq, self.nkv, self.hd = n_heads, n_kv_heads, head_dim
         self.theta, self.frac = float(rope_theta), float(rope_fraction)
         self.cache = KVCache(n_kv_heads, max_t, head_dim, device)
+        self.rope = rope_table(self.theta, self.frac, head_dim, max_t, self.cache.k.device)
         b = ctypes.c_int64(0)
         N.call("pyre_attn_decode_workspace_bytes", n_heads, n_kv_heads, head_dim, max_t, ctypes.byref(b))
         self.dec_ws = torch.zeros(int(b.value), dtype=torch.uint8, device=self.cache.k.device)
@@ -119,7 +132,7 @@ class AttentionOp:
             raise ValueError("KV cache full")
         q_out = torch.empty((self.nq, T, self.hd), dtype=torch.float16, device=q.device)
         N.call("pyre_rope_kv_append", D.ptr(q), D.ptr(k), D.ptr(v), q.stride(0), k.stride(0), T, self.nq, self.nkv,
-               self.hd, start, self.theta, self.frac, D.ptr(q_out), D.ptr(self.cache.k), D.ptr(self.cache.v),
+               self.hd, start, D.ptr(self.rope), self.frac, D.ptr(q_out), D.ptr(self.cache.k), D.ptr(self.cache.v),
                self.cache.max_t, D.stream_ptr(stream))
         self.cache.length = start + T
         return q_out

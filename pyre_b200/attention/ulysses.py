@@ -47,6 +47,8 @@ class UlyssesAttention:
             self._opened.append(p.value)
             ptrs.append(p.value)
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        from .ops import rope_table
+        self.rope = rope_table(self.theta, self.frac, self.hd, self.S, torch.device("cuda", torch.cuda.current_device()))
 
     @property
     def local_tokens(self) -> int:
@@ -65,7 +67,7 @@ class UlyssesAttention:
         s = D.stream_ptr(stream)
         args = (self.S, self.nq, self.nkv, self.hd)
         N.call("pyre_ulysses_rope_scatter", self._bufs, self.rank, self.world, D.ptr(q), D.ptr(k), D.ptr(v),
-               q.stride(0), k.stride(0), *args, self.theta, self.frac, s)
+               q.stride(0), k.stride(0), *args, D.ptr(self.rope), self.frac, s)
         N.call("pyre_ulysses_barrier", self._bufs, self.rank, self.world, *args, 0, self.timeout_ns, s)
         N.call("pyre_ulysses_attention", self._bufs, self.rank, self.world, *args, s)
         N.call("pyre_ulysses_barrier", self._bufs, self.rank, self.world, *args, 1, self.timeout_ns, s)

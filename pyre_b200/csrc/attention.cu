@@ -14,11 +14,17 @@
 //   softmax_rows_kernel   one CTA per row (max initialised to -1e10 like the reference)
 //   rope_append_kernel    RoPE of q and k at positions start_pos.., clip, f16 store / append
 //                         (one CTA per token, shared cos/sin table)
-//   attn_decode_kernel    flash-decoding: (kv head, chunk) CTAs, partials combined in
-//                         chunk order by the last CTA of each kv head (deterministic)
+//   attn_decode_kernel    flash-decoding: CTAs split the cache of a kv head, f16 mma.sync
+//                         scores / weighted values with an online softmax, partials added
+//                         in order through a cluster's distributed shared memory
+//                         (deterministic)
 //   attn_prefill_kernel   causal attention, 64 queries x 64 keys per step, f16 mma.sync with
 //                         f32 accumulation and an online softmax, GQA by kv head = h / rep
 #include <cmath>
+
+#include <algorithm>
+#include <cooperative_groups.h>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -84,16 +90,18 @@ __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restri
 }
 
 // ---------------------------------------------------------------------------------------
-// One CTA per token: the cos/sin of the token's position for the rotated half-dims are
-// computed once (freq_i = 1 / theta^(2i/dims) and pos * freq_i in f64, cast to f32, as the
-// reference does), then every q and k head of the token is rotated in f32 (pair (i, i+half)),
+// One CTA per token: the cos/sin of the token's position for the rotated half-dims come
+// from the table of pyre_rope_table (f64 on the host, as the reference computes them), then
+// every q and k head of the token is rotated in f32 (pair (i, i+half)),
 // clipped to +-1000 and stored as f16; v is clipped and appended.
 constexpr int kRopeMaxHalf = 256;
+constexpr int kRopeHeadsPerCta = 8;
+
 
 __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v, int64_t q_stride,
                                                            int64_t kv_stride, int T, int nq, int nkv, int hd,
-                                                           int start_pos, double theta, int dims,
+                                                           int start_pos, const float2* __restrict__ table, int dims,
                                                            __half* __restrict__ q_out, __half* __restrict__ k_cache,
                                                            __half* __restrict__ v_cache, int max_t) {
   __shared__ float cs[kRopeMaxHalf], sn[kRopeMaxHalf];
@@ -101,25 +109,27 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
   const int pos = start_pos + t;
   const int half = dims >= 2 ? dims / 2 : 0;
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
-    const double freq = 1.0 / pow(theta, static_cast<double>(2 * j) / static_cast<double>(dims));
-    const double ang = static_cast<double>(pos) * freq;
-    cs[j] = static_cast<float>(cos(ang));
-    sn[j] = static_cast<float>(sin(ang));
+    const float2 c = table[static_cast<int64_t>(pos) * half + j];
+    cs[j] = c.x;
+    sn[j] = c.y;
   }
   __syncthreads();
-  const int nh = nq + nkv;
-  for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
-    const int hh = e / hd, i = e - hh * hd;
+  // this CTA's heads: q heads then k heads, kRopeHeadsPerCta of them starting at y * that
+  const int h0 = blockIdx.y * kRopeHeadsPerCta;
+  const int h1 = min(h0 + kRopeHeadsPerCta, nq + nkv);
+#pragma unroll 4
+  for (int e = threadIdx.x; e < (h1 - h0) * hd; e += blockDim.x) {
+    const int hh = h0 + e / hd, i = e % hd;
     const bool is_q = hh < nq;
     const int h = is_q ? hh : hh - nq;
     const float* src = is_q ? q + t * q_stride + static_cast<int64_t>(h) * hd : k + t * kv_stride + static_cast<int64_t>(h) * hd;
     float r;
     if (i < 2 * half) {
       const int jj = i < half ? i : i - half;
-      const float x1 = src[jj], x2 = src[jj + half];
+      const float x1 = __ldg(src + jj), x2 = __ldg(src + jj + half);
       r = i < half ? x1 * cs[jj] - x2 * sn[jj] : x1 * sn[jj] + x2 * cs[jj];
     } else {
-      r = src[i];
+      r = __ldg(src + i);
     }
     r = fminf(fmaxf(r, -1000.f), 1000.f);
     if (is_q)
@@ -127,133 +137,18 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
     else
       k_cache[(static_cast<int64_t>(h) * max_t + pos) * hd + i] = __float2half_rn(r);
   }
-  for (int e = threadIdx.x; e < nkv * hd; e += blockDim.x) {
-    const int h = e / hd, i = e - h * hd;
-    const float x = v[t * kv_stride + static_cast<int64_t>(h) * hd + i];
+  // v heads with the k heads of this CTA
+  const int v0 = max(h0, nq) - nq, v1 = max(h1, nq) - nq;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < (v1 - v0) * hd; e += blockDim.x) {
+    const int h = v0 + e / hd, i = e % hd;
+    const float x = __ldg(v + t * kv_stride + static_cast<int64_t>(h) * hd + i);
     v_cache[(static_cast<int64_t>(h) * max_t + pos) * hd + i] = __float2half_rn(fminf(fmaxf(x, -1000.f), 1000.f));
   }
 }
 
 // ---------------------------------------------------------------------------------------
-// Flash-decoding. grid (n_kv, splits), 128 threads. Each CTA scores positions
-// [c0, c1) of one kv head for its rep = nq / nkv query heads, keeps the chunk's max, sum of
-// exp and exp-weighted V sum per head, and the last CTA of the kv head combines the chunks
-// in chunk order.
-constexpr int kDecThreads = 128;
-constexpr int kDecMaxChunk = 256;
-constexpr int kDecMinChunk = 32;
-constexpr int kDecMaxRep = 8;
-
-struct DecodeParams {
-  const __half* q;       // [nq, hd] rotated, clipped
-  const __half* kc;      // [nkv, max_t, hd]
-  const __half* vc;
-  float* out;            // [nq * hd]
-  float* part;           // [nkv, splits, rep, hd + 2]  (m, l, acc[hd])
-  unsigned int* counters;// [nkv]
-  int nq, nkv, hd, t, max_t, splits, chunk, mask_lo, mask_hi;
-  float scale;           // 1 / sqrt(hd)
-};
-
-template <int HD>
-__global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeParams p) {
-  const int g = blockIdx.x, sp = blockIdx.y;
-  const int rep = p.nq / p.nkv;
-  const int c0 = sp * p.chunk, c1 = min(c0 + p.chunk, p.t);
-  __shared__ float qs[kDecMaxRep][HD];
-  __shared__ float sc[kDecMaxRep][kDecMaxChunk];
-  __shared__ float stat[kDecMaxRep][2];
-  __shared__ int s_last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < rep * HD; i += kDecThreads)
-    qs[i / HD][i % HD] = __half2float(p.q[(static_cast<int64_t>(g) * rep + i / HD) * HD + i % HD]);
-  __syncthreads();
-  const __half* kh = p.kc + static_cast<int64_t>(g) * p.max_t * HD;
-  const __half* vh = p.vc + static_cast<int64_t>(g) * p.max_t * HD;
-  // scores: one warp per position, lanes over hd
-  for (int pos = c0 + warp; pos < c1; pos += kDecThreads / 32) {
-    float kv[HD / 32];
-#pragma unroll
-    for (int j = 0; j < HD / 32; ++j) kv[j] = __half2float(kh[static_cast<int64_t>(pos) * HD + lane + 32 * j]);
-    for (int r = 0; r < rep; ++r) {
-      float d = 0.f;
-#pragma unroll
-      for (int j = 0; j < HD / 32; ++j) d += qs[r][lane + 32 * j] * kv[j];
-      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      const bool masked = pos >= p.mask_lo && pos < p.mask_hi;
-      if (lane == 0) sc[r][pos - c0] = masked ? -INFINITY : d * p.scale;
-    }
-  }
-  __syncthreads();
-  // per head: chunk max and sum of exp (one warp per head)
-  for (int r = warp; r < rep; r += kDecThreads / 32) {
-    float m = -INFINITY;
-    for (int i = lane; i < c1 - c0; i += 32) m = fmaxf(m, sc[r][i]);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int i = lane; i < c1 - c0; i += 32) {
-      const float e = m == -INFINITY ? 0.f : expf(sc[r][i] - m);
-      sc[r][i] = e;
-      l += e;
-    }
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      stat[r][0] = m;
-      stat[r][1] = l;
-    }
-  }
-  __syncthreads();
-  // exp-weighted V sum: thread per dimension
-  float* part = p.part + (static_cast<int64_t>(g) * p.splits + sp) * rep * (HD + 2);
-  for (int d = threadIdx.x; d < HD; d += kDecThreads) {
-    float acc[kDecMaxRep];
-#pragma unroll
-    for (int r = 0; r < kDecMaxRep; ++r) acc[r] = 0.f;
-    for (int pos = c0; pos < c1; ++pos) {
-      const float vv = __half2float(vh[static_cast<int64_t>(pos) * HD + d]);
-#pragma unroll
-      for (int r = 0; r < kDecMaxRep; ++r)
-        if (r < rep) acc[r] += sc[r][pos - c0] * vv;
-    }
-    for (int r = 0; r < rep; ++r) __stcg(part + r * (HD + 2) + 2 + d, acc[r]);
-  }
-  if (threadIdx.x < rep) {
-    __stcg(part + threadIdx.x * (HD + 2), stat[threadIdx.x][0]);
-    __stcg(part + threadIdx.x * (HD + 2) + 1, stat[threadIdx.x][1]);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(p.counters + g, 1u);
-    const int last = prev == static_cast<unsigned>(p.splits - 1);
-    if (last) {
-      __threadfence();
-      p.counters[g] = 0u;
-    }
-    s_last = last;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  // combine the chunks of this kv head in chunk order
-  const float* base = p.part + static_cast<int64_t>(g) * p.splits * rep * (HD + 2);
-  for (int i = threadIdx.x; i < rep * HD; i += kDecThreads) {
-    const int r = i / HD, d = i % HD;
-    float M = -INFINITY;
-    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(base + (static_cast<int64_t>(s) * rep + r) * (HD + 2)));
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float* ps = base + (static_cast<int64_t>(s) * rep + r) * (HD + 2);
-      const float m = __ldcg(ps);
-      const float w = m == -INFINITY ? 0.f : expf(m - M);
-      L += __ldcg(ps + 1) * w;
-      O += __ldcg(ps + 2 + d) * w;
-    }
-    p.out[(static_cast<int64_t>(g) * rep + r) * HD + d] = O / L;
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// Causal prefill attention. grid (ceil(T / 64), nq), 128 threads (4 warps x 16 query rows).
+// Causal prefill attention. grid (nq, ceil(T / 64)), 128 threads (4 warps x 16 query rows).
 constexpr int kPM = 64, kPN = 64;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
@@ -286,6 +181,362 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---------------------------------------------------------------------------------------
+// Decode attention (flash-decoding on mma.sync). grid (S, nkv), 256 threads, clusters of
+// C = min(S, 8) CTAs along x; S = C * X splits of the cache of kv head g. CTA (s, g) takes
+// positions [s*t/S, (s+1)*t/S) and its 8 warps take batches of 16 positions in turn, the
+// loads of a warp's next batch issued before its current batch is computed. Per batch a
+// warp computes S^T[16 pos x 8 heads] = K . Q^T with f16 MMAs (the rep <= 8 query heads of
+// the kv head are the N = 8 columns), an online softmax per head, and
+// O^T[hd x 8 heads] += V^T . P^T. The operands go from global memory straight to registers,
+// every load instruction reading whole 32-byte sectors:
+//   * a dot product may take its terms in any order, so lane (g, c) of the score MMA holds
+//     dims {32j + 8c + e : e < 8} of key rows g, g+8 and of query head g;
+//   * the value MMA's A operand (rows = dims, columns = positions) is built with byte
+//     permutes from 16-byte pieces of 4 value rows (positions 2c, 2c+1, 2c+8, 2c+9): lane
+//     (g, c) reads the hd/8 dims dec_vdim(g, j) + [0, 8) of each; m-tile mt takes the pair of
+//     dims in word mt of that slice (row g the even one, row g + 8 the odd one);
+//   * P^T (positions x heads) is the score accumulator transposed with movmatrix.
+// Partials (running max, sum of exponentials, weighted values) are rescaled to the CTA's
+// maximum and added in warp order in shared memory; each CTA of a cluster stores its partial
+// into rank 0's shared memory (distributed shared memory), and rank 0 adds the C partials in
+// rank order. With X > 1, rank 0 of each cluster writes its partial to the workspace and the
+// cluster that arrives last for its kv head (an arrival counter, reset by it) adds the X
+// partials in order. No waits on other CTAs beyond the cluster barrier; deterministic for a
+// given S.
+constexpr int kDecThreads = 256;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecBatch = 16;
+constexpr int kDecMaxRep = 8;
+constexpr int kDecCluster = 8;
+constexpr int kDecMaxGroups = 8;       // X, clusters per kv head
+constexpr int kDecMinChunk = 128;      // positions per CTA at least (one batch per warp)
+constexpr int kDecGroupChunk = 4096;   // positions per cluster before another cluster is added
+
+struct DecodeParams {
+  const __half* q;       // [nq, hd] rotated, clipped
+  const __half* kc;      // [nkv, max_t, hd]
+  const __half* vc;
+  float* out;            // [nq * hd]
+  float* part;           // [nkv][X][2 * rep + rep * hd]: max, sum, weighted values per cluster
+  unsigned* count;       // [nkv] arrival counters, zero between launches
+  int nq, nkv, t, max_t, mask_lo, mask_hi;
+  float scale;           // 1 / sqrt(hd)
+};
+
+// Shared memory: the static part below, then (dynamic) the warps' rescaled partials
+// [kDecWarps][rep][HD + 8] and the cluster ranks' partials [kDecCluster][rep][HD].
+struct DecodeSmem {
+  float wm[kDecWarps][kDecMaxRep], wl[kDecWarps][kDecMaxRep];
+  float cm[kDecCluster * kDecMaxGroups][kDecMaxRep], cl[kDecCluster * kDecMaxGroups][kDecMaxRep];
+  float L[kDecMaxRep];
+  int last;
+};
+template <int HD>
+constexpr int dec_dyn_bytes(int rep) {
+  return (kDecWarps * rep * (HD + 8) + kDecCluster * rep * HD) * 4;
+}
+
+template <int HD>
+struct DecodeRows {                            // one batch of 16 positions, per lane
+  uint4 ka[HD / 32], kb[HD / 32];              // key rows base+g, base+g+8
+  uint4 va[HD / 64], vb[HD / 64], vc[HD / 64], vd[HD / 64];   // value rows base+2c, +1, +8, +9
+};
+
+__device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ float dec_weight(float m, float M, float scale) {
+  return m == -INFINITY ? 0.f : expf((m - M) * scale);
+}
+// First dim of 16-byte piece j of lane group g's value slice: lanes 2k, 2k+1 read the two
+// halves of one 32-byte sector in each load.
+template <int HD>
+__device__ __forceinline__ int dec_vdim(int g, int j) {
+  return HD == 128 ? 32 * (g >> 1) + 16 * j + 8 * (g & 1) : 8 * g;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Rows past the chunk end (last) are clamped to it; their scores are masked.
+template <int HD>
+__device__ __forceinline__ void dec_load(DecodeRows<HD>& b, const __half* kh, const __half* vh, int base, int last,
+                                         int lg, int lc) {
+  const __half* ka = kh + static_cast<int64_t>(min(base + lg, last)) * HD + 8 * lc;
+  const __half* kb = kh + static_cast<int64_t>(min(base + lg + 8, last)) * HD + 8 * lc;
+#pragma unroll
+  for (int j = 0; j < HD / 32; ++j) {
+    b.ka[j] = __ldg(reinterpret_cast<const uint4*>(ka + 32 * j));
+    b.kb[j] = __ldg(reinterpret_cast<const uint4*>(kb + 32 * j));
+  }
+  const __half* va = vh + static_cast<int64_t>(min(base + 2 * lc, last)) * HD;
+  const __half* vb = vh + static_cast<int64_t>(min(base + 2 * lc + 1, last)) * HD;
+  const __half* vc = vh + static_cast<int64_t>(min(base + 2 * lc + 8, last)) * HD;
+  const __half* vd = vh + static_cast<int64_t>(min(base + 2 * lc + 9, last)) * HD;
+#pragma unroll
+  for (int j = 0; j < HD / 64; ++j) {
+    const int d = dec_vdim<HD>(lg, j);
+    b.va[j] = __ldg(reinterpret_cast<const uint4*>(va + d));
+    b.vb[j] = __ldg(reinterpret_cast<const uint4*>(vb + d));
+    b.vc[j] = __ldg(reinterpret_cast<const uint4*>(vc + d));
+    b.vd[j] = __ldg(reinterpret_cast<const uint4*>(vd + d));
+  }
+}
+
+struct DecodeState {
+  float m0, m1, l0, l1;    // heads 2c, 2c+1: running max (raw score units), this lane's sum
+};
+
+template <int HD>
+__device__ __forceinline__ void dec_batch(const DecodeRows<HD>& b, const uint4 (&qv)[HD / 32], float (&o)[HD / 16][4],
+                                          DecodeState& st, int base, int c1, int mask_lo, int mask_hi, float scale,
+                                          int lg) {
+  constexpr int KS = HD / 16;
+  // scores: s[0], s[1] = position base+lg, heads 2c, 2c+1; s[2], s[3] = position base+lg+8
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < KS; ++i) {
+    const int j = i >> 1, w = 2 * (i & 1);
+    const uint32_t a[4] = {u4w(b.ka[j], w), u4w(b.kb[j], w), u4w(b.ka[j], w + 1), u4w(b.kb[j], w + 1)};
+    mma16816(s, a, u4w(qv[j], w), u4w(qv[j], w + 1));
+  }
+  const int pa = base + lg, pb = base + lg + 8;
+  if (pa >= c1 || (pa >= mask_lo && pa < mask_hi)) s[0] = s[1] = -INFINITY;
+  if (pb >= c1 || (pb >= mask_lo && pb < mask_hi)) s[2] = s[3] = -INFINITY;
+  float x0 = fmaxf(s[0], s[2]), x1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+    x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
+  }
+  const float n0 = fmaxf(st.m0, x0), n1 = fmaxf(st.m1, x1);
+  const float al0 = dec_weight(st.m0, n0, scale), al1 = dec_weight(st.m1, n1, scale);
+  const float p0 = n0 == -INFINITY ? 0.f : expf((s[0] - n0) * scale);
+  const float p1 = n1 == -INFINITY ? 0.f : expf((s[1] - n1) * scale);
+  const float p2 = n0 == -INFINITY ? 0.f : expf((s[2] - n0) * scale);
+  const float p3 = n1 == -INFINITY ? 0.f : expf((s[3] - n1) * scale);
+  st.l0 = st.l0 * al0 + p0 + p2;     // this lane's positions only; summed over lanes at the end
+  st.l1 = st.l1 * al1 + p1 + p3;
+  st.m0 = n0;
+  st.m1 = n1;
+  const uint32_t b0 = movmatrix_t(pack_h2(p0, p1)), b1 = movmatrix_t(pack_h2(p2, p3));
+#pragma unroll
+  for (int mt = 0; mt < KS; ++mt) {
+    o[mt][0] *= al0;
+    o[mt][2] *= al0;
+    o[mt][1] *= al1;
+    o[mt][3] *= al1;
+    const int j = mt >> 2, w = mt & 3;
+    const uint32_t wa = u4w(b.va[j], w), wb = u4w(b.vb[j], w), wc = u4w(b.vc[j], w), wd = u4w(b.vd[j], w);
+    const uint32_t a[4] = {__byte_perm(wa, wb, 0x5410), __byte_perm(wa, wb, 0x7632), __byte_perm(wc, wd, 0x5410),
+                           __byte_perm(wc, wd, 0x7632)};
+    mma16816(o[mt], a, b0, b1);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const DecodeParams p) {
+  namespace cg = cooperative_groups;
+  constexpr int KS = HD / 16;
+  constexpr int KQ = HD / 32;
+  constexpr int WP = HD + 8;            // row pitch of the warp partials
+  __shared__ DecodeSmem sm;
+  extern __shared__ float4 dec_dyn[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  if (C > 1) cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on below)
+  const int split = blockIdx.x, S = gridDim.x, g = blockIdx.y;
+  const int X = S / C, grp = split / C;
+  const int rep = p.nq / p.nkv;
+  const int E = rep * HD;
+  float* wo = reinterpret_cast<float*>(dec_dyn);                 // [kDecWarps][rep][WP]
+  float* co = wo + kDecWarps * rep * WP;                         // [kDecCluster][rep][HD]
+  const int c0 = static_cast<int>(static_cast<int64_t>(p.t) * split / S);
+  const int c1 = static_cast<int>(static_cast<int64_t>(p.t) * (split + 1) / S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, lg = lane >> 2, lc = lane & 3;
+
+  uint4 qv[KQ];
+#pragma unroll
+  for (int j = 0; j < KQ; ++j)
+    qv[j] = lg < rep ? __ldg(reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(g) * rep + lg) * HD + 32 * j +
+                                                            8 * lc))
+                     : make_uint4(0u, 0u, 0u, 0u);
+  const __half* kh = p.kc + static_cast<int64_t>(g) * p.max_t * HD;
+  const __half* vh = p.vc + static_cast<int64_t>(g) * p.max_t * HD;
+  float o[KS][4];
+#pragma unroll
+  for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  DecodeState st{-INFINITY, -INFINITY, 0.f, 0.f};
+
+  constexpr int kStep = kDecWarps * kDecBatch;
+  DecodeRows<HD> r0, r1;
+  int base = c0 + warp * kDecBatch;
+  if (base < c1) dec_load(r0, kh, vh, base, c1 - 1, lg, lc);
+  while (base < c1) {
+    if (base + kStep < c1) dec_load(r1, kh, vh, base + kStep, c1 - 1, lg, lc);
+    dec_batch(r0, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale, lg);
+    base += kStep;
+    if (base >= c1) break;
+    if (base + kStep < c1) dec_load(r0, kh, vh, base + kStep, c1 - 1, lg, lc);
+    dec_batch(r1, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale, lg);
+    base += kStep;
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
+    st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
+  }
+  if (lg == 0) {
+    sm.wm[warp][2 * lc] = st.m0;
+    sm.wm[warp][2 * lc + 1] = st.m1;
+  }
+  __syncthreads();
+  // rescale this warp's partial to the CTA maximum of each head
+  float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kDecWarps; ++w) {
+    M0 = fmaxf(M0, sm.wm[w][2 * lc]);
+    M1 = fmaxf(M1, sm.wm[w][2 * lc + 1]);
+  }
+  const float f0 = dec_weight(st.m0, M0, p.scale), f1 = dec_weight(st.m1, M1, p.scale);
+  if (lg == 0) {
+    sm.wl[warp][2 * lc] = st.l0 * f0;
+    sm.wl[warp][2 * lc + 1] = st.l1 * f1;
+  }
+#pragma unroll
+  for (int mt = 0; mt < KS; ++mt) {
+    const int d = dec_vdim<HD>(lg, mt >> 2) + 2 * (mt & 3);
+    if (2 * lc < rep)
+      *reinterpret_cast<float2*>(wo + (warp * rep + 2 * lc) * WP + d) = make_float2(o[mt][0] * f0, o[mt][2] * f0);
+    if (2 * lc + 1 < rep)
+      *reinterpret_cast<float2*>(wo + (warp * rep + 2 * lc + 1) * WP + d) = make_float2(o[mt][1] * f1, o[mt][3] * f1);
+  }
+  __syncthreads();
+
+  // this CTA's partial (warps in order), into rank 0's shared memory when C > 1
+  if (C > 1) cluster_wait();            // rank 0 has started: its shared memory can be written
+  float* dst_o = C > 1 ? cluster.map_shared_rank(co, 0) + rank * E : nullptr;
+  float* dst_m = C > 1 ? cluster.map_shared_rank(&sm.cm[0][0], 0) + rank * kDecMaxRep : nullptr;
+  float* dst_l = C > 1 ? cluster.map_shared_rank(&sm.cl[0][0], 0) + rank * kDecMaxRep : nullptr;
+  for (int i = threadIdx.x; i < E; i += kDecThreads) {
+    const int r = i / HD, d = i - r * HD;
+    float O = 0.f, L = 0.f, M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w) {
+      O += wo[(w * rep + r) * WP + d];
+      L += sm.wl[w][r];
+      M = fmaxf(M, sm.wm[w][r]);
+    }
+    if (C == 1 && X == 1) {
+      p.out[static_cast<int64_t>(g) * E + i] = O / L;
+    } else if (C == 1) {
+      co[i] = O;
+      if (d == 0) {
+        sm.cm[0][r] = M;
+        sm.cl[0][r] = L;
+      }
+    } else {
+      dst_o[i] = O;
+      if (d == 0) {
+        dst_m[r] = M;
+        dst_l[r] = L;
+      }
+    }
+  }
+  if (C > 1) {
+    cluster_arrive();                   // release: the stores above are visible to rank 0
+    cluster_wait();
+    if (rank != 0) return;              // nothing reads this CTA's shared memory any more
+  } else {
+    if (X == 1) return;
+    __syncthreads();
+  }
+
+  // rank 0: the C partials of this cluster, in rank order
+  if (threadIdx.x < rep) {
+    const int r = threadIdx.x;
+    float M = -INFINITY;
+    for (int cc = 0; cc < C; ++cc) M = fmaxf(M, sm.cm[cc][r]);
+    float L = 0.f;
+    for (int cc = 0; cc < C; ++cc) {
+      const float wt = dec_weight(sm.cm[cc][r], M, p.scale);
+      L += sm.cl[cc][r] * wt;
+      sm.cl[cc][r] = wt;                // weight of rank cc from here on
+    }
+    sm.cm[0][r] = M;
+    sm.L[r] = L;
+  }
+  __syncthreads();
+  const int stride = 2 * rep + E;
+  float* gpart = X > 1 ? p.part + (static_cast<int64_t>(g) * X + grp) * stride : nullptr;
+  for (int i = threadIdx.x; i < E; i += kDecThreads) {
+    const int r = i / HD;
+    float O = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < kDecCluster; ++cc)
+      if (cc < C) O += co[cc * E + i] * sm.cl[cc][r];
+    if (X == 1)
+      p.out[static_cast<int64_t>(g) * E + i] = O / sm.L[r];
+    else
+      gpart[2 * rep + i] = O;
+  }
+  if (X == 1) return;
+  if (threadIdx.x < rep) {
+    gpart[threadIdx.x] = sm.cm[0][threadIdx.x];
+    gpart[rep + threadIdx.x] = sm.L[threadIdx.x];
+  }
+  // arrival: the barrier orders this CTA's stores before thread 0's fence and atomic
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const bool last = atomicAdd(p.count + g, 1u) == static_cast<unsigned>(X - 1);
+    if (last) __threadfence();
+    sm.last = last;
+  }
+  __syncthreads();
+  if (!sm.last) return;
+  // the last cluster of kv head g adds the X cluster partials in order
+  const float* pg = p.part + static_cast<int64_t>(g) * X * stride;
+  if (threadIdx.x < X * rep) {
+    const int x = threadIdx.x / rep, r = threadIdx.x - x * rep;
+    sm.cm[x][r] = __ldcg(pg + x * stride + r);
+    sm.cl[x][r] = __ldcg(pg + x * stride + rep + r);
+  }
+  __syncthreads();
+  if (threadIdx.x < rep) {
+    const int r = threadIdx.x;
+    float M = -INFINITY;
+    for (int x = 0; x < X; ++x) M = fmaxf(M, sm.cm[x][r]);
+    float L = 0.f;
+    for (int x = 0; x < X; ++x) {
+      const float wt = dec_weight(sm.cm[x][r], M, p.scale);
+      L += sm.cl[x][r] * wt;
+      sm.cl[x][r] = wt;
+    }
+    sm.L[r] = L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += kDecThreads) {
+    const int r = i / HD;
+    float v[kDecMaxGroups];
+#pragma unroll
+    for (int x = 0; x < kDecMaxGroups; ++x) v[x] = x < X ? __ldcg(pg + x * stride + 2 * rep + i) : 0.f;
+    float O = 0.f;
+#pragma unroll
+    for (int x = 0; x < kDecMaxGroups; ++x)
+      if (x < X) O += v[x] * sm.cl[x][r];
+    p.out[static_cast<int64_t>(g) * E + i] = O / sm.L[r];
+  }
+  if (threadIdx.x == 0) p.count[g] = 0u;
+}
+
 struct PrefillParams {
   const __half* q;     // [nq, T, hd]
   const __half* kc;    // [nkv, max_t, hd]
@@ -314,7 +565,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillParams p
   __half* qs = sm;
   __half* ks = sm + S::kQ;              // [2][kPN][kLd]
   __half* vs = ks + 2 * S::kKV;
-  const int qb = blockIdx.x, h = blockIdx.y;
+  // heaviest query blocks (most keys under the causal mask) first, all heads together
+  const int qb = gridDim.y - 1 - blockIdx.y, h = blockIdx.x;
   const int g = h / (p.nq / p.nkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = qb * kPM;
@@ -486,9 +738,25 @@ extern "C" int pyre_softmax_rows(const float* x, int64_t rows, int cols, float* 
   return PYRE_OK;
 }
 
+extern "C" int pyre_rope_table(double theta, double rope_fraction, int hd, int n_pos, float* host_out) {
+  PYRE_CHECK_ARG(host_out != nullptr && hd >= 1 && n_pos >= 1 && theta > 0.0, "pyre_rope_table: bad arguments");
+  const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
+  PYRE_CHECK_ARG(dims <= hd && dims / 2 <= kRopeMaxHalf, "pyre_rope_table: rope_fraction must be in [0, 1]");
+  const int half = dims >= 2 ? dims / 2 : 0;
+  for (int i = 0; i < half; ++i) {
+    const double freq = 1.0 / std::pow(theta, static_cast<double>(2 * i) / static_cast<double>(dims));
+    for (int p = 0; p < n_pos; ++p) {
+      const double ang = static_cast<double>(p) * freq;
+      host_out[(static_cast<int64_t>(p) * half + i) * 2] = static_cast<float>(std::cos(ang));
+      host_out[(static_cast<int64_t>(p) * half + i) * 2 + 1] = static_cast<float>(std::sin(ang));
+    }
+  }
+  return PYRE_OK;
+}
+
 extern "C" int pyre_rope_kv_append(const float* q, const float* k, const float* v, int64_t q_stride,
                                    int64_t kv_stride, int T, int nq, int nkv, int hd,
-                                   int start_pos, double theta, double rope_fraction, uint16_t* q_out,
+                                   int start_pos, const float* rope_table, double rope_fraction, uint16_t* q_out,
                                    uint16_t* k_cache, uint16_t* v_cache, int max_t, void* stream) {
   PYRE_CHECK_ARG(q && k && v && q_out && k_cache && v_cache, "pyre_rope_kv_append: null pointer");
   PYRE_CHECK_ARG(T >= 1 && nq >= 1 && nkv >= 1 && hd >= 2 && nq % nkv == 0, "pyre_rope_kv_append: bad head counts");
@@ -497,61 +765,130 @@ extern "C" int pyre_rope_kv_append(const float* q, const float* k, const float* 
                  "pyre_rope_kv_append: row strides smaller than the heads");
   const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
   PYRE_CHECK_ARG(dims <= hd && dims / 2 <= kRopeMaxHalf, "pyre_rope_kv_append: rope_fraction must be in [0, 1]");
-  PYRE_CHECK_ARG(theta > 0.0, "pyre_rope_kv_append: theta must be positive");
-  rope_append_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k, v, q_stride, kv_stride, T, nq, nkv, hd, start_pos, theta, dims < 2 ? 0 : dims, reinterpret_cast<__half*>(q_out),
+  PYRE_CHECK_ARG(rope_table != nullptr || dims < 2, "pyre_rope_kv_append: null RoPE table");
+  dim3 grid(T, (nq + nkv + kRopeHeadsPerCta - 1) / kRopeHeadsPerCta);
+  rope_append_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, k, v, q_stride, kv_stride, T, nq, nkv, hd, start_pos, reinterpret_cast<const float2*>(rope_table),
+      dims < 2 ? 0 : dims, reinterpret_cast<__half*>(q_out),
       reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), max_t);
   PYRE_LAUNCH_CHECK("rope_append_kernel");
   return PYRE_OK;
 }
 
+namespace pyre {
+namespace attn {
+// Cluster size C: the largest power of two <= 8 that leaves every CTA kDecMinChunk positions.
+inline int decode_cluster(int t) {
+  int c = 1;
+  while (c < kDecCluster && 2 * c * kDecMinChunk <= t) c *= 2;
+  return c;
+}
+// Clusters per kv head X: one per kDecGroupChunk positions, at most kDecMaxGroups.
+inline int decode_max_groups(int t) {
+  return decode_cluster(t) < kDecCluster ? 1 : std::min(kDecMaxGroups, (t + kDecGroupChunk - 1) / kDecGroupChunk);
+}
+inline int64_t decode_counter_bytes(int nkv) { return (static_cast<int64_t>(nkv) * 4 + 255) / 256 * 256; }
+inline int64_t decode_group_bytes(int nq, int nkv, int hd) {
+  const int rep = nq / nkv;
+  return static_cast<int64_t>(2 * rep + rep * hd) * 4;
+}
+
+// Splits S = C * X of the cache per kv head; X is also bounded by the number of 8-CTA
+// clusters the device runs at once, so that the grid is one wave.
+template <int HD>
+int decode_splits(int nkv, int t, int* C, int* X) {
+  static std::mutex mu;
+  static int cached[64] = {};
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  int clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    int& c = cached[dev & 63];
+    if (c == 0) {
+      int rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD>), dec_dyn_bytes<HD>(kDecMaxRep));
+      if (rc) return rc;
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(kDecCluster, 1, 1);
+      cfg.blockDim = dim3(kDecThreads, 1, 1);
+      cfg.dynamicSmemBytes = static_cast<size_t>(dec_dyn_bytes<HD>(kDecMaxRep));
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = kDecCluster;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&c, attn_decode_kernel<HD>, &cfg));
+      c = std::max(1, c);
+    }
+    clusters = c;
+  }
+  *C = decode_cluster(t);
+  *X = std::max(1, std::min(decode_max_groups(t), clusters / nkv));
+  return PYRE_OK;
+}
+}  // namespace attn
+}  // namespace pyre
+
 extern "C" int pyre_attn_decode_workspace_bytes(int nq, int nkv, int hd, int t, int64_t* bytes) {
-  PYRE_CHECK_ARG(bytes != nullptr && nq >= 1 && nkv >= 1 && hd >= 1 && t >= 1, "pyre_attn_decode_workspace_bytes: bad args");
-  const int64_t splits = (t + kDecMinChunk - 1) / kDecMinChunk;   // the most chunks a call can use
-  *bytes = 256 + (static_cast<int64_t>(nq) * splits * (hd + 2) * 4 + 255) / 256 * 256;
+  PYRE_CHECK_ARG(bytes != nullptr && nq >= 1 && nkv >= 1 && hd >= 1 && t >= 1 && nq % nkv == 0,
+                 "pyre_attn_decode_workspace_bytes: bad args");
+  *bytes = decode_counter_bytes(nkv) + static_cast<int64_t>(nkv) * decode_max_groups(t) * decode_group_bytes(nq, nkv, hd);
   return PYRE_OK;
 }
 
 extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int t, int nq,
                                 int nkv, int hd, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
                                 int64_t ws_bytes, void* stream) {
-  PYRE_CHECK_ARG(q && k_cache && v_cache && out && workspace, "pyre_attn_decode: null pointer");
+  PYRE_CHECK_ARG(q && k_cache && v_cache && out, "pyre_attn_decode: null pointer");
   PYRE_CHECK_ARG(t >= 1 && t <= max_t && nkv >= 1 && nq % nkv == 0 && nq / nkv <= kDecMaxRep,
                  "pyre_attn_decode: bad sizes (at most 8 query heads per kv head)");
   PYRE_CHECK_ARG(hd == 64 || hd == 128, "pyre_attn_decode: head dim must be 64 or 128");
-  PYRE_CHECK_ARG(nkv <= 64, "pyre_attn_decode: at most 64 kv heads");
-  int64_t need = 0;
-  pyre_attn_decode_workspace_bytes(nq, nkv, hd, t, &need);
-  PYRE_CHECK_ARG(ws_bytes >= need && reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
-                 "pyre_attn_decode: workspace too small or not 256-byte aligned");
+  PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(k_cache) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(v_cache) % 16 == 0,
+                 "pyre_attn_decode: q and the caches must be 16-byte aligned");
+  int C = 1, X = 1;
+  int rc = hd == 64 ? decode_splits<64>(nkv, t, &C, &X) : decode_splits<128>(nkv, t, &C, &X);
+  if (rc) return rc;
+  const int64_t need = decode_counter_bytes(nkv) + static_cast<int64_t>(nkv) * X * decode_group_bytes(nq, nkv, hd);
+  if (X > 1)
+    PYRE_CHECK_ARG(workspace != nullptr && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 && ws_bytes >= need,
+                   "pyre_attn_decode: workspace missing, misaligned or smaller than pyre_attn_decode_workspace_bytes");
   DecodeParams p{};
   p.q = reinterpret_cast<const __half*>(q);
   p.kc = reinterpret_cast<const __half*>(k_cache);
   p.vc = reinterpret_cast<const __half*>(v_cache);
   p.out = out;
-  p.counters = static_cast<unsigned int*>(workspace);
-  p.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  p.count = static_cast<unsigned*>(workspace);
+  p.part = X > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + decode_counter_bytes(nkv)) : nullptr;
   p.nq = nq;
   p.nkv = nkv;
-  p.hd = hd;
   p.t = t;
   p.max_t = max_t;
-  p.chunk = kDecMaxChunk;
-  p.splits = (t + kDecMaxChunk - 1) / kDecMaxChunk;
-  // more, smaller chunks while the kv heads alone leave SMs idle
-  while (p.chunk > kDecMinChunk && static_cast<int64_t>(nkv) * ((t + p.chunk / 2 - 1) / (p.chunk / 2)) <= 2 * sm_count()) {
-    p.chunk /= 2;
-    p.splits = (t + p.chunk - 1) / p.chunk;
-  }
   p.mask_lo = mask_lo;
   p.mask_hi = mask_hi;
   p.scale = 1.0f / sqrtf(static_cast<float>(hd));
-  dim3 grid(nkv, p.splits);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rep = nq / nkv;
+  rc = hd == 64 ? set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<64>), dec_dyn_bytes<64>(kDecMaxRep))
+                : set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<128>), dec_dyn_bytes<128>(kDecMaxRep));
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(C * X), static_cast<unsigned>(nkv), 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(hd == 64 ? dec_dyn_bytes<64>(rep) : dec_dyn_bytes<128>(rep));
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(C);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
   if (hd == 64)
-    attn_decode_kernel<64><<<grid, kDecThreads, 0, s>>>(p);
+    PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, p));
   else
-    attn_decode_kernel<128><<<grid, kDecThreads, 0, s>>>(p);
+    PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, p));
   PYRE_LAUNCH_CHECK("attn_decode_kernel");
   return PYRE_OK;
 }
@@ -559,7 +896,7 @@ extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, cons
 namespace pyre {
 namespace attn {
 int launch_prefill(PrefillParams p, int hd, cudaStream_t s) {
-  dim3 grid((p.T + kPM - 1) / kPM, p.nq);
+  dim3 grid(p.nq, (p.T + kPM - 1) / kPM);
   int rc;
   if (hd == 64) {
     rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<64>), PrefillSmem<64>::kBytes);
@@ -640,17 +977,17 @@ struct UlyPeers {
 
 __global__ void __launch_bounds__(256) ulysses_rope_scatter_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, int64_t q_stride,
-    int64_t kv_stride, int S_local, int seq_off, int S, int nq, int nkv, int hd, double theta, int dims, int P,
+    int64_t kv_stride, int S_local, int seq_off, int S, int nq, int nkv, int hd, const float2* __restrict__ table,
+    int dims, int P,
     UlyPeers peers, int64_t off_q, int64_t off_k, int64_t off_v) {
   __shared__ float cs[kRopeMaxHalf], sn[kRopeMaxHalf];
   const int t = blockIdx.x;
   const int pos = seq_off + t;
   const int half = dims >= 2 ? dims / 2 : 0;
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
-    const double freq = 1.0 / pow(theta, static_cast<double>(2 * j) / static_cast<double>(dims));
-    const double ang = static_cast<double>(pos) * freq;
-    cs[j] = static_cast<float>(cos(ang));
-    sn[j] = static_cast<float>(sin(ang));
+    const float2 c = table[static_cast<int64_t>(pos) * half + j];
+    cs[j] = c.x;
+    sn[j] = c.y;
   }
   __syncthreads();
   const int qpr = nq / P, kpr = nkv / P;
@@ -732,21 +1069,23 @@ extern "C" int pyre_ulysses_buffer_bytes(int S, int P, int nq, int nkv, int hd, 
 
 extern "C" int pyre_ulysses_rope_scatter(void* const* bufs, int rank, int P, const float* q, const float* k,
                                          const float* v, int64_t q_stride, int64_t kv_stride, int S, int nq, int nkv,
-                                         int hd, double theta, double rope_fraction, void* stream) {
+                                         int hd, const float* rope_table, double rope_fraction, void* stream) {
   int rc = uly_check_shape(S, P, nq, nkv, hd);
   if (rc) return rc;
   PYRE_CHECK_ARG(q && k && v && rank >= 0 && rank < P, "pyre_ulysses_rope_scatter: bad arguments");
   PYRE_CHECK_ARG(q_stride >= static_cast<int64_t>(nq) * hd && kv_stride >= static_cast<int64_t>(nkv) * hd,
                  "pyre_ulysses_rope_scatter: row strides smaller than the heads");
   const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
-  PYRE_CHECK_ARG(dims <= hd && theta > 0.0, "pyre_ulysses_rope_scatter: bad RoPE parameters");
+  PYRE_CHECK_ARG(dims <= hd && dims / 2 <= kRopeMaxHalf && (rope_table != nullptr || dims < 2),
+                 "pyre_ulysses_rope_scatter: bad RoPE parameters");
   UlyPeers peers{};
   rc = uly_peers(bufs, P, &peers);
   if (rc) return rc;
   const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
   const int S_local = S / P;
   ulysses_rope_scatter_kernel<<<S_local, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k, v, q_stride, kv_stride, S_local, rank * S_local, S, nq, nkv, hd, theta, dims < 2 ? 0 : dims, P, peers,
+      q, k, v, q_stride, kv_stride, S_local, rank * S_local, S, nq, nkv, hd,
+      reinterpret_cast<const float2*>(rope_table), dims < 2 ? 0 : dims, P, peers,
       L.q, L.k, L.v);
   PYRE_LAUNCH_CHECK("ulysses_rope_scatter_kernel");
   return PYRE_OK;

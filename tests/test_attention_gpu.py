@@ -149,6 +149,28 @@ def test_decode_padding_mask_golden():
     assert rel(got, z["decode__attn"][0, 0]) < TOL_ATTN
 
 
+@pytest.mark.parametrize("nq,nkv,hd,t", [(32, 8, 128, 2175), (16, 2, 128, 9000), (8, 8, 64, 5000), (14, 2, 64, 700), (8, 1, 128, 40000)])
+def test_decode_long_cache(nq, nkv, hd, t):
+    """Split decode over long caches (cluster and cross-cluster partial combines, GQA groups
+    of 1..8 heads) against the oracle's attention_decode on the same f16 cache."""
+    from pyre_b200 import _device as D, _native as N
+    rng = np.random.default_rng(t + nq)
+    q = (rng.standard_normal((nq, hd)) * 2).astype(np.float16)
+    k = (rng.standard_normal((nkv, t, hd)) * 2).astype(np.float16)
+    v = (rng.standard_normal((nkv, t, hd)) * 2).astype(np.float16)
+    b = ctypes.c_int64(0)
+    N.call("pyre_attn_decode_workspace_bytes", nq, nkv, hd, t, ctypes.byref(b))
+    ws = torch.zeros(b.value, dtype=torch.uint8, device="cuda")
+    qh, kh, vh = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    out = torch.empty(nq * hd, device="cuda")
+    ref = OA.attention_decode(q.astype(np.float32).reshape(1, nq, 1, hd), k.astype(np.float32)[None],
+                              v.astype(np.float32)[None])[0, 0]
+    for _ in range(2):     # the workspace's arrival counters are left at zero for the next call
+        N.call("pyre_attn_decode", D.ptr(qh), D.ptr(kh), D.ptr(vh), t, nq, nkv, hd, t, 0, 0, D.ptr(out), D.ptr(ws),
+               ws.numel(), D.stream_ptr())
+        assert rel(out.cpu().numpy(), ref) < TOL_ATTN
+
+
 def test_ulysses_builder_projection():
     """build_ulysses_attention_graph through the session, on the reference's golden shards."""
     from pyre_b200.attention import ShardSpec, build_ulysses_attention_graph
