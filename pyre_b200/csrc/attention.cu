@@ -211,7 +211,7 @@ constexpr int kDecMaxRep = 8;
 constexpr int kDecCluster = 8;
 constexpr int kDecMaxGroups = 8;       // X, clusters per kv head
 constexpr int kDecMinChunk = 128;      // positions per CTA at least (one batch per warp)
-constexpr int kDecGroupChunk = 4096;   // positions per cluster before another cluster is added
+constexpr int kDecGroupChunk = 2048;   // positions per cluster before another cluster is added
 
 struct DecodeParams {
   const __half* q;       // [nq, hd] rotated, clipped
@@ -221,7 +221,7 @@ struct DecodeParams {
   float* part;           // [nkv][X][2 * rep + rep * hd]: max, sum, weighted values per cluster
   unsigned* count;       // [nkv] arrival counters, zero between launches
   int nq, nkv, t, max_t, mask_lo, mask_hi;
-  float scale;           // 1 / sqrt(hd)
+  float scale2;          // log2(e) / sqrt(hd): exponentials are taken base 2
 };
 
 // Shared memory: the static part below, then (dynamic) the warps' rescaled partials
@@ -229,7 +229,6 @@ struct DecodeParams {
 struct DecodeSmem {
   float wm[kDecWarps][kDecMaxRep], wl[kDecWarps][kDecMaxRep];
   float cm[kDecCluster * kDecMaxGroups][kDecMaxRep], cl[kDecCluster * kDecMaxGroups][kDecMaxRep];
-  float L[kDecMaxRep];
   int last;
 };
 template <int HD>
@@ -251,8 +250,15 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
-__device__ __forceinline__ float dec_weight(float m, float M, float scale) {
-  return m == -INFINITY ? 0.f : expf((m - M) * scale);
+// 2^x (PTX ex2.approx: relative error below 2^-22, far inside the path's tolerance).
+__device__ __forceinline__ float dec_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// exp((m - M) / sqrt(hd)) with scale2 = log2(e) / sqrt(hd); 0 for an empty partial (m = -inf).
+__device__ __forceinline__ float dec_weight(float m, float M, float scale2) {
+  return m == -INFINITY ? 0.f : dec_exp2((m - M) * scale2);
 }
 // First dim of 16-byte piece j of lane group g's value slice: lanes 2k, 2k+1 read the two
 // halves of one 32-byte sector in each load.
@@ -295,7 +301,7 @@ struct DecodeState {
 
 template <int HD>
 __device__ __forceinline__ void dec_batch(const DecodeRows<HD>& b, const uint4 (&qv)[HD / 32], float (&o)[HD / 16][4],
-                                          DecodeState& st, int base, int c1, int mask_lo, int mask_hi, float scale,
+                                          DecodeState& st, int base, int c1, int mask_lo, int mask_hi, float scale2,
                                           int lg) {
   constexpr int KS = HD / 16;
   // scores: s[0], s[1] = position base+lg, heads 2c, 2c+1; s[2], s[3] = position base+lg+8
@@ -316,22 +322,28 @@ __device__ __forceinline__ void dec_batch(const DecodeRows<HD>& b, const uint4 (
     x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
   }
   const float n0 = fmaxf(st.m0, x0), n1 = fmaxf(st.m1, x1);
-  const float al0 = dec_weight(st.m0, n0, scale), al1 = dec_weight(st.m1, n1, scale);
-  const float p0 = n0 == -INFINITY ? 0.f : expf((s[0] - n0) * scale);
-  const float p1 = n1 == -INFINITY ? 0.f : expf((s[1] - n1) * scale);
-  const float p2 = n0 == -INFINITY ? 0.f : expf((s[2] - n0) * scale);
-  const float p3 = n1 == -INFINITY ? 0.f : expf((s[3] - n1) * scale);
+  const float al0 = dec_weight(st.m0, n0, scale2), al1 = dec_weight(st.m1, n1, scale2);
+  const float p0 = n0 == -INFINITY ? 0.f : dec_exp2((s[0] - n0) * scale2);
+  const float p1 = n1 == -INFINITY ? 0.f : dec_exp2((s[1] - n1) * scale2);
+  const float p2 = n0 == -INFINITY ? 0.f : dec_exp2((s[2] - n0) * scale2);
+  const float p3 = n1 == -INFINITY ? 0.f : dec_exp2((s[3] - n1) * scale2);
   st.l0 = st.l0 * al0 + p0 + p2;     // this lane's positions only; summed over lanes at the end
   st.l1 = st.l1 * al1 + p1 + p3;
+  // the weighted sums are rescaled only when a running maximum of the warp has grown
+  if (__any_sync(0xffffffffu, n0 > st.m0 || n1 > st.m1)) {
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][2] *= al0;
+      o[mt][1] *= al1;
+      o[mt][3] *= al1;
+    }
+  }
   st.m0 = n0;
   st.m1 = n1;
   const uint32_t b0 = movmatrix_t(pack_h2(p0, p1)), b1 = movmatrix_t(pack_h2(p2, p3));
 #pragma unroll
   for (int mt = 0; mt < KS; ++mt) {
-    o[mt][0] *= al0;
-    o[mt][2] *= al0;
-    o[mt][1] *= al1;
-    o[mt][3] *= al1;
     const int j = mt >> 2, w = mt & 3;
     const uint32_t wa = u4w(b.va[j], w), wb = u4w(b.vb[j], w), wc = u4w(b.vc[j], w), wd = u4w(b.vd[j], w);
     const uint32_t a[4] = {__byte_perm(wa, wb, 0x5410), __byte_perm(wa, wb, 0x7632), __byte_perm(wc, wd, 0x5410),
@@ -381,11 +393,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   if (base < c1) dec_load(r0, kh, vh, base, c1 - 1, lg, lc);
   while (base < c1) {
     if (base + kStep < c1) dec_load(r1, kh, vh, base + kStep, c1 - 1, lg, lc);
-    dec_batch(r0, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale, lg);
+    dec_batch(r0, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale2, lg);
     base += kStep;
     if (base >= c1) break;
     if (base + kStep < c1) dec_load(r0, kh, vh, base + kStep, c1 - 1, lg, lc);
-    dec_batch(r1, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale, lg);
+    dec_batch(r1, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale2, lg);
     base += kStep;
   }
 #pragma unroll
@@ -405,7 +417,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
     M0 = fmaxf(M0, sm.wm[w][2 * lc]);
     M1 = fmaxf(M1, sm.wm[w][2 * lc + 1]);
   }
-  const float f0 = dec_weight(st.m0, M0, p.scale), f1 = dec_weight(st.m1, M1, p.scale);
+  const float f0 = dec_weight(st.m0, M0, p.scale2), f1 = dec_weight(st.m1, M1, p.scale2);
   if (lg == 0) {
     sm.wl[warp][2 * lc] = st.l0 * f0;
     sm.wl[warp][2 * lc + 1] = st.l1 * f1;
@@ -459,39 +471,34 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
     __syncthreads();
   }
 
-  // rank 0: the C partials of this cluster, in rank order
-  if (threadIdx.x < rep) {
-    const int r = threadIdx.x;
-    float M = -INFINITY;
-    for (int cc = 0; cc < C; ++cc) M = fmaxf(M, sm.cm[cc][r]);
-    float L = 0.f;
-    for (int cc = 0; cc < C; ++cc) {
-      const float wt = dec_weight(sm.cm[cc][r], M, p.scale);
-      L += sm.cl[cc][r] * wt;
-      sm.cl[cc][r] = wt;                // weight of rank cc from here on
-    }
-    sm.cm[0][r] = M;
-    sm.L[r] = L;
-  }
-  __syncthreads();
+  // rank 0: the C partials of this cluster, in rank order (weights recomputed per element)
   const int stride = 2 * rep + E;
   float* gpart = X > 1 ? p.part + (static_cast<int64_t>(g) * X + grp) * stride : nullptr;
   for (int i = threadIdx.x; i < E; i += kDecThreads) {
     const int r = i / HD;
-    float O = 0.f;
+    float M = -INFINITY;
 #pragma unroll
     for (int cc = 0; cc < kDecCluster; ++cc)
-      if (cc < C) O += co[cc * E + i] * sm.cl[cc][r];
-    if (X == 1)
-      p.out[static_cast<int64_t>(g) * E + i] = O / sm.L[r];
-    else
+      if (cc < C) M = fmaxf(M, sm.cm[cc][r]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < kDecCluster; ++cc)
+      if (cc < C) {
+        const float wt = dec_weight(sm.cm[cc][r], M, p.scale2);
+        O += co[cc * E + i] * wt;
+        L += sm.cl[cc][r] * wt;
+      }
+    if (X == 1) {
+      p.out[static_cast<int64_t>(g) * E + i] = O / L;
+    } else {
       gpart[2 * rep + i] = O;
+      if (i - r * HD == 0) {
+        gpart[r] = M;
+        gpart[rep + r] = L;
+      }
+    }
   }
   if (X == 1) return;
-  if (threadIdx.x < rep) {
-    gpart[threadIdx.x] = sm.cm[0][threadIdx.x];
-    gpart[rep + threadIdx.x] = sm.L[threadIdx.x];
-  }
   // arrival: the barrier orders this CTA's stores before thread 0's fence and atomic
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -504,35 +511,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   if (!sm.last) return;
   // the last cluster of kv head g adds the X cluster partials in order
   const float* pg = p.part + static_cast<int64_t>(g) * X * stride;
-  if (threadIdx.x < X * rep) {
-    const int x = threadIdx.x / rep, r = threadIdx.x - x * rep;
-    sm.cm[x][r] = __ldcg(pg + x * stride + r);
-    sm.cl[x][r] = __ldcg(pg + x * stride + rep + r);
-  }
-  __syncthreads();
-  if (threadIdx.x < rep) {
-    const int r = threadIdx.x;
-    float M = -INFINITY;
-    for (int x = 0; x < X; ++x) M = fmaxf(M, sm.cm[x][r]);
-    float L = 0.f;
-    for (int x = 0; x < X; ++x) {
-      const float wt = dec_weight(sm.cm[x][r], M, p.scale);
-      L += sm.cl[x][r] * wt;
-      sm.cl[x][r] = wt;
-    }
-    sm.L[r] = L;
-  }
-  __syncthreads();
   for (int i = threadIdx.x; i < E; i += kDecThreads) {
     const int r = i / HD;
-    float v[kDecMaxGroups];
+    float m[kDecMaxGroups], l[kDecMaxGroups], v[kDecMaxGroups];
 #pragma unroll
-    for (int x = 0; x < kDecMaxGroups; ++x) v[x] = x < X ? __ldcg(pg + x * stride + 2 * rep + i) : 0.f;
-    float O = 0.f;
+    for (int x = 0; x < kDecMaxGroups; ++x) {
+      m[x] = x < X ? __ldcg(pg + x * stride + r) : -INFINITY;
+      l[x] = x < X ? __ldcg(pg + x * stride + rep + r) : 0.f;
+      v[x] = x < X ? __ldcg(pg + x * stride + 2 * rep + i) : 0.f;
+    }
+    float M = -INFINITY;
 #pragma unroll
-    for (int x = 0; x < kDecMaxGroups; ++x)
-      if (x < X) O += v[x] * sm.cl[x][r];
-    p.out[static_cast<int64_t>(g) * E + i] = O / sm.L[r];
+    for (int x = 0; x < kDecMaxGroups; ++x) M = fmaxf(M, m[x]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int x = 0; x < kDecMaxGroups; ++x) {
+      const float wt = dec_weight(m[x], M, p.scale2);
+      O += v[x] * wt;
+      L += l[x] * wt;
+    }
+    p.out[static_cast<int64_t>(g) * E + i] = O / L;
   }
   if (threadIdx.x == 0) p.count[g] = 0u;
 }
@@ -783,9 +781,13 @@ inline int decode_cluster(int t) {
   while (c < kDecCluster && 2 * c * kDecMinChunk <= t) c *= 2;
   return c;
 }
-// Clusters per kv head X: one per kDecGroupChunk positions, at most kDecMaxGroups.
+// Up to kDecSingleCluster positions one cluster per kv head adds all partials in distributed
+// shared memory; longer caches take X clusters of 4 (twice as many of them fit on the device
+// at once as clusters of 8) and add the X cluster partials through the workspace.
+constexpr int kDecSingleCluster = 6144;
+constexpr int kDecLongCluster = 4;
 inline int decode_max_groups(int t) {
-  return decode_cluster(t) < kDecCluster ? 1 : std::min(kDecMaxGroups, (t + kDecGroupChunk - 1) / kDecGroupChunk);
+  return t <= kDecSingleCluster ? 1 : std::min(kDecMaxGroups, (t + kDecGroupChunk - 1) / kDecGroupChunk);
 }
 inline int64_t decode_counter_bytes(int nkv) { return (static_cast<int64_t>(nkv) * 4 + 255) / 256 * 256; }
 inline int64_t decode_group_bytes(int nq, int nkv, int hd) {
@@ -793,39 +795,51 @@ inline int64_t decode_group_bytes(int nq, int nkv, int hd) {
   return static_cast<int64_t>(2 * rep + rep * hd) * 4;
 }
 
-// Splits S = C * X of the cache per kv head; X is also bounded by the number of 8-CTA
-// clusters the device runs at once, so that the grid is one wave.
+// Clusters of C CTAs the device runs at once (one CTA per SM).
 template <int HD>
-int decode_splits(int nkv, int t, int* C, int* X) {
+int decode_active_clusters(int C, int* n) {
   static std::mutex mu;
-  static int cached[64] = {};
+  static int cached[64][4] = {};
   int dev = 0;
   PYRE_CUDA_TRY(cudaGetDevice(&dev));
-  int clusters = 0;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    int& c = cached[dev & 63];
-    if (c == 0) {
-      int rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD>), dec_dyn_bytes<HD>(kDecMaxRep));
-      if (rc) return rc;
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(kDecCluster, 1, 1);
-      cfg.blockDim = dim3(kDecThreads, 1, 1);
-      cfg.dynamicSmemBytes = static_cast<size_t>(dec_dyn_bytes<HD>(kDecMaxRep));
-      cudaLaunchAttribute attr{};
-      attr.id = cudaLaunchAttributeClusterDimension;
-      attr.val.clusterDim.x = kDecCluster;
-      attr.val.clusterDim.y = 1;
-      attr.val.clusterDim.z = 1;
-      cfg.attrs = &attr;
-      cfg.numAttrs = 1;
-      PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&c, attn_decode_kernel<HD>, &cfg));
-      c = std::max(1, c);
-    }
-    clusters = c;
+  const int slot = C == 8 ? 3 : C == 4 ? 2 : C == 2 ? 1 : 0;
+  std::lock_guard<std::mutex> lock(mu);
+  int& c = cached[dev & 63][slot];
+  if (c == 0) {
+    int rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD>), dec_dyn_bytes<HD>(kDecMaxRep));
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(C), 1, 1);
+    cfg.blockDim = dim3(kDecThreads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(dec_dyn_bytes<HD>(kDecMaxRep));
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(C);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&c, attn_decode_kernel<HD>, &cfg));
+    c = std::max(1, c);
   }
+  *n = c;
+  return PYRE_OK;
+}
+
+// Splits S = C * X of the cache per kv head, with the grid in one wave.
+template <int HD>
+int decode_splits(int nkv, int t, int* C, int* X) {
   *C = decode_cluster(t);
-  *X = std::max(1, std::min(decode_max_groups(t), clusters / nkv));
+  *X = 1;
+  if (t <= kDecSingleCluster) return PYRE_OK;
+  int n = 0;
+  int rc = decode_active_clusters<HD>(kDecLongCluster, &n);
+  if (rc) return rc;
+  const int x = std::min(decode_max_groups(t), n / nkv);
+  if (x >= 2) {
+    *C = kDecLongCluster;
+    *X = x;
+  }
   return PYRE_OK;
 }
 }  // namespace attn
@@ -868,7 +882,7 @@ extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, cons
   p.max_t = max_t;
   p.mask_lo = mask_lo;
   p.mask_hi = mask_hi;
-  p.scale = 1.0f / sqrtf(static_cast<float>(hd));
+  p.scale2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   const int rep = nq / nkv;
   rc = hd == 64 ? set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<64>), dec_dyn_bytes<64>(kDecMaxRep))
                 : set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<128>), dec_dyn_bytes<128>(kDecMaxRep));
