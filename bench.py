@@ -175,7 +175,8 @@ def attention_bench(dev, stream, hbm, tf_burst):
         "decode": {"cache_len": t, "us_per_layer": round(dec_us, 2), "kv_bytes_per_layer": kv_bytes,
                    "gbs": round(kv_bytes / (dec_us * 1e-6) / 1e9, 1),
                    "frac_of_hbm": round(kv_bytes / (dec_us * 1e-6) / 1e9 / hbm, 4),
-                   "launches_per_layer": 2, "l2": f"{layers} layers' caches rotating"},
+                   "launches_per_layer": 1, "kernel": "attn_decode_kernel (RoPE + clip + KV append + flash-decoding, f16 mma.sync, cluster combine)",
+                   "l2": f"{layers} layers' caches rotating"},
         "prefill": {"tokens": S, "ms": round(pf_ms, 4), "tflops": round(flops / (pf_ms * 1e-3) / 1e12, 1),
                     "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / tf_burst, 4),
                     "kernel": "attn_prefill_kernel (f16 mma.sync, online softmax) + rope_append_kernel"},

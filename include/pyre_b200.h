@@ -237,6 +237,16 @@ PYRE_API int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const 
                               int nkv, int hd, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
                               int64_t ws_bytes, void* stream);
 
+/* One decode step of the attention block in one launch (root_node.py:900-933 then
+ * :1009-1031): RoPE of the token's q and k at position start_pos (the cache length before
+ * the step; table from pyre_rope_table), clip +-1000, append of k and v at row start_pos,
+ * then decode attention over positions 0..start_pos as pyre_attn_decode. q: f32 [nq * hd];
+ * k, v: f32 [nkv * hd]; same workspace as pyre_attn_decode. */
+PYRE_API int pyre_attn_decode_step(const float* q, const float* k, const float* v, int start_pos,
+                                   const float* rope_table, double rope_fraction, int nq, int nkv, int hd,
+                                   uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo, int mask_hi,
+                                   float* out, void* workspace, int64_t ws_bytes, void* stream);
+
 /* ---- Ulysses sequence parallelism over NVLink (one process per GPU, P <= 16) ----------
  * Replaces the gather of every node's q/k/v at the root over TCP and the full-sequence
  * attention there (src/orchestrator/root_node.py:250-314; Ulysses mode :110): rank r owns

@@ -75,6 +75,8 @@ _SIGNATURES = {
     "pyre_attn_prefill": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp],
     "pyre_attn_decode_workspace_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_attn_decode": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _c_i64, _vp],
+    "pyre_attn_decode_step": [_vp, _vp, _vp, _i, _vp, ctypes.c_double, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp,
+                              _c_i64, _vp],
     "pyre_ulysses_buffer_bytes": [_i, _i, _i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_ulysses_rope_scatter": [_vp, _i, _i, _vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _vp,
                                   ctypes.c_double, _vp],

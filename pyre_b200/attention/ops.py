@@ -155,11 +155,18 @@ class AttentionOp:
         prefill_max_seq) of the cache are masked. Returns f32 ``[1, n_heads * head_dim]``."""
         if q.shape[0] != 1:
             raise ValueError("decode takes one token")
-        q_out = self._append(q, k, v, stream)
-        t = self.cache.length
+        for x, n in ((q, self.nq), (k, self.nkv), (v, self.nkv)):
+            if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != n * self.hd or not x.is_contiguous():
+                raise ValueError(f"q, k, v must be contiguous f32 [1, heads * {self.hd}]")
+        start = self.cache.length
+        if start + 1 > self.cache.max_t:
+            raise ValueError("KV cache full")
         out = torch.empty((1, self.nq * self.hd), dtype=torch.float32, device=q.device)
         lo, hi = (int(prefill_real), int(prefill_max_seq)) if prefill_max_seq > prefill_real else (0, 0)
         ws = self.dec_ws
-        N.call("pyre_attn_decode", D.ptr(q_out), D.ptr(self.cache.k), D.ptr(self.cache.v), t, self.nq, self.nkv,
-               self.hd, self.cache.max_t, lo, hi, D.ptr(out), D.ptr(ws), ws.numel(), D.stream_ptr(stream))
+        # RoPE + clip + KV append + flash-decoding in one launch
+        N.call("pyre_attn_decode_step", D.ptr(q), D.ptr(k), D.ptr(v), start, D.ptr(self.rope), self.frac, self.nq,
+               self.nkv, self.hd, D.ptr(self.cache.k), D.ptr(self.cache.v), self.cache.max_t, lo, hi, D.ptr(out),
+               D.ptr(ws), ws.numel(), D.stream_ptr(stream))
+        self.cache.length = start + 1
         return out

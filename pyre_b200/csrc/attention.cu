@@ -97,6 +97,21 @@ __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restri
 constexpr int kRopeMaxHalf = 256;
 constexpr int kRopeHeadsPerCta = 8;
 
+// Element i of a rotated, clipped head (rotate-half pairs (i, i + half), cos/sin from the
+// table row of the position, dims >= 2 * half pass through), as rope_append_kernel and the
+// fused decode step both store it.
+__device__ __forceinline__ float rope_clip(const float* __restrict__ src, int i, int half, float c, float s) {
+  float r;
+  if (i < 2 * half) {
+    const int jj = i < half ? i : i - half;
+    const float x1 = __ldg(src + jj), x2 = __ldg(src + jj + half);
+    r = i < half ? x1 * c - x2 * s : x1 * s + x2 * c;
+  } else {
+    r = __ldg(src + i);
+  }
+  return fminf(fmaxf(r, -1000.f), 1000.f);
+}
+
 
 __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v, int64_t q_stride,
@@ -123,15 +138,8 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
     const bool is_q = hh < nq;
     const int h = is_q ? hh : hh - nq;
     const float* src = is_q ? q + t * q_stride + static_cast<int64_t>(h) * hd : k + t * kv_stride + static_cast<int64_t>(h) * hd;
-    float r;
-    if (i < 2 * half) {
-      const int jj = i < half ? i : i - half;
-      const float x1 = __ldg(src + jj), x2 = __ldg(src + jj + half);
-      r = i < half ? x1 * cs[jj] - x2 * sn[jj] : x1 * sn[jj] + x2 * cs[jj];
-    } else {
-      r = __ldg(src + i);
-    }
-    r = fminf(fmaxf(r, -1000.f), 1000.f);
+    const int jj = i < 2 * half ? (i < half ? i : i - half) : 0;
+    const float r = rope_clip(src, i, half, half ? cs[jj] : 0.f, half ? sn[jj] : 0.f);
     if (is_q)
       q_out[(static_cast<int64_t>(h) * T + t) * hd + i] = __float2half_rn(r);
     else
@@ -214,9 +222,16 @@ constexpr int kDecMinChunk = 128;      // positions per CTA at least (one batch 
 constexpr int kDecGroupChunk = 2048;   // positions per cluster before another cluster is added
 
 struct DecodeParams {
-  const __half* q;       // [nq, hd] rotated, clipped
+  const __half* q;       // [nq, hd] rotated, clipped (attention alone)
   const __half* kc;      // [nkv, max_t, hd]
   const __half* vc;
+  const float* qf;       // fused decode step: the token's f32 q [nq * hd], k and v [nkv * hd],
+  const float* kf;       // rotated at position t - 1 (rope row), clipped, k and v appended
+  const float* vf;       // to the caches at row t - 1 by the CTAs of the last split
+  const float2* rope;    // (cos, sin) [half] of position t - 1
+  int half;
+  __half* kw;            // kc, vc as written by the append
+  __half* vw;
   float* out;            // [nq * hd]
   float* part;           // [nkv][X][2 * rep + rep * hd]: max, sum, weighted values per cluster
   unsigned* count;       // [nkv] arrival counters, zero between launches
@@ -270,16 +285,30 @@ __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
+// 16 bytes of the cache: through the read-only path, or (COH, when this kernel appends a
+// row that its own CTA then reads) a plain load, ordered after the appending stores by the
+// CTA barrier.
+template <bool COH>
+__device__ __forceinline__ uint4 ld_row16(const __half* p) {
+  if constexpr (!COH) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+  } else {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+  }
+}
+
 // Rows past the chunk end (last) are clamped to it; their scores are masked.
-template <int HD>
+template <int HD, bool COH>
 __device__ __forceinline__ void dec_load(DecodeRows<HD>& b, const __half* kh, const __half* vh, int base, int last,
                                          int lg, int lc) {
   const __half* ka = kh + static_cast<int64_t>(min(base + lg, last)) * HD + 8 * lc;
   const __half* kb = kh + static_cast<int64_t>(min(base + lg + 8, last)) * HD + 8 * lc;
 #pragma unroll
   for (int j = 0; j < HD / 32; ++j) {
-    b.ka[j] = __ldg(reinterpret_cast<const uint4*>(ka + 32 * j));
-    b.kb[j] = __ldg(reinterpret_cast<const uint4*>(kb + 32 * j));
+    b.ka[j] = ld_row16<COH>(ka + 32 * j);
+    b.kb[j] = ld_row16<COH>(kb + 32 * j);
   }
   const __half* va = vh + static_cast<int64_t>(min(base + 2 * lc, last)) * HD;
   const __half* vb = vh + static_cast<int64_t>(min(base + 2 * lc + 1, last)) * HD;
@@ -288,10 +317,10 @@ __device__ __forceinline__ void dec_load(DecodeRows<HD>& b, const __half* kh, co
 #pragma unroll
   for (int j = 0; j < HD / 64; ++j) {
     const int d = dec_vdim<HD>(lg, j);
-    b.va[j] = __ldg(reinterpret_cast<const uint4*>(va + d));
-    b.vb[j] = __ldg(reinterpret_cast<const uint4*>(vb + d));
-    b.vc[j] = __ldg(reinterpret_cast<const uint4*>(vc + d));
-    b.vd[j] = __ldg(reinterpret_cast<const uint4*>(vd + d));
+    b.va[j] = ld_row16<COH>(va + d);
+    b.vb[j] = ld_row16<COH>(vb + d);
+    b.vc[j] = ld_row16<COH>(vc + d);
+    b.vd[j] = ld_row16<COH>(vd + d);
   }
 }
 
@@ -352,7 +381,7 @@ __device__ __forceinline__ void dec_batch(const DecodeRows<HD>& b, const uint4 (
   }
 }
 
-template <int HD>
+template <int HD, bool FUSED>
 __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const DecodeParams p) {
   namespace cg = cooperative_groups;
   constexpr int KS = HD / 16;
@@ -375,11 +404,37 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, lg = lane >> 2, lc = lane & 3;
 
   uint4 qv[KQ];
+  if constexpr (FUSED) {
+    // RoPE + clip of this kv head's query heads into shared memory; the last split appends
+    // the token's rotated k and clipped v at row t - 1 before any of its warps reads it
+    __shared__ __align__(16) __half qs[kDecMaxRep * HD];
+    const int pos = p.t - 1;
+    for (int e = threadIdx.x; e < E; e += kDecThreads) {
+      const int r = e / HD, i = e - r * HD;
+      const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
+      const float2 cs = p.half ? __ldg(p.rope + jj) : make_float2(0.f, 0.f);
+      qs[e] = __float2half_rn(rope_clip(p.qf + (static_cast<int64_t>(g) * rep + r) * HD, i, p.half, cs.x, cs.y));
+    }
+    if (split == S - 1) {
+      for (int i = threadIdx.x; i < HD; i += kDecThreads) {
+        const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
+        const float2 cs = p.half ? __ldg(p.rope + jj) : make_float2(0.f, 0.f);
+        const int64_t row = (static_cast<int64_t>(g) * p.max_t + pos) * HD;
+        p.kw[row + i] = __float2half_rn(rope_clip(p.kf + static_cast<int64_t>(g) * HD, i, p.half, cs.x, cs.y));
+        p.vw[row + i] = __float2half_rn(fminf(fmaxf(__ldg(p.vf + static_cast<int64_t>(g) * HD + i), -1000.f), 1000.f));
+      }
+    }
+    __syncthreads();
 #pragma unroll
-  for (int j = 0; j < KQ; ++j)
-    qv[j] = lg < rep ? __ldg(reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(g) * rep + lg) * HD + 32 * j +
-                                                            8 * lc))
-                     : make_uint4(0u, 0u, 0u, 0u);
+    for (int j = 0; j < KQ; ++j)
+      qv[j] = lg < rep ? *reinterpret_cast<const uint4*>(qs + lg * HD + 32 * j + 8 * lc) : make_uint4(0u, 0u, 0u, 0u);
+  } else {
+#pragma unroll
+    for (int j = 0; j < KQ; ++j)
+      qv[j] = lg < rep ? __ldg(reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(g) * rep + lg) * HD +
+                                                              32 * j + 8 * lc))
+                       : make_uint4(0u, 0u, 0u, 0u);
+  }
   const __half* kh = p.kc + static_cast<int64_t>(g) * p.max_t * HD;
   const __half* vh = p.vc + static_cast<int64_t>(g) * p.max_t * HD;
   float o[KS][4];
@@ -390,13 +445,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   constexpr int kStep = kDecWarps * kDecBatch;
   DecodeRows<HD> r0, r1;
   int base = c0 + warp * kDecBatch;
-  if (base < c1) dec_load(r0, kh, vh, base, c1 - 1, lg, lc);
+  if (base < c1) dec_load<HD, FUSED>(r0, kh, vh, base, c1 - 1, lg, lc);
   while (base < c1) {
-    if (base + kStep < c1) dec_load(r1, kh, vh, base + kStep, c1 - 1, lg, lc);
+    if (base + kStep < c1) dec_load<HD, FUSED>(r1, kh, vh, base + kStep, c1 - 1, lg, lc);
     dec_batch(r0, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale2, lg);
     base += kStep;
     if (base >= c1) break;
-    if (base + kStep < c1) dec_load(r0, kh, vh, base + kStep, c1 - 1, lg, lc);
+    if (base + kStep < c1) dec_load<HD, FUSED>(r0, kh, vh, base + kStep, c1 - 1, lg, lc);
     dec_batch(r1, qv, o, st, base, c1, p.mask_lo, p.mask_hi, p.scale2, lg);
     base += kStep;
   }
@@ -806,7 +861,7 @@ int decode_active_clusters(int C, int* n) {
   std::lock_guard<std::mutex> lock(mu);
   int& c = cached[dev & 63][slot];
   if (c == 0) {
-    int rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD>), dec_dyn_bytes<HD>(kDecMaxRep));
+    int rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD, true>), dec_dyn_bytes<HD>(kDecMaxRep));
     if (rc) return rc;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(C), 1, 1);
@@ -819,7 +874,7 @@ int decode_active_clusters(int C, int* n) {
     attr.val.clusterDim.z = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&c, attn_decode_kernel<HD>, &cfg));
+    PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&c, attn_decode_kernel<HD, true>, &cfg));
     c = std::max(1, c);
   }
   *n = c;
@@ -852,6 +907,43 @@ extern "C" int pyre_attn_decode_workspace_bytes(int nq, int nkv, int hd, int t, 
   return PYRE_OK;
 }
 
+namespace pyre {
+namespace attn {
+// Shared by the attention-only call and the fused decode step: splits, workspace check,
+// cluster launch.
+template <int HD, bool FUSED>
+int launch_decode(DecodeParams p, void* workspace, int64_t ws_bytes, cudaStream_t stream) {
+  int C = 1, X = 1;
+  int rc = decode_splits<HD>(p.nkv, p.t, &C, &X);
+  if (rc) return rc;
+  const int64_t need = decode_counter_bytes(p.nkv) + static_cast<int64_t>(p.nkv) * X * decode_group_bytes(p.nq, p.nkv, HD);
+  if (X > 1)
+    PYRE_CHECK_ARG(workspace != nullptr && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 && ws_bytes >= need,
+                   "pyre_attn_decode: workspace missing, misaligned or smaller than pyre_attn_decode_workspace_bytes");
+  p.count = static_cast<unsigned*>(workspace);
+  p.part = X > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + decode_counter_bytes(p.nkv)) : nullptr;
+  p.scale2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  rc = set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<HD, FUSED>), dec_dyn_bytes<HD>(kDecMaxRep));
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(C * X), static_cast<unsigned>(p.nkv), 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(dec_dyn_bytes<HD>(p.nq / p.nkv));
+  cfg.stream = stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(C);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, FUSED>, p));
+  PYRE_LAUNCH_CHECK("attn_decode_kernel");
+  return PYRE_OK;
+}
+}  // namespace attn
+}  // namespace pyre
+
 extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int t, int nq,
                                 int nkv, int hd, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
                                 int64_t ws_bytes, void* stream) {
@@ -862,49 +954,56 @@ extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, cons
   PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(k_cache) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(v_cache) % 16 == 0,
                  "pyre_attn_decode: q and the caches must be 16-byte aligned");
-  int C = 1, X = 1;
-  int rc = hd == 64 ? decode_splits<64>(nkv, t, &C, &X) : decode_splits<128>(nkv, t, &C, &X);
-  if (rc) return rc;
-  const int64_t need = decode_counter_bytes(nkv) + static_cast<int64_t>(nkv) * X * decode_group_bytes(nq, nkv, hd);
-  if (X > 1)
-    PYRE_CHECK_ARG(workspace != nullptr && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 && ws_bytes >= need,
-                   "pyre_attn_decode: workspace missing, misaligned or smaller than pyre_attn_decode_workspace_bytes");
   DecodeParams p{};
   p.q = reinterpret_cast<const __half*>(q);
   p.kc = reinterpret_cast<const __half*>(k_cache);
   p.vc = reinterpret_cast<const __half*>(v_cache);
   p.out = out;
-  p.count = static_cast<unsigned*>(workspace);
-  p.part = X > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + decode_counter_bytes(nkv)) : nullptr;
   p.nq = nq;
   p.nkv = nkv;
   p.t = t;
   p.max_t = max_t;
   p.mask_lo = mask_lo;
   p.mask_hi = mask_hi;
-  p.scale2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
-  const int rep = nq / nkv;
-  rc = hd == 64 ? set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<64>), dec_dyn_bytes<64>(kDecMaxRep))
-                : set_smem_limit(reinterpret_cast<const void*>(attn_decode_kernel<128>), dec_dyn_bytes<128>(kDecMaxRep));
-  if (rc) return rc;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(C * X), static_cast<unsigned>(nkv), 1);
-  cfg.blockDim = dim3(kDecThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(hd == 64 ? dec_dyn_bytes<64>(rep) : dec_dyn_bytes<128>(rep));
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr{};
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = static_cast<unsigned>(C);
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  if (hd == 64)
-    PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, p));
-  else
-    PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, p));
-  PYRE_LAUNCH_CHECK("attn_decode_kernel");
-  return PYRE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return hd == 64 ? launch_decode<64, false>(p, workspace, ws_bytes, st)
+                  : launch_decode<128, false>(p, workspace, ws_bytes, st);
+}
+
+extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float* v, int start_pos,
+                                     const float* rope_table, double rope_fraction, int nq, int nkv, int hd,
+                                     uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo, int mask_hi,
+                                     float* out, void* workspace, int64_t ws_bytes, void* stream) {
+  PYRE_CHECK_ARG(q && k && v && k_cache && v_cache && out, "pyre_attn_decode_step: null pointer");
+  PYRE_CHECK_ARG(start_pos >= 0 && start_pos < max_t && nkv >= 1 && nq % nkv == 0 && nq / nkv <= kDecMaxRep,
+                 "pyre_attn_decode_step: bad sizes (cache full, or more than 8 query heads per kv head)");
+  PYRE_CHECK_ARG(hd == 64 || hd == 128, "pyre_attn_decode_step: head dim must be 64 or 128");
+  PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(k_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(v_cache) % 16 == 0,
+                 "pyre_attn_decode_step: the caches must be 16-byte aligned");
+  const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
+  PYRE_CHECK_ARG(dims >= 0 && dims <= hd, "pyre_attn_decode_step: rope_fraction must be in [0, 1]");
+  const int half = dims >= 2 ? dims / 2 : 0;
+  PYRE_CHECK_ARG(rope_table != nullptr || half == 0, "pyre_attn_decode_step: null RoPE table");
+  DecodeParams p{};
+  p.kc = reinterpret_cast<const __half*>(k_cache);
+  p.vc = reinterpret_cast<const __half*>(v_cache);
+  p.kw = reinterpret_cast<__half*>(k_cache);
+  p.vw = reinterpret_cast<__half*>(v_cache);
+  p.qf = q;
+  p.kf = k;
+  p.vf = v;
+  p.rope = half ? reinterpret_cast<const float2*>(rope_table) + static_cast<int64_t>(start_pos) * half : nullptr;
+  p.half = half;
+  p.out = out;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.t = start_pos + 1;
+  p.max_t = max_t;
+  p.mask_lo = mask_lo;
+  p.mask_hi = mask_hi;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return hd == 64 ? launch_decode<64, true>(p, workspace, ws_bytes, st)
+                  : launch_decode<128, true>(p, workspace, ws_bytes, st);
 }
 
 namespace pyre {

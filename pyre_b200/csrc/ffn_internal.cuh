@@ -37,41 +37,12 @@ __device__ __forceinline__ void store_out(void* out, int out_bf16, int N, int t,
 }
 
 // Cross-rank sum of one finished tile (the reference's `ffn_out += partial`,
-// src/orchestrator/root_node.py:582-594): push the partial into every rank's receive slot
-// (self included) over NVLink, release a flag per peer, wait (bounded) for every peer's
-// flag of this tile and add the partials in rank order 0..world-1 into out.
-template <int T>
-__device__ void tp_reduce_tile(const comm::DevComm& c, uint32_t epoch, int tile, const float* fin, float* out, int N,
-                               int tid) {
-  const int slot = epoch & 1u;
-  const int n = T * kTileN;
-  for (int peer = 0; peer < c.world; ++peer) {
-    float* dst = comm::fused_slot(c, peer, slot, c.rank) + static_cast<int64_t>(tile) * n;
-    for (int i = tid; i < n; i += kConsumers) dst[i] = fin[i];
-  }
-  __threadfence_system();
-  consumer_sync();
-  if (tid < c.world) st_release_sys(comm::fused_flag(c, tid, slot, c.rank, tile), epoch);
-  if (tid < c.world) {
-    if (!wait_flag_eq(comm::fused_flag(c, c.rank, slot, tid, tile), epoch, c.timeout_ns))
-      atomicExch(c.status, PYRE_ETIMEOUT);
-  }
-  consumer_sync();
-  for (int i = tid; i < n; i += kConsumers) {
-    const int t = i / kTileN, cc = i % kTileN;
-    const int col = tile * kTileN + cc;
-    if (col >= N) continue;
-    float acc = 0.f;
-    for (int src = 0; src < c.world; ++src)
-      acc += __ldcg(comm::fused_slot(c, c.rank, slot, src) + static_cast<int64_t>(tile) * n + i);
-    out[static_cast<int64_t>(t) * N + col] = acc;
-  }
-}
-
-// Split form of tp_reduce_tile for kernels that schedule work dynamically (the chunk to CTA
-// map differs between ranks, so a CTA must never block on a peer while it still holds
-// unprocessed work): tp_push_tile() pushes and flags without waiting; tp_finish_tile()
-// waits for every peer's flag of the tile and sums, called after all work is drained.
+// src/orchestrator/root_node.py:582-594), split for kernels that schedule work dynamically
+// (the chunk to CTA map differs between ranks, so a CTA must never block on a peer while it
+// still holds unprocessed work): tp_push_tile() pushes the partial into every rank's receive
+// slot (self included) over NVLink and releases a flag per peer without waiting;
+// tp_finish_tile() waits (bounded) for every peer's flag of the tile and adds the partials in
+// rank order 0..world-1, called after all work is drained.
 template <int T>
 __device__ void tp_push_tile(const comm::DevComm& c, uint32_t epoch, int tile, const float* fin, int tid) {
   const int slot = epoch & 1u;
@@ -109,22 +80,6 @@ __device__ void tp_finish_tile(const comm::DevComm& c, uint32_t epoch, int tile,
 template <typename K>
 int set_smem_once(K kern, int bytes) {
   return set_smem_limit(reinterpret_cast<const void*>(kern), bytes);
-}
-
-// Co-resident grid for a kernel: never more CTAs than fit at once (the tensor-parallel
-// epilogues and the per-slab ready flags wait on other CTAs), capped by want_per_sm and the
-// work.
-template <typename K>
-int coresident_grid(K kern, int threads, int smem, int want_per_sm, int64_t units, int* grid) {
-  int occ = 0;
-  PYRE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem));
-  if (occ < 1) return set_error(PYRE_ECUDA, "kernel does not fit on an SM");
-  if (occ > want_per_sm) occ = want_per_sm;
-  int64_t g = static_cast<int64_t>(occ) * sm_count();
-  if (g > kMaxGrid) g = kMaxGrid;
-  if (g > units) g = units;
-  *grid = static_cast<int>(g < 1 ? 1 : g);
-  return PYRE_OK;
 }
 
 }  // namespace ffn

@@ -168,72 +168,7 @@ __device__ __forceinline__ void reduce_tile(float2 (&acc)[NMAT][T][8], float* re
   consumer_sync();
 }
 
-// CTA whose unit range [c*U/G, (c+1)*U/G) contains unit index x.
-__host__ __device__ __forceinline__ int cta_of_unit(int64_t x, int64_t U, int G) {
-  return static_cast<int>(((x + 1) * G - 1) / U);
-}
-
-// Stream-K fix-up of a tile shared by CTAs cf..cl: every CTA stores its piece; the last to
-// arrive adds all pieces in piece (= CTA) order into fin and returns true. A CTA that owns
-// the whole tile returns true at once. ws holds [tiles, pmax, NMAT*T*kTileN] floats.
-template <int T, int NMAT>
-__device__ __forceinline__ bool fixup_tile(float* fin, float* ws, unsigned int* counters, int pmax, int tile, int c,
-                                           int cf, int cl, int* s_last, int tid) {
-  if (cf == cl) return true;
-  constexpr int kItems = NMAT * T * kTileN;
-  const int piece = c - cf;
-  const int np = cl - cf + 1;
-  float* slot = ws + (static_cast<int64_t>(tile) * pmax + piece) * kItems;
-  for (int i = tid; i < kItems; i += kConsumers) __stcg(slot + i, fin[i]);
-  __threadfence();
-  consumer_sync();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(counters + tile, 1u);
-    *s_last = (prev == static_cast<unsigned>(np - 1));
-  }
-  consumer_sync();
-  if (!*s_last) return false;
-  __threadfence();
-  const float* base = ws + static_cast<int64_t>(tile) * pmax * kItems;
-  for (int i = tid; i < kItems; i += kConsumers) {
-    // all piece loads in flight at once, then summed in piece order
-    float v = 0.f;
-    for (int pc0 = 0; pc0 < np; pc0 += 16) {
-      float pv[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        pv[j] = (pc0 + j < np) ? __ldcg(base + static_cast<int64_t>(pc0 + j) * kItems + i) : 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (pc0 + j < np) v += pv[j];
-    }
-    fin[i] = v;
-  }
-  consumer_sync();
-  if (tid == 0) counters[tile] = 0u;
-  return true;
-}
-
-// Largest number of pieces any tile has for a grid of G CTAs.
-inline int pmax_for(int tiles, int upt, int G) {
-  const int64_t U = static_cast<int64_t>(tiles) * upt;
-  int pm = 1;
-  for (int t = 0; t < tiles; ++t) {
-    const int64_t u0 = static_cast<int64_t>(t) * upt;
-    const int np = cta_of_unit(u0 + upt - 1, U, G) - cta_of_unit(u0, U, G) + 1;
-    pm = pm > np ? pm : np;
-  }
-  return pm;
-}
-
 inline int tiles_of(int N) { return (N + kTileN - 1) / kTileN; }
-
-// Upper bound of a piece region for any grid <= kMaxGrid.
-inline int64_t pieces_bytes(int T, int N, int nmat) {
-  const int tiles = tiles_of(N);
-  const int64_t pmax = (kMaxGrid + tiles - 1) / tiles + 1;
-  return static_cast<int64_t>(tiles) * pmax * nmat * T * kTileN * 4;
-}
 
 template <typename XT>
 inline CUtensorMapDataType tma_dtype();

@@ -171,6 +171,37 @@ def test_decode_long_cache(nq, nkv, hd, t):
         assert rel(out.cpu().numpy(), ref) < TOL_ATTN
 
 
+@pytest.mark.parametrize("hd,frac,t0", [(128, 1.0, 3000), (64, 0.5, 40), (128, 0.0, 7000)])
+def test_decode_step_fused_equals_rope_then_attention(hd, frac, t0):
+    """pyre_attn_decode_step (RoPE + clip + append + attention in one launch) against
+    pyre_rope_kv_append followed by pyre_attn_decode on a copy of the same cache, with a
+    masked range."""
+    from pyre_b200 import _device as D, _native as N
+    from pyre_b200.attention.ops import rope_table
+    nq, nkv, max_t = 16, 4, t0 + 4
+    rng = np.random.default_rng(hd + t0)
+    kc = torch.from_numpy((rng.standard_normal((nkv, max_t, hd)) * 2).astype(np.float16)).cuda()
+    vc = torch.from_numpy((rng.standard_normal((nkv, max_t, hd)) * 2).astype(np.float16)).cuda()
+    kc2, vc2 = kc.clone(), vc.clone()
+    q, k, v = (torch.from_numpy((rng.standard_normal((1, n * hd)) * 3).astype(np.float32)).cuda()
+               for n in (nq, nkv, nkv))
+    tab = rope_table(1e6, frac, hd, max_t, kc.device)
+    b = ctypes.c_int64(0)
+    N.call("pyre_attn_decode_workspace_bytes", nq, nkv, hd, max_t, ctypes.byref(b))
+    ws = torch.zeros(b.value, dtype=torch.uint8, device="cuda")
+    out = torch.empty(nq * hd, device="cuda")
+    N.call("pyre_attn_decode_step", D.ptr(q), D.ptr(k), D.ptr(v), t0, D.ptr(tab), frac, nq, nkv, hd, D.ptr(kc),
+           D.ptr(vc), max_t, 5, 9, D.ptr(out), D.ptr(ws), ws.numel(), D.stream_ptr())
+    q_out = torch.empty((nq, 1, hd), dtype=torch.float16, device="cuda")
+    N.call("pyre_rope_kv_append", D.ptr(q), D.ptr(k), D.ptr(v), q.stride(0), k.stride(0), 1, nq, nkv, hd, t0,
+           D.ptr(tab), frac, D.ptr(q_out), D.ptr(kc2), D.ptr(vc2), max_t, D.stream_ptr())
+    out2 = torch.empty(nq * hd, device="cuda")
+    N.call("pyre_attn_decode", D.ptr(q_out), D.ptr(kc2), D.ptr(vc2), t0 + 1, nq, nkv, hd, max_t, 5, 9, D.ptr(out2),
+           D.ptr(ws), ws.numel(), D.stream_ptr())
+    assert torch.equal(kc[:, :t0 + 1], kc2[:, :t0 + 1]) and torch.equal(vc[:, :t0 + 1], vc2[:, :t0 + 1])
+    assert torch.equal(out, out2)
+
+
 def test_ulysses_builder_projection():
     """build_ulysses_attention_graph through the session, on the reference's golden shards."""
     from pyre_b200.attention import ShardSpec, build_ulysses_attention_graph
