@@ -56,6 +56,13 @@ def parse():
     return ap.parse_args()
 
 
+def check_status(op, where):
+    """A timed run counts only if no kernel stopped early on a bounded wait."""
+    st = op.status()
+    if st != 0:
+        raise SystemExit(f"{where}: FFN kernel status {st} (a bounded wait ran out); the timing is invalid")
+
+
 def peaks():
     try:
         d = json.loads(PEAKS.read_text())
@@ -110,7 +117,9 @@ def attention_bench(dev, stream, hbm, tf_burst):
     Decode: one token per layer over a t = 2175 cache (the mean cache length of a
     2048-token prompt plus 256 generated tokens), RoPE + append + flash-decoding, 16 layers'
     caches rotating (151 MB > L2). Prefill: causal attention of a 2048-token prompt."""
+    import ctypes
     import torch
+    from pyre_b200 import _native as N
     from pyre_b200.attention import AttentionOp
     nq, nkv, hd, t, layers = 32, 8, 128, 2175, 16
     gen = torch.Generator(device=dev).manual_seed(3)
@@ -170,6 +179,10 @@ def attention_bench(dev, stream, hbm, tf_burst):
     stream.synchronize()
     pf_ms = e0.elapsed_time(e1) / reps
     flops = 2 * 2 * hd * nq * S * S / 2          # causal: half of q k^T and of p v
+    st = ctypes.c_int(0)
+    N.call("pyre_attn_status", ctypes.byref(st))
+    if st.value != 0:
+        raise SystemExit(f"attention kernel status {st.value} (a bounded wait ran out); the timing is invalid")
     return {
         "shape": "Mistral-7B attention: 32 q heads, 8 kv heads, head_dim 128, f16 KV cache",
         "decode": {"cache_len": t, "us_per_layer": round(dec_us, 2), "kv_bytes_per_layer": kv_bytes,
@@ -179,7 +192,7 @@ def attention_bench(dev, stream, hbm, tf_burst):
                    "l2": f"{layers} layers' caches rotating"},
         "prefill": {"tokens": S, "ms": round(pf_ms, 4), "tflops": round(flops / (pf_ms * 1e-3) / 1e12, 1),
                     "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / tf_burst, 4),
-                    "kernel": "attn_prefill_kernel (f16 mma.sync, online softmax) + rope_append_kernel"},
+                    "kernel": "attn_prefill_tc_kernel (tcgen05, S and O in tensor memory, TMA-fed) + rope_append_kernel"},
     }
 
 
@@ -383,6 +396,7 @@ def run_ours(args):
         e2e_runners[i % len(e2e_runners)].execute(xh)
     e2e_s = time.perf_counter() - t0
     barrier()
+    check_status(op, "decode and end-to-end")
 
     # prefill: T = 512 tokens per call, 4 weight sets rotating (prefill weight traffic is
     # amortised over 512 tokens; the GEMM is compute-bound)
@@ -414,6 +428,7 @@ def run_ours(args):
         barrier()
         pf_ms = p0.elapsed_time(p1) / n_pf
         prefill = {"tokens": TP, "ms_per_step": pf_ms}
+        check_status(op, "prefill")
 
     attn = None if args.no_attention else attention_bench(dev, stream, hbm, tf_burst)
     barrier()

@@ -61,6 +61,13 @@ PYRE_API int pyre_version(void);
  * truncated to len). Returns the length of the full message. */
 PYRE_API int pyre_last_error(char* buf, int len);
 
+/* One call of a captured op, end to end (the compiled model's execute(), root_node.py:574-580):
+ * copies in_bytes from host src into the pinned staging buffer stage_in that the graph's
+ * first node copies to the device, launches the instantiated CUDA graph exec
+ * (cudaGraphExec_t) on stream, and waits for it; the graph's last node has written the
+ * result to its pinned output buffer. in_bytes may be 0 (input already staged). */
+PYRE_API int pyre_graph_run(void* exec, void* stream, const void* src, void* stage_in, int64_t in_bytes);
+
 /* ---- Q8_0 format ------------------------------------------------------------------
  * pyre_q80_quantize replaces quantize_q80 (src/orchestrator/quantizer.py:11-26):
  *   flatten -> zero-pad to a multiple of 32 -> per block absmax (0 -> 1.0) ->
@@ -222,10 +229,16 @@ PYRE_API int pyre_rope_kv_append(const float* q, const float* k, const float* v,
 
 /* Causal prefill attention over positions 0..T-1 of the caches (root_node.py:292-307:
  * GQA q head h -> kv head h / (nq / nkv), q k^T / sqrt(hd), -inf above the diagonal, softmax,
- * probs @ v), f16 operands, f32 accumulation. q: f16 [nq, T, hd] (pyre_rope_kv_append);
- * out: f32 [T, nq * hd]. hd: 64 or 128. */
+ * probs @ v), f16 operands on the tcgen05 tensor cores, f32 accumulation. q: f16 [nq, T, hd]
+ * (pyre_rope_kv_append); out: f32 [T, nq * hd]. hd: 64 or 128. */
 PYRE_API int pyre_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int T, int nq,
                                int nkv, int hd, int max_t, float* out, void* stream);
+
+/* Device status of the prefill attention kernels on the current device (PYRE_OK, or
+ * PYRE_ETIMEOUT if a bounded pipeline wait ran out; that launch's output is incomplete).
+ * Synchronous: waits for the device, returns the word and clears it. No counterpart in the
+ * reference (its attention is host numpy). */
+PYRE_API int pyre_attn_status(int* status);
 
 /* Decode attention of one query token over cache positions 0..t-1 (root_node.py:1009-1031):
  * positions in [mask_lo, mask_hi) are masked (the reference's padded prefill). q: f16

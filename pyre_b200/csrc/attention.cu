@@ -18,8 +18,9 @@
 //                         scores / weighted values with an online softmax, partials added
 //                         in order through a cluster's distributed shared memory
 //                         (deterministic)
-//   attn_prefill_kernel   causal attention, 64 queries x 64 keys per step, f16 mma.sync with
-//                         f32 accumulation and an online softmax, GQA by kv head = h / rep
+//   attn_prefill_tc_kernel causal attention on tcgen05: 128 queries x 128 keys per step, S and
+//                         O accumulated in tensor memory, online softmax by one warpgroup,
+//                         TMA-fed, GQA by kv head = h / rep
 #include <cmath>
 
 #include <algorithm>
@@ -27,6 +28,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace pyre {
 namespace attn {
@@ -156,19 +158,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
 }
 
 // ---------------------------------------------------------------------------------------
-// Causal prefill attention. grid (nq, ceil(T / 64)), 128 threads (4 warps x 16 query rows).
-constexpr int kPM = 64, kPN = 64;
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
-}
+// Warp-level f16 MMA (m16n8k16, f32 accumulation) and f16 packing, used by decode attention.
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
@@ -176,14 +166,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
-  const int n = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src), "r"(n));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -603,167 +585,303 @@ struct PrefillParams {
   float* out_peers[16];
 };
 
-template <int HD>
-struct PrefillSmem {
-  static constexpr int kLd = HD + 8;   // padded row (halves): conflict-free ldmatrix
-  static constexpr int kQ = kPM * kLd;
-  static constexpr int kKV = kPN * kLd;
-  static constexpr int kBytes = (kQ + 4 * kKV) * 2;   // Q + double-buffered K and V
+// ---------------------------------------------------------------------------------------
+// Causal prefill attention on the 5th-generation tensor cores. CTA = (q head h, block of
+// 128 queries), heaviest blocks first; 192 threads:
+//   warp 0     TMA producer (Q once; K and V tiles of 128 keys into a 2-stage ring) and
+//              tensor-memory allocator;
+//   warp 1     MMA issuer (one thread): S_j = Q K_j^T into S buffer j % 2 of tensor memory
+//              (M = 128 queries, N = 128 keys, K = hd) and O += P_j V_j (N = hd, K = 128
+//              keys); S_{j+1} is issued before O += P_j V_j so the tensor core works while
+//              the softmax does;
+//   warps 2-5  softmax (thread = query row = tensor-memory lane): reads S_j, masks, runs the
+//              online softmax in base 2, writes P_j (f16) into shared memory in the A-operand
+//              layout; at the end O / l to the output.
+// The running maximum of a row is raised only when the row's maximum grows by more than 8
+// (base 2), so P <= 2^8 fits f16 and O (in tensor memory) is rescaled rarely; the rescale
+// waits for the previous O += P V. Q, K, V arrive by 3-D TMA with 128-byte swizzle
+// (positions past T read as zero); P is written in the same swizzled K-major layout.
+// Every mbarrier wait is bounded; a timeout is recorded in the attention status word.
+constexpr int kTcBM = 128, kTcBN = 128;
+constexpr int kTcThreads = 192;
+constexpr int kTcTmemCols = 512;   // S buffers 0..255, O 256..256+hd
+
+struct PrefillTcParams {
+  CUtensorMap tq, tk, tv;          // q [nq][T][hd]; k, v [nkv][T][hd] with row stride max_t * hd
+  float* out;                      // [T, nq * hd]
+  int T, nq, nkv;
+  float scale_log2;                // log2(e) / sqrt(hd)
+  int scatter, rows_per_rank, head_off, nq_total;
+  float* out_peers[16];
+  int* status;
 };
 
 template <int HD>
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillParams p) {
-  using S = PrefillSmem<HD>;
-  extern __shared__ __align__(16) __half sm[];
-  __half* qs = sm;
-  __half* ks = sm + S::kQ;              // [2][kPN][kLd]
-  __half* vs = ks + 2 * S::kKV;
-  // heaviest query blocks (most keys under the causal mask) first, all heads together
-  const int qb = gridDim.y - 1 - blockIdx.y, h = blockIdx.x;
-  const int g = h / (p.nq / p.nkv);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = qb * kPM;
-  const __half* qg = p.q + (static_cast<int64_t>(h) * p.T + q0) * HD;
-  const __half* kg = p.kc + static_cast<int64_t>(g) * p.max_t * HD;
-  const __half* vg = p.vc + static_cast<int64_t>(g) * p.max_t * HD;
-  constexpr int kChunks = HD / 8;       // 16-byte chunks per row
-  auto load_kv = [&](int kb, int buf) {
-    const int k0 = kb * kPN;
-    for (int i = threadIdx.x; i < kPN * kChunks; i += 128) {
-      const int r = i / kChunks, c = i % kChunks;
-      const bool ok = k0 + r < p.T;
-      const int rr = ok ? k0 + r : 0;
-      cp_async16(ks + buf * S::kKV + r * S::kLd + c * 8, kg + static_cast<int64_t>(rr) * HD + c * 8, ok);
-      cp_async16(vs + buf * S::kKV + r * S::kLd + c * 8, vg + static_cast<int64_t>(rr) * HD + c * 8, ok);
-    }
-  };
-  for (int i = threadIdx.x; i < kPM * kChunks; i += 128) {
-    const int r = i / kChunks, c = i % kChunks;
-    const bool ok = q0 + r < p.T;
-    cp_async16(qs + r * S::kLd + c * 8, qg + static_cast<int64_t>(ok ? r : 0) * HD + c * 8, ok);
-  }
-  load_kv(0, 0);
-  cp_async_commit();
+struct TcLayout {
+  static constexpr int kRegion = kTcBM * 128;                 // 128 rows x 128 bytes, swizzled
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + (HD / 64) * kRegion;          // 2 stages
+  static constexpr int kV = kK + 2 * (HD / 64) * kRegion;      // 2 stages
+  static constexpr int kP = kV + 2 * (HD / 64) * kRegion;      // 2 buffers x (128 keys = 2 regions)
+  static constexpr int kBar = kP + 2 * 2 * kRegion;
+  static constexpr int kBytes = 1024 + kBar + 256;             // alignment slack, barriers
+};
 
-  float o[HD / 8][4];
-#pragma unroll
-  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // rows g and g + 8 of this warp
-  const int row0 = q0 + warp * 16 + (lane >> 2), row1 = row0 + 8;
-  const int nkb = qb + 1;   // causal: key blocks 0..qb
-  uint32_t qa[HD / 16][4];
-  for (int kb = 0; kb < nkb; ++kb) {
-    const int buf = kb & 1;
-    if (kb + 1 < nkb) load_kv(kb + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    if (kb == 0) {
-#pragma unroll
-      for (int kk = 0; kk < HD / 16; ++kk)
-        ldsm_x4(qa[kk], qs + (warp * 16 + (lane & 15)) * S::kLd + kk * 16 + (lane >> 4) * 8);
+__device__ int g_attn_status;
+
+// Waits for the tensor-memory loads in flight; r is passed through so that no use of the
+// loaded registers is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const __grid_constant__ PrefillTcParams p) {
+  using L = TcLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 7;
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 11;
+  uint64_t* mma_done = bars + 13;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 14);
+
+  const int qb = static_cast<int>(gridDim.y) - 1 - static_cast<int>(blockIdx.y), h = blockIdx.x;
+  const int g = h / (p.nq / p.nkv);
+  const int q0 = qb * kTcBM;
+  const int nkb = qb + 1;                 // causal: key blocks 0..qb (kTcBN == kTcBM)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t kTileBytes = kTcBN * HD * 2;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
     }
-    // S = Q K^T for this warp's 16 rows x 64 keys
-    float s[kPN / 8][4];
-#pragma unroll
-    for (int j = 0; j < kPN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-    const __half* kt = ks + buf * S::kKV;
-#pragma unroll
-    for (int kk = 0; kk < HD / 16; ++kk) {
-#pragma unroll
-      for (int nt = 0; nt < kPN / 16; ++nt) {
-        uint32_t b[4];
-        ldsm_x4(b, kt + (nt * 16 + (lane >> 4) * 8 + (lane & 7)) * S::kLd + kk * 16 + ((lane >> 3) & 1) * 8);
-        mma16816(s[2 * nt], qa[kk], b[0], b[1]);
-        mma16816(s[2 * nt + 1], qa[kk], b[2], b[3]);
-      }
-    }
-    // mask (causal and past-the-end keys), online softmax in base 2
-    const int k0 = kb * kPN;
-    float mx0 = m0, mx1 = m1;
-#pragma unroll
-    for (int j = 0; j < kPN / 8; ++j) {
-      const int c = k0 + j * 8 + (lane & 3) * 2;
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const bool ok0 = c + e <= row0 && c + e < p.T;
-        const bool ok1 = c + e <= row1 && c + e < p.T;
-        s[j][e] = ok0 ? s[j][e] * p.scale_log2 : -INFINITY;
-        s[j][2 + e] = ok1 ? s[j][2 + e] * p.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[j][e]);
-        mx1 = fmaxf(mx1, s[j][2 + e]);
-      }
-    }
-#pragma unroll
-    for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o2));
-    }
-    const float a0 = mx0 == -INFINITY ? 1.f : exp2f(m0 - mx0);
-    const float a1 = mx1 == -INFINITY ? 1.f : exp2f(m1 - mx1);
-    m0 = mx0;
-    m1 = mx1;
-    float rs0 = 0.f, rs1 = 0.f;
-    uint32_t pa[kPN / 16][4];
-#pragma unroll
-    for (int j = 0; j < kPN / 8; ++j) {
-      const float p0 = mx0 == -INFINITY ? 0.f : exp2f(s[j][0] - mx0);
-      const float p1 = mx0 == -INFINITY ? 0.f : exp2f(s[j][1] - mx0);
-      const float p2 = mx1 == -INFINITY ? 0.f : exp2f(s[j][2] - mx1);
-      const float p3 = mx1 == -INFINITY ? 0.f : exp2f(s[j][3] - mx1);
-      rs0 += p0 + p1;
-      rs1 += p2 + p3;
-      pa[j / 2][(j & 1) * 2] = pack_h2(p0, p1);
-      pa[j / 2][(j & 1) * 2 + 1] = pack_h2(p2, p3);
-    }
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-#pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      o[j][0] *= a0;
-      o[j][1] *= a0;
-      o[j][2] *= a1;
-      o[j][3] *= a1;
-    }
-    // O += P V
-    const __half* vt = vs + buf * S::kKV;
-#pragma unroll
-    for (int kk = 0; kk < kPN / 16; ++kk) {
-#pragma unroll
-      for (int dt = 0; dt < HD / 16; ++dt) {
-        uint32_t b[4];
-        ldsm_x4_t(b, vt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * S::kLd + dt * 16 + (lane >> 4) * 8);
-        mma16816(o[2 * dt], pa[kk], b[0], b[1]);
-        mma16816(o[2 * dt + 1], pa[kk], b[2], b[3]);
-      }
-    }
-    __syncthreads();
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
   }
-  // row sums over the quad, normalise, store f32
-#pragma unroll
-  for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
+  __syncwarp();
+  if (warp == 0) {
+    umma::tmem_alloc(s_tmem, kTcTmemCols);
+    umma::tmem_relinquish();
   }
-  const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  float* dst0 = nullptr;
-  float* dst1 = nullptr;
-  if (!p.scatter) {
-    const int64_t ld = static_cast<int64_t>(p.nq) * HD;
-    dst0 = p.out + row0 * ld + static_cast<int64_t>(h) * HD;
-    dst1 = p.out + row1 * ld + static_cast<int64_t>(h) * HD;
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&p.tq);
+      prefetch_tmap(&p.tk);
+      prefetch_tmap(&p.tv);
+      mbar_arrive_expect_tx(q_full, kTcBM * HD * 2);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) tma_load_3d(sm + L::kQ + c * L::kRegion, &p.tq, 64 * c, q0, h, q_full);
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, p.status)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_3d(sm + L::kK + (s * (HD / 64) + c) * L::kRegion, &p.tk, 64 * c, j * kTcBN, g, &kv_full[s]);
+          tma_load_3d(sm + L::kV + (s * (HD / 64) + c) * L::kRegion, &p.tv, 64 * c, j * kTcBN, g, &kv_full[s]);
+        }
+        issued = j + 1;
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      mbar_wait(q_full, 0, nullptr, 500000000ull);
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j)
+        mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, 500000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t id_s = umma::idesc_f16_f32_kmaj_kmaj<kTcBM, kTcBN>();
+      constexpr uint32_t id_o = umma::idesc_f16_f32_kmaj_mnmaj<kTcBM, HD>();
+      const uint32_t q_base = smem_u32(sm + L::kQ);
+      auto issue_s = [&](int j) {   // S_j = Q K_j^T into S buffer j & 1
+        const uint32_t k_base = smem_u32(sm + L::kK + (j & 1) * (HD / 64) * L::kRegion);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kRegion + (kk & 3) * 32;
+          umma::mma_f16(tmem + (j & 1) * kTcBN, umma::smem_desc(q_base + off, 16, 1024, umma::kLayoutSW128),
+                        umma::smem_desc(k_base + off, 16, 1024, umma::kLayoutSW128), id_s, kk ? 1u : 0u);
+        }
+        umma::mma_commit(&s_full[j & 1]);
+      };
+      bool ok = mbar_wait(q_full, 0, p.status) && mbar_wait(&kv_full[0], 0, p.status);
+      if (ok) {
+        umma::fence_after_sync();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nkb; ++j) {
+        if (j + 1 < nkb) {
+          const int n = j + 1;
+          ok = mbar_wait(&kv_full[n & 1], (n >> 1) & 1, p.status);
+          if (ok && n >= 2) ok = mbar_wait(&s_free[n & 1], ((n >> 1) - 1) & 1, p.status);
+          if (!ok) break;
+          umma::fence_after_sync();
+          issue_s(n);
+        }
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status)) break;
+        umma::fence_after_sync();
+        const uint32_t p_base = smem_u32(sm + L::kP + (j & 1) * 2 * L::kRegion);
+        const uint32_t v_base = smem_u32(sm + L::kV + (j & 1) * (HD / 64) * L::kRegion);
+#pragma unroll
+        for (int kk = 0; kk < kTcBN / 16; ++kk) {
+          const uint64_t ad =
+              umma::smem_desc(p_base + (kk >> 2) * L::kRegion + (kk & 3) * 32, 16, 1024, umma::kLayoutSW128);
+          const uint64_t bd = umma::smem_desc(v_base + kk * 2048, L::kRegion, 1024, umma::kLayoutSW128);
+          umma::mma_f16(tmem + 2 * kTcBN, ad, bd, id_o, (j | kk) ? 1u : 0u);
+        }
+        umma::mma_commit(&pv_done[j & 1]);
+        umma::mma_commit(&kv_empty[j & 1]);
+      }
+      umma::mma_commit(mma_done);   // every MMA issued (also after an early stop) has completed
+    }
   } else {
-    // NVLink peer stores into the owning rank's output rows
-    const int64_t ld = static_cast<int64_t>(p.nq_total) * HD;
-    const int64_t hc = static_cast<int64_t>(p.head_off + h) * HD;
-    if (row0 < p.T) dst0 = p.out_peers[row0 / p.rows_per_rank] + (row0 % p.rows_per_rank) * ld + hc;
-    if (row1 < p.T) dst1 = p.out_peers[row1 / p.rows_per_rank] + (row1 % p.rows_per_rank) * ld + hc;
-  }
+    // ---------------- softmax (thread = query row = tensor-memory lane) ----------------
+    const int quarter = warp & 3;                      // warps 2, 3, 4, 5 -> lanes 64, 96, 0, 32
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      const int b = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, p.status));
+      if (!ok) break;
+      umma::fence_after_sync();
+      float x[kTcBN];
+      {
+        uint32_t r[kTcBN / 16][16];
 #pragma unroll
-  for (int j = 0; j < HD / 8; ++j) {
-    const int d = j * 8 + (lane & 3) * 2;
-    if (row0 < p.T) *reinterpret_cast<float2*>(dst0 + d) = make_float2(o[j][0] * i0, o[j][1] * i0);
-    if (row1 < p.T) *reinterpret_cast<float2*>(dst1 + d) = make_float2(o[j][2] * i1, o[j][3] * i1);
+        for (int c = 0; c < kTcBN / 16; ++c) umma::tmem_ld16(tmem + lane_addr + b * kTcBN + c * 16, r[c]);
+#pragma unroll
+        for (int c = 0; c < kTcBN / 16; ++c) {
+          tmem_wait_ld_regs(r[c]);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(r[c][e]);
+        }
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      // mask (causal on the diagonal block, keys past T), scale to base 2
+      const int k0 = j * kTcBN;
+      const int klim = min(p.T - 1, qrow);             // last valid key of this row
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTcBN; ++c) {
+        x[c] = k0 + c <= klim ? x[c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, x[c]);
+      }
+      const bool grow = mx > m_run + 8.f;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float alpha = !grow ? 1.f : (m_run == -INFINITY ? 0.f : dec_exp2(m_run - mx));
+        if (grow) {
+          l_run *= alpha;
+          m_run = mx;
+        }
+        if (j > 0) {
+          // O holds P_0..P_{j-1} V: wait for the last of those, rescale the row in place
+          ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status));
+          if (!ok) break;
+          umma::fence_after_sync();
+#pragma unroll
+          for (int c = 0; c < HD / 16; ++c) {
+            uint32_t r[16];
+            umma::tmem_ld16(tmem + lane_addr + 2 * kTcBN + c * 16, r);
+            tmem_wait_ld_regs(r);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            umma::tmem_st16(tmem + lane_addr + 2 * kTcBN + c * 16, r);
+          }
+          umma::tmem_wait_st();
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kTcBN; ++c) {
+        x[c] = m_run == -INFINITY ? 0.f : dec_exp2(x[c] - m_run);
+        rs += x[c];
+      }
+      l_run += rs;
+      // P buffer b was last read by O += P_{j-2} V_{j-2}
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, p.status));
+        if (!ok) break;
+      }
+      uint8_t* prow = sm + L::kP + b * 2 * L::kRegion + row * 128;
+#pragma unroll
+      for (int ch = 0; ch < kTcBN / 8; ++ch) {
+        uint4 v;
+        v.x = pack_h2(x[ch * 8 + 0], x[ch * 8 + 1]);
+        v.y = pack_h2(x[ch * 8 + 2], x[ch * 8 + 3]);
+        v.z = pack_h2(x[ch * 8 + 4], x[ch * 8 + 5]);
+        v.w = pack_h2(x[ch * 8 + 6], x[ch * 8 + 7]);
+        const int region = ch >> 3, c16 = ch & 7;
+        *reinterpret_cast<uint4*>(prow + region * L::kRegion + ((c16 ^ (row & 7)) << 4)) = v;
+      }
+      umma::fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, p.status));
+    if (ok) {
+      umma::fence_after_sync();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float* dst = nullptr;
+      if (qrow < p.T) {
+        if (!p.scatter) {
+          dst = p.out + static_cast<int64_t>(qrow) * p.nq * HD + static_cast<int64_t>(h) * HD;
+        } else {
+          // NVLink peer stores into the owning rank's output rows
+          dst = p.out_peers[qrow / p.rows_per_rank] +
+                static_cast<int64_t>(qrow % p.rows_per_rank) * p.nq_total * HD + static_cast<int64_t>(p.head_off + h) * HD;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < HD / 16; ++c) {
+        uint32_t r[16];
+        umma::tmem_ld16(tmem + lane_addr + 2 * kTcBN + c * 16, r);
+        tmem_wait_ld_regs(r);
+        if (dst != nullptr) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            *reinterpret_cast<float4*>(dst + c * 16 + 4 * e) =
+                make_float4(__uint_as_float(r[4 * e]) * inv, __uint_as_float(r[4 * e + 1]) * inv,
+                            __uint_as_float(r[4 * e + 2]) * inv, __uint_as_float(r[4 * e + 3]) * inv);
+        }
+      }
+    }
+    umma::fence_before_sync();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    mbar_wait(mma_done, 0, nullptr, 500000000ull);   // no MMA still uses tensor memory
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, kTcTmemCols);
   }
 }
 
@@ -1008,23 +1126,63 @@ extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float
 
 namespace pyre {
 namespace attn {
-int launch_prefill(PrefillParams p, int hd, cudaStream_t s) {
-  dim3 grid(p.nq, (p.T + kPM - 1) / kPM);
-  int rc;
-  if (hd == 64) {
-    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<64>), PrefillSmem<64>::kBytes);
-    if (rc) return rc;
-    attn_prefill_kernel<64><<<grid, 128, PrefillSmem<64>::kBytes, s>>>(p);
-  } else {
-    rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_kernel<128>), PrefillSmem<128>::kBytes);
-    if (rc) return rc;
-    attn_prefill_kernel<128><<<grid, 128, PrefillSmem<128>::kBytes, s>>>(p);
-  }
-  PYRE_LAUNCH_CHECK("attn_prefill_kernel");
+template <int HD>
+int launch_prefill_tc(const PrefillParams& pp, cudaStream_t s) {
+  using L = TcLayout<HD>;
+  static int* status_of[64] = {};
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  int*& status = status_of[dev & 63];
+  if (status == nullptr) PYRE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_attn_status));
+  PrefillTcParams p{};
+  const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc = make_tmap_3d(&p.tq, pp.q, f16, 2, HD, static_cast<uint64_t>(pp.T), static_cast<uint64_t>(pp.nq), HD * 2,
+                        static_cast<uint64_t>(pp.T) * HD * 2, 64, kTcBM, sw);
+  if (!rc)
+    rc = make_tmap_3d(&p.tk, pp.kc, f16, 2, HD, static_cast<uint64_t>(pp.T), static_cast<uint64_t>(pp.nkv), HD * 2,
+                      static_cast<uint64_t>(pp.max_t) * HD * 2, 64, kTcBN, sw);
+  if (!rc)
+    rc = make_tmap_3d(&p.tv, pp.vc, f16, 2, HD, static_cast<uint64_t>(pp.T), static_cast<uint64_t>(pp.nkv), HD * 2,
+                      static_cast<uint64_t>(pp.max_t) * HD * 2, 64, kTcBN, sw);
+  if (rc) return rc;
+  p.out = pp.out;
+  p.T = pp.T;
+  p.nq = pp.nq;
+  p.nkv = pp.nkv;
+  p.scale_log2 = pp.scale_log2;
+  p.scatter = pp.scatter;
+  p.rows_per_rank = pp.rows_per_rank;
+  p.head_off = pp.head_off;
+  p.nq_total = pp.nq_total;
+  for (int i = 0; i < 16; ++i) p.out_peers[i] = pp.out_peers[i];
+  p.status = status;
+  rc = set_smem_limit(reinterpret_cast<const void*>(attn_prefill_tc_kernel<HD>), L::kBytes);
+  if (rc) return rc;
+  const dim3 grid(static_cast<unsigned>(pp.nq), static_cast<unsigned>((pp.T + kTcBM - 1) / kTcBM));
+  attn_prefill_tc_kernel<HD><<<grid, kTcThreads, L::kBytes, s>>>(p);
+  PYRE_LAUNCH_CHECK("attn_prefill_tc_kernel");
   return PYRE_OK;
 }
+
+int launch_prefill(PrefillParams p, int hd, cudaStream_t s) {
+  return hd == 64 ? launch_prefill_tc<64>(p, s) : launch_prefill_tc<128>(p, s);
+}
+
 }  // namespace attn
 }  // namespace pyre
+
+extern "C" int pyre_attn_status(int* status) {
+  PYRE_CHECK_ARG(status != nullptr, "pyre_attn_status: null pointer");
+  int v = 0;
+  PYRE_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attn_status, sizeof(int)));
+  if (v != PYRE_OK) {
+    const int zero = 0;
+    PYRE_CUDA_TRY(cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int)));
+  }
+  *status = v;
+  return PYRE_OK;
+}
 
 extern "C" int pyre_attn_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int T, int nq,
                                  int nkv, int hd, int max_t, float* out, void* stream) {

@@ -63,3 +63,14 @@ extern "C" int pyre_last_error(char* buf, int len) {
   }
   return static_cast<int>(s.size());
 }
+
+extern "C" int pyre_graph_run(void* exec, void* stream, const void* src, void* stage_in, int64_t in_bytes) {
+  PYRE_CHECK_ARG(exec != nullptr, "pyre_graph_run: null graph");
+  PYRE_CHECK_ARG(in_bytes >= 0 && (in_bytes == 0 || (src != nullptr && stage_in != nullptr)),
+                 "pyre_graph_run: bad input copy");
+  if (in_bytes > 0) std::memcpy(stage_in, src, static_cast<size_t>(in_bytes));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PYRE_CUDA_TRY(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), s));
+  PYRE_CUDA_TRY(cudaStreamSynchronize(s));
+  return PYRE_OK;
+}

@@ -14,6 +14,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                  uint64_t rows, uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows,
                  uint32_t box_cols, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
+// Encodes a 3-D tiled tensor map over [d2][d1][d0] (d0 innermost, contiguous) with the
+// given byte strides of d1 and d2; box box0 x box1 x 1. Reads past an extent return zeros.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                 uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                 uint32_t box1, CUtensorMapSwizzle swizzle);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -71,6 +77,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           smem_u32(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3-D tiled TMA load (coordinates innermost first; c0 * elem_bytes a multiple of 16).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -38,6 +38,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// The store counterpart: thread t of the warp writes lane (base + t), 16 consecutive columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Generic-proxy writes to shared memory made visible to the tensor core (async proxy).
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -69,6 +80,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32_kmaj_mnmaj() {
          | (1u << 16)                                // B MN-major
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, M x N.
+template <int M, int N>
+__host__ __device__ constexpr uint32_t idesc_f16_f32_kmaj_kmaj() {
+  static_assert(M == 128 && N % 16 == 0 && N >= 16 && N <= 256, "M = 128, N in [16, 256] step 16");
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]; accumulate == 0 overwrites D. Issued by one thread.

@@ -5,13 +5,15 @@ The reference compiles one FFN graph per (shard, seq_len) at start-up and then c
 :574-580; src/orchestrator/worker_node.py:122-130, :319-329). The B200 equivalent of that
 compile step is a CUDA graph: :class:`CapturedFfn` captures the host->device copy of the
 activations, the two FFN kernels (and, with a communicator, the in-kernel NVLink
-reduction) and the device->host copy of the partial sum, so one ``execute`` is one graph
-launch plus a stream synchronisation, with no per-kernel launch cost on the CPU.
+reduction) and the device->host copy of the partial sum, so one ``execute`` is one native
+call (``pyre_graph_run``: host copy into the pinned input, graph launch, stream wait), with
+no per-kernel launch cost on the CPU.
 """
 from __future__ import annotations
 
 import torch
 
+from .. import _native as N
 from .op import FfnShardOp, FfnWeights
 
 
@@ -37,6 +39,16 @@ class CapturedFfn:
             self.x_dev.copy_(self.x_host, non_blocking=True)
             op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
             self.out_host.copy_(self.out_dev, non_blocking=True)
+        # the instantiated graph, launched by the library's native runner
+        lib = N.load()
+        self._exec = self.graph.raw_cuda_graph_exec()
+        self._stream_ptr = self.stream.cuda_stream
+        self._x_ptr = self.x_host.data_ptr()
+        fn = lib.pyre_graph_run
+
+        def run(*args):
+            N.check(fn(*args))
+        self._run = run
 
     @property
     def h2d_bytes(self) -> int:
@@ -50,8 +62,13 @@ class CapturedFfn:
         """Runs one call on host activations ``x [tokens, hidden]``; returns the host f32
         partial (the op's cross-rank sum when it has a communicator). The returned tensor
         is the runner's pinned output buffer, overwritten by the next call."""
-        self.x_host.copy_(torch.as_tensor(x).reshape(self.x_host.shape))
-        with torch.cuda.stream(self.stream):
-            self.graph.replay()
-        self.stream.synchronize()
+        if (isinstance(x, torch.Tensor) and x.dtype == self.x_host.dtype and not x.is_cuda and x.is_contiguous()
+                and x.numel() == self.x_host.numel()):
+            # same-dtype host tensor: the native runner copies it into the pinned buffer
+            src, nbytes = x.data_ptr(), self.h2d_bytes
+        else:
+            self.x_host.copy_(torch.as_tensor(x).reshape(self.x_host.shape))
+            src, nbytes = None, 0
+        # one native call: host copy into the pinned input, graph launch, wait
+        self._run(self._exec, self._stream_ptr, src, self._x_ptr, nbytes)
         return self.out_host

@@ -69,7 +69,9 @@ def _as4(x, T, n, hd):
 
 
 @pytest.mark.parametrize("T,nq,nkv,hd,frac,theta", [(70, 8, 2, 64, 1.0, 1e4), (130, 4, 4, 128, 1.0, 1e6),
-                                                     (200, 32, 8, 128, 1.0, 5e5), (65, 6, 2, 64, 0.5, 1e4)])
+                                                     (200, 32, 8, 128, 1.0, 5e5), (65, 6, 2, 64, 0.5, 1e4),
+                                                     (1000, 8, 2, 128, 1.0, 1e6), (2048, 4, 1, 64, 1.0, 5e5),
+                                                     (1, 4, 2, 128, 1.0, 1e4), (129, 2, 2, 128, 1.0, 1e4)])
 def test_prefill_attention_vs_oracle(T, nq, nkv, hd, frac, theta):
     from pyre_b200.attention import AttentionOp
     rng = np.random.default_rng(T + nq)
@@ -81,6 +83,10 @@ def test_prefill_attention_vs_oracle(T, nq, nkv, hd, frac, theta):
     # the cache holds the rotated, clipped keys (f16)
     kr = np.clip(OK.apply_rope(_as4(k, T, nkv, hd).transpose(0, 2, 1, 3), theta, 0, frac), -1000, 1000)[0]
     assert rel(op.cache.k[:, :T].float().cpu().numpy(), kr) < 2e-3
+    from pyre_b200 import _native as N
+    st = ctypes.c_int(-1)
+    N.call("pyre_attn_status", ctypes.byref(st))
+    assert st.value == 0      # no bounded pipeline wait of the tensor-core kernel ran out
 
 
 def test_prefill_golden_cases():

@@ -262,3 +262,28 @@ def test_prefill_split_k_deterministic():
     assert int(hdr[2]) == 0
     assert int(hdr[256:256 + 2048].abs().sum()) == 0
     assert rel_err(outs[0].cpu().numpy(), offn.ffn_shard_f64(x, gd, ud, dd)) < TOL_BF16
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_captured_ffn_host_in_host_out(T):
+    """CapturedFfn.execute (host input -> native graph run -> pinned host output) equals the
+    op on device tensors, for a same-dtype host tensor (copied by the native runner) and for a
+    numpy f32 array (converted on the host), call after call."""
+    from pyre_b200.ffn import FfnShardOp, FfnWeights
+    from pyre_b200.ffn.captured import CapturedFfn
+    H, W = 576, 768
+    rng = np.random.default_rng(T + 5)
+    g, _ = make_weight((H, W), rng, torch.float16)
+    u, _ = make_weight((H, W), rng, torch.float16)
+    d, _ = make_weight((W, H), rng, torch.float16)
+    op = FfnShardOp(H, W, max_tokens=4)
+    fw = FfnWeights.prepare(g, u, d)
+    run = CapturedFfn(op, fw, tokens=T)
+    for i in range(3):
+        x = torch.from_numpy(bf16_round(rng.standard_normal((T, H)))).to(torch.bfloat16)
+        want = op.run(x.cuda(), fw).cpu()
+        got = run.execute(x).clone()
+        assert torch.equal(got, want), i
+        got2 = run.execute(x.float().numpy()).clone()
+        assert torch.equal(got2, want), i
+    assert op.status() == 0
