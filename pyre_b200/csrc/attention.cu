@@ -92,26 +92,96 @@ __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restri
 }
 
 // ---------------------------------------------------------------------------------------
-// One CTA per token: the cos/sin of the token's position for the rotated half-dims come
-// from the table of pyre_rope_table (f64 on the host, as the reference computes them), then
-// every q and k head of the token is rotated in f32 (pair (i, i+half)),
-// clipped to +-1000 and stored as f16; v is clipped and appended.
+// RoPE + clip + append. The cos/sin of a token's position for the rotated half-dims come
+// from the table of pyre_rope_table (f64 on the host, as the reference computes them); every
+// q and k head of the token is rotated in f32 (pair (i, i+half)), clipped to +-1000 and
+// stored as f16; v is clipped and appended. rope_append_vec_kernel handles hd 64 / 128 with
+// half a multiple of 4 (16-byte loads); rope_append_kernel (one CTA per token and group of
+// heads, scalar) everything else.
 constexpr int kRopeMaxHalf = 256;
 constexpr int kRopeHeadsPerCta = 8;
 
+// The rotate-half pair (x1, x2) = (src[j], src[j + half]) -> (x1 c - x2 s, x1 s + x2 c), each
+// product and sum rounded separately in f32 like the reference's numpy arithmetic (no FMA),
+// so that every kernel that rotates stores the same bits.
+__device__ __forceinline__ float rope_lo(float x1, float x2, float c, float s) {
+  return __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+}
+__device__ __forceinline__ float rope_hi(float x1, float x2, float c, float s) {
+  return __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+}
+__device__ __forceinline__ float clip1000(float r) { return fminf(fmaxf(r, -1000.f), 1000.f); }
+
 // Element i of a rotated, clipped head (rotate-half pairs (i, i + half), cos/sin from the
-// table row of the position, dims >= 2 * half pass through), as rope_append_kernel and the
-// fused decode step both store it.
+// table row of the position, dims >= 2 * half pass through), as the fused decode step and
+// the scalar append kernel store it.
 __device__ __forceinline__ float rope_clip(const float* __restrict__ src, int i, int half, float c, float s) {
   float r;
   if (i < 2 * half) {
     const int jj = i < half ? i : i - half;
     const float x1 = __ldg(src + jj), x2 = __ldg(src + jj + half);
-    r = i < half ? x1 * c - x2 * s : x1 * s + x2 * c;
+    r = i < half ? rope_lo(x1, x2, c, s) : rope_hi(x1, x2, c, s);
   } else {
     r = __ldg(src + i);
   }
-  return fminf(fmaxf(r, -1000.f), 1000.f);
+  return clip1000(r);
+}
+
+__device__ __forceinline__ uint32_t pack_h2_rn(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Vectorised RoPE + clip + append for hd in {64, 128} with half a multiple of 4: one CTA per
+// token, one thread per 4 consecutive dims of a q, k or v row (float4 loads of the dims and
+// of their rotation partners, 8-byte f16 stores), all heads of the token.
+template <int HD>
+__global__ void __launch_bounds__(256) rope_append_vec_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                               const float* __restrict__ v, int64_t q_stride,
+                                                               int64_t kv_stride, int T, int nq, int nkv,
+                                                               int start_pos, const float2* __restrict__ table,
+                                                               int half, __half* __restrict__ q_out,
+                                                               __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+                                                               int max_t) {
+  constexpr int U = HD / 4;
+  const int t = blockIdx.x;
+  const int pos = start_pos + t;
+  const float2* row_cs = table + static_cast<int64_t>(pos) * half;
+  const int units = (nq + 2 * nkv) * U;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int r = u / U, c4 = (u - r * U) * 4;
+    const float* src;
+    __half* dst;
+    bool rot = true;
+    if (r < nq) {
+      src = q + t * q_stride + static_cast<int64_t>(r) * HD;
+      dst = q_out + (static_cast<int64_t>(r) * T + t) * HD;
+    } else if (r < nq + nkv) {
+      src = k + t * kv_stride + static_cast<int64_t>(r - nq) * HD;
+      dst = k_cache + (static_cast<int64_t>(r - nq) * max_t + pos) * HD;
+    } else {
+      src = v + t * kv_stride + static_cast<int64_t>(r - nq - nkv) * HD;
+      dst = v_cache + (static_cast<int64_t>(r - nq - nkv) * max_t + pos) * HD;
+      rot = false;
+    }
+    const float4 x = __ldg(reinterpret_cast<const float4*>(src + c4));
+    float o[4] = {x.x, x.y, x.z, x.w};
+    if (rot && c4 < 2 * half) {
+      const bool lo = c4 < half;
+      const int j = lo ? c4 : c4 - half;
+      const float4 pr = __ldg(reinterpret_cast<const float4*>(src + (lo ? c4 + half : c4 - half)));
+      const float4 cs01 = __ldg(reinterpret_cast<const float4*>(row_cs + j));
+      const float4 cs23 = __ldg(reinterpret_cast<const float4*>(row_cs + j + 2));
+      const float p[4] = {pr.x, pr.y, pr.z, pr.w};
+      const float c[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, sn[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = lo ? rope_lo(o[e], p[e], c[e], sn[e]) : rope_hi(p[e], o[e], c[e], sn[e]);
+    }
+    uint2 h;
+    h.x = pack_h2_rn(clip1000(o[0]), clip1000(o[1]));
+    h.y = pack_h2_rn(clip1000(o[2]), clip1000(o[3]));
+    *reinterpret_cast<uint2*>(dst + c4) = h;
+  }
 }
 
 
@@ -937,6 +1007,26 @@ extern "C" int pyre_rope_kv_append(const float* q, const float* k, const float* 
   const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
   PYRE_CHECK_ARG(dims <= hd && dims / 2 <= kRopeMaxHalf, "pyre_rope_kv_append: rope_fraction must be in [0, 1]");
   PYRE_CHECK_ARG(rope_table != nullptr || dims < 2, "pyre_rope_kv_append: null RoPE table");
+  const int half = dims >= 2 ? dims / 2 : 0;
+  const bool vec = (hd == 64 || hd == 128) && half % 4 == 0 && q_stride % 4 == 0 && kv_stride % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(v) % 16 == 0 && reinterpret_cast<uintptr_t>(q_out) % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(k_cache) % 8 == 0 && reinterpret_cast<uintptr_t>(v_cache) % 8 == 0 &&
+                   (half == 0 || reinterpret_cast<uintptr_t>(rope_table) % 16 == 0);
+  if (vec) {
+    const float2* tab = reinterpret_cast<const float2*>(rope_table);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (hd == 64)
+      rope_append_vec_kernel<64><<<T, 256, 0, st>>>(q, k, v, q_stride, kv_stride, T, nq, nkv, start_pos, tab, half,
+                                                    reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_cache),
+                                                    reinterpret_cast<__half*>(v_cache), max_t);
+    else
+      rope_append_vec_kernel<128><<<T, 256, 0, st>>>(q, k, v, q_stride, kv_stride, T, nq, nkv, start_pos, tab, half,
+                                                     reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_cache),
+                                                     reinterpret_cast<__half*>(v_cache), max_t);
+    PYRE_LAUNCH_CHECK("rope_append_vec_kernel");
+    return PYRE_OK;
+  }
   dim3 grid(T, (nq + nkv + kRopeHeadsPerCta - 1) / kRopeHeadsPerCta);
   rope_append_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       q, k, v, q_stride, kv_stride, T, nq, nkv, hd, start_pos, reinterpret_cast<const float2*>(rope_table),
@@ -1271,11 +1361,11 @@ __global__ void __launch_bounds__(256) ulysses_rope_scatter_kernel(
     if (i < 2 * half) {
       const int jj = i < half ? i : i - half;
       const float x1 = src[jj], x2 = src[jj + half];
-      r = i < half ? x1 * cs[jj] - x2 * sn[jj] : x1 * sn[jj] + x2 * cs[jj];
+      r = i < half ? rope_lo(x1, x2, cs[jj], sn[jj]) : rope_hi(x1, x2, cs[jj], sn[jj]);
     } else {
       r = src[i];
     }
-    const __half hv = __float2half_rn(fminf(fmaxf(r, -1000.f), 1000.f));
+    const __half hv = __float2half_rn(clip1000(r));
     const int owner = is_q ? h / qpr : h / kpr;
     const int hl = is_q ? h - owner * qpr : h - owner * kpr;
     __half* dst = reinterpret_cast<__half*>(peers.buf[owner] + (is_q ? off_q : off_k));
