@@ -90,6 +90,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Spins until *flag == want or timeout_ns elapses. Returns true on success.
 __device__ __forceinline__ bool wait_flag_eq(const uint32_t* flag, uint32_t want,
                                              uint64_t timeout_ns) {

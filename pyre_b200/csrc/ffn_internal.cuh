@@ -93,7 +93,7 @@ int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nma
                 unsigned int* counters, int* status, cudaStream_t s);
 int64_t ffn_gemm_partial_bytes(int T, int N, int nmat);
 // Workspace regions of the T > 4 path after the header: f16 staging of the activations,
-// then split-K partial tiles.
+// then the stream-K partial tiles of the GEMM (one per CTA).
 inline int64_t ffn_gemm_staging_bytes(int T, int H, int W) {
   return (static_cast<int64_t>(T) * (H > W ? H : W) * 2 + 255) / 256 * 256;
 }

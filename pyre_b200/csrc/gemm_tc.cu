@@ -14,7 +14,9 @@
 //                     one packed subtract, one packed multiply by the f16 scale);
 //   MMA warp (1 thr): tcgen05.mma M=128 N=256 K=16, R/16 per matrix, accumulators in tensor
 //                     memory (256 columns per matrix); tcgen05.commit frees the stage.
-// The dequant warps then read the accumulators (tcgen05.ld) and run the epilogue. Bulk
+// The dequant warps then read the accumulators (tcgen05.ld) and run the epilogue. The
+// k-steps of all tiles are split evenly over one CTA per SM (stream-K, below), so no wave
+// of tiles leaves SMs idle. Bulk
 // copies and TMA loads only; no cluster multicast. Every mbarrier wait is bounded.
 //
 // Operands are f16: the weights as f16(q * scale) (q exact in f16, one rounding of the product,
@@ -32,7 +34,8 @@ namespace tc {
 using namespace gemv;
 
 constexpr int kBM = 128;
-constexpr int kMaxSplits = 4;
+constexpr int kMaxCtas = 160;     // stream-K CTAs at most (>= the SM count of a B200)
+constexpr int kMinSteps = 8;      // k-steps per CTA at least
 constexpr int kBN = 256;
 constexpr int kStages = 3;
 constexpr int kDequantWarps = 8;
@@ -68,10 +71,9 @@ struct Params {
   void* out;                // [T, N]
   int out_bf16, out_f16;
   int* status;
-  int splits;               // split-K factor (1: no split)
   int64_t partial_cap;      // bytes available at partial
-  float* partial;           // [tiles, splits, NMAT, 128 x 256] f32 partial tiles (splits > 1)
-  unsigned int* counters;   // [tiles] splits finished, zero between calls
+  float* partial;           // [CTAs][NMAT, 128 x 256] f32: stream-K partial tile of each CTA
+  unsigned int* counters;   // [CTAs] partial-ready flags, zero between calls
 };
 
 // Stores 16 consecutive outputs of row t starting at column col0 (bounds-checked on N).
@@ -133,6 +135,24 @@ __device__ __forceinline__ uint32_t b_offset(int n, int k) {
   return static_cast<uint32_t>((n >> 6) * 1024 + (k >> 3) * 4096 + (k & 7) * 128 + ((((n & 63) >> 3) ^ (k & 7)) << 4));
 }
 
+// Stream-K schedule: the tiles' k-steps, tile after tile (tile = slab * mtiles + m-tile, so
+// consecutive CTAs share weight slabs), are cut into G equal ranges, one per CTA. A CTA's
+// range covers segments of one or more tiles:
+//   * a whole tile: accumulate, epilogue;
+//   * the start of a tile that continues in the next CTAs (always the CTA's last segment):
+//     this CTA finishes the tile: it waits (bounded) for the partials of those CTAs, adds
+//     them in k order to its own accumulator and runs the epilogue;
+//   * a tile's continuation (always the CTA's first segment): the partial goes to this CTA's
+//     slot in the workspace and a flag releases it.
+// Waits only go to higher CTA indices and all G <= SM-count CTAs are resident, so the
+// schedule has no cycles. Results are deterministic: the same ranges, the same order.
+struct Seg {
+  int tile, k0, k1;   // k-steps [k0, k1) of tile
+};
+__device__ __forceinline__ int sk_owner(int64_t u, int64_t total, int G) {   // CTA whose range holds u
+  return static_cast<int>(((u + 1) * G - 1) / total);
+}
+
 template <int NMAT, int EPI, typename ST>
 __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_constant__ Params p) {
   using C = Cfg<NMAT, ST>;
@@ -144,20 +164,24 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_c
   uint64_t* bfull = full + kStages;
   uint64_t* empty = bfull + kStages;
   uint64_t* accfull = empty + kStages;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accfull + 1);
-  int* s_last = reinterpret_cast<int*>(s_tmem + 1);
+  uint64_t* tmem_free = accfull + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(tmem_free + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // CTA order: split (fastest), then token tile, then slab, so the CTAs sharing a weight slab
-  // run together and its blocks are read from HBM about once
-  const int ks = blockIdx.x % p.splits;
-  const int tile = blockIdx.x / p.splits;
-  const int slab = tile / p.mtiles;
-  const int mt = tile - slab * p.mtiles;
-  const int m0 = mt * kBM;
-  const int kbeg = static_cast<int>(static_cast<int64_t>(ks) * p.upt / p.splits);
-  const int nj = static_cast<int>(static_cast<int64_t>(ks + 1) * p.upt / p.splits) - kbeg;   // k-steps here
+  const int G = gridDim.x, c = blockIdx.x;
+  const int64_t total = static_cast<int64_t>(p.tiles) * p.mtiles * p.upt;
+  const int64_t ub = total * c / G, ue = total * (c + 1) / G;   // this CTA's k-steps
+  const int t_first = static_cast<int>(ub / p.upt);
+  const int nseg = ue > ub ? static_cast<int>((ue - 1) / p.upt) - t_first + 1 : 0;
+  auto seg_of = [&](int i) {
+    Seg sg;
+    sg.tile = t_first + i;
+    const int64_t base = static_cast<int64_t>(sg.tile) * p.upt;
+    sg.k0 = static_cast<int>((ub > base ? ub : base) - base);
+    sg.k1 = static_cast<int>((ue < base + p.upt ? ue : base + p.upt) - base);
+    return sg;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -166,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_c
       mbar_init(&empty[i], 1);
     }
     mbar_init(accfull, 1);
+    mbar_init(tmem_free, kDequant / 32);
     fence_mbar_init();
   }
   __syncwarp();
@@ -182,155 +207,178 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_c
     // ---------------- producer ----------------
     if (lane == 0) {
       prefetch_tmap(&p.ta);
-      const uint8_t* wslab = p.w + static_cast<int64_t>(slab) * p.upt * C::kWBytes;
-      int issued = 0;
-      for (int j = 0; j < nj; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) break;
-        uint8_t* st = smem + s * C::kStageBytes;
-        const int kt = kbeg + j;
-        mbar_arrive_expect_tx(&full[s], C::kABytes + C::kWBytes);
-        tma_load_2d(st + C::kAOff, &p.ta, kt * C::R, m0, &full[s]);
-        bulk_load(st + C::kWOff, wslab + static_cast<int64_t>(kt) * C::kWBytes, C::kWBytes, &full[s]);
-        issued = j + 1;
+      int64_t j = 0, issued = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < nseg; ++i) {
+        const Seg sg = seg_of(i);
+        const int slab = sg.tile / p.mtiles, m0 = (sg.tile - slab * p.mtiles) * kBM;
+        const uint8_t* wslab = p.w + static_cast<int64_t>(slab) * p.upt * C::kWBytes;
+        for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
+          const int s = static_cast<int>(j % kStages);
+          const uint32_t ph = static_cast<uint32_t>(j / kStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], C::kABytes + C::kWBytes);
+          tma_load_2d(st + C::kAOff, &p.ta, kt * C::R, m0, &full[s]);
+          bulk_load(st + C::kWOff, wslab + static_cast<int64_t>(kt) * C::kWBytes, C::kWBytes, &full[s]);
+          issued = j + 1;
+        }
       }
       // no copy may still be landing in shared memory when the CTA exits
-      for (int j = issued - kStages < 0 ? 0 : issued - kStages; j < issued; ++j)
-        mbar_wait(&full[j % kStages], (j / kStages) & 1u, nullptr, 500000000ull);
+      for (int64_t q = issued - kStages < 0 ? 0 : issued - kStages; q < issued; ++q)
+        mbar_wait(&full[q % kStages], static_cast<uint32_t>(q / kStages) & 1u, nullptr, 500000000ull);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma::idesc_f16_f32_kmaj_mnmaj<kBM, kBN>();
-      for (int j = 0; j < nj; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1u;
-        if (!mbar_wait(&bfull[s], ph, p.status)) break;
+      int64_t j = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < nseg; ++i) {
+        const Seg sg = seg_of(i);
+        // the accumulator is overwritten: the previous segment's epilogue must have read it
+        if (i > 0 && !mbar_wait(tmem_free, static_cast<uint32_t>(i - 1) & 1u, p.status)) break;
         umma::fence_after_sync();
-        const uint32_t a_base = smem_u32(smem + s * C::kStageBytes + C::kAOff);
-        const uint32_t b_base = smem_u32(smem + s * C::kStageBytes + C::kBOff);
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-#pragma unroll
-          for (int kk = 0; kk < C::R / 16; ++kk) {
-            const uint64_t ad = umma::smem_desc(a_base + kk * 32, 16, C::kSboA, C::kSwizzleA);
-            const uint64_t bd = umma::smem_desc(b_base + m * C::kBMatBytes + kk * 2 * 4096, 1024, 4096,
-                                                umma::kLayoutSW128);
-            umma::mma_f16(tmem + m * kBN, ad, bd, idesc, (j | kk) != 0 ? 1u : 0u);
+        for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
+          const int s = static_cast<int>(j % kStages);
+          const uint32_t ph = static_cast<uint32_t>(j / kStages) & 1u;
+          if (!mbar_wait(&bfull[s], ph, p.status)) {
+            ok = false;
+            break;
           }
+          umma::fence_after_sync();
+          const uint32_t a_base = smem_u32(smem + s * C::kStageBytes + C::kAOff);
+          const uint32_t b_base = smem_u32(smem + s * C::kStageBytes + C::kBOff);
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+#pragma unroll
+            for (int kk = 0; kk < C::R / 16; ++kk) {
+              const uint64_t ad = umma::smem_desc(a_base + kk * 32, 16, C::kSboA, C::kSwizzleA);
+              const uint64_t bd = umma::smem_desc(b_base + m * C::kBMatBytes + kk * 2 * 4096, 1024, 4096,
+                                                  umma::kLayoutSW128);
+              umma::mma_f16(tmem + m * kBN, ad, bd, idesc, (kt != sg.k0 || kk != 0) ? 1u : 0u);
+            }
+          }
+          umma::mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
         }
-        umma::mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+        umma::mma_commit(accfull);       // this segment's MMAs (also after an early stop) are done
       }
-      umma::mma_commit(accfull);       // all MMAs (also after an early stop) have completed
     }
   } else {
-    // ---------------- dequant, then epilogue ----------------
+    // ---------------- dequant, then the epilogue of each segment ----------------
     const int dt = threadIdx.x - 64;
-    for (int j = 0; j < nj; ++j) {
-      const int s = j % kStages;
-      const uint32_t ph = (j / kStages) & 1u;
-      if (!mbar_wait(&full[s], ph, p.status)) break;
-      uint8_t* st = smem + s * C::kStageBytes;
-      const uint8_t* wq = st + C::kWOff;
-      const ST* ws = reinterpret_cast<const ST*>(st + C::kWOff + NMAT * C::R * kTileN);
-      uint8_t* bt = st + C::kBOff;
-      constexpr int kGroups = NMAT * C::R * 32;   // 8-column groups per stage
-#pragma unroll 2
-      for (int g = dt; g < kGroups; g += kDequant) {
-        const int m = g / (C::R * 32);
-        const int rem = g - m * (C::R * 32);
-        const int k = rem >> 5;
-        const int n8 = rem & 31;
-        const uint2 q = *reinterpret_cast<const uint2*>(wq + m * C::R * kTileN + k * kTileN + n8 * 8);
-        const __half2 sc = __half2half2(to_f16(ws[m * C::R * 8 + k * 8 + (n8 >> 2)]));
-        // byte b (offset by 128) -> f16 1024 + b -> minus 1152 = the int8 value, exactly
-        const uint32_t w0 = q.x ^ 0x80808080u, w1 = q.y ^ 0x80808080u;
-        const __half2 k1152 = __half2half2(__ushort_as_half(0x6480u));
-        uint4 o;
-        o.x = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w0, 0x64646464u, 0x4140u)), k1152), sc));
-        o.y = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w0, 0x64646464u, 0x4342u)), k1152), sc));
-        o.z = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w1, 0x64646464u, 0x4140u)), k1152), sc));
-        o.w = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w1, 0x64646464u, 0x4342u)), k1152), sc));
-        *reinterpret_cast<uint4*>(bt + m * C::kBMatBytes + b_offset(n8 * 8, k)) = o;
-      }
-      umma::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bfull[s]);
-    }
-    // epilogue: this warp reads TMEM lanes 32*(warp % 4) .. +31 = tile rows
-    mbar_wait(accfull, 0, p.status);
-    umma::fence_after_sync();
     // warps 2..9: TMEM lane quarter = warp % 4, column half = (warp - 2) / 4
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int t = m0 + row;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     constexpr int kColsPerWarp = kBN * 4 / kDequantWarps;
     const int cbeg = ((warp - 2) / 4) * kColsPerWarp;
-    // split-K: every split stores its partial tile (thread-major, coalesced); the split that
-    // counts last adds them in split order (deterministic) and runs the epilogue
     constexpr int kPartFloats = NMAT * kBN * kBM;
-    float* part = p.partial + static_cast<int64_t>(tile) * p.splits * kPartFloats;
-    auto part_at = [&](int split, int m, int c0) {
-      return part + static_cast<int64_t>(split) * kPartFloats + ((m * (kBN / 16) + c0 / 16) * kBM + row) * 16;
+    auto part_at = [&](int cta, int m, int c0) {   // coalesced: 16 floats per (thread row, column group)
+      return p.partial + static_cast<int64_t>(cta) * kPartFloats + ((m * (kBN / 16) + c0 / 16) * kBM + row) * 16;
     };
-    if (p.splits > 1) {
-      for (int c0 = cbeg; c0 < cbeg + kColsPerWarp; c0 += 16) {
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          uint32_t a[16];
-          umma::tmem_ld16(trow + m * kBN + c0, a);
-          umma::tmem_wait_ld();
-          float4* dst = reinterpret_cast<float4*>(part_at(ks, m, c0));
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            __stcg(dst + i, make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
-                                        __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3])));
+    int64_t j = 0;
+    bool ok = true;
+    for (int i = 0; ok && i < nseg; ++i) {
+      const Seg sg = seg_of(i);
+      for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
+        const int s = static_cast<int>(j % kStages);
+        const uint32_t ph = static_cast<uint32_t>(j / kStages) & 1u;
+        if (!mbar_wait(&full[s], ph, p.status)) {
+          ok = false;
+          break;
         }
-      }
-      named_bar(1, kDequant);
-      if (dt == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(p.counters + tile, 1u);
-        const int last = prev == static_cast<unsigned>(p.splits - 1);
-        if (last) {
-          __threadfence();
-          p.counters[tile] = 0u;
+        uint8_t* st = smem + s * C::kStageBytes;
+        const uint8_t* wq = st + C::kWOff;
+        const ST* ws = reinterpret_cast<const ST*>(st + C::kWOff + NMAT * C::R * kTileN);
+        uint8_t* bt = st + C::kBOff;
+        constexpr int kGroups = NMAT * C::R * 32;   // 8-column groups per stage
+#pragma unroll 2
+        for (int g = dt; g < kGroups; g += kDequant) {
+          const int m = g / (C::R * 32);
+          const int rem = g - m * (C::R * 32);
+          const int k = rem >> 5;
+          const int n8 = rem & 31;
+          const uint2 q = *reinterpret_cast<const uint2*>(wq + m * C::R * kTileN + k * kTileN + n8 * 8);
+          const __half2 sc = __half2half2(to_f16(ws[m * C::R * 8 + k * 8 + (n8 >> 2)]));
+          // byte b (offset by 128) -> f16 1024 + b -> minus 1152 = the int8 value, exactly
+          const uint32_t w0 = q.x ^ 0x80808080u, w1 = q.y ^ 0x80808080u;
+          const __half2 k1152 = __half2half2(__ushort_as_half(0x6480u));
+          uint4 o;
+          o.x = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w0, 0x64646464u, 0x4140u)), k1152), sc));
+          o.y = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w0, 0x64646464u, 0x4342u)), k1152), sc));
+          o.z = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w1, 0x64646464u, 0x4140u)), k1152), sc));
+          o.w = h2_bits(__hmul2(__hsub2(bits_h2(__byte_perm(w1, 0x64646464u, 0x4342u)), k1152), sc));
+          *reinterpret_cast<uint4*>(bt + m * C::kBMatBytes + b_offset(n8 * 8, k)) = o;
         }
-        *s_last = last;
+        umma::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[s]);
       }
-      named_bar(1, kDequant);
-    }
-    if (p.splits == 1 || *s_last) {
-      for (int c0 = cbeg; c0 < cbeg + kColsPerWarp; c0 += 16) {
-        float acc[NMAT][16];
-        if (p.splits == 1) {
+      if (!ok) break;
+      // epilogue of this segment: this warp reads TMEM lanes 32*(warp % 4) .. +31 = tile rows
+      if (!mbar_wait(accfull, static_cast<uint32_t>(i) & 1u, p.status)) break;
+      umma::fence_after_sync();
+      const int slab = sg.tile / p.mtiles;
+      const int t = (sg.tile - slab * p.mtiles) * kBM + row;
+      const bool whole = sg.k0 == 0 && sg.k1 == p.upt;
+      const bool finisher = sg.k0 == 0 && sg.k1 < p.upt;
+      if (!whole && !finisher) {
+        // a tile's continuation: partial into this CTA's slot, then release it
+        for (int c0 = cbeg; c0 < cbeg + kColsPerWarp; c0 += 16) {
 #pragma unroll
           for (int m = 0; m < NMAT; ++m) {
             uint32_t a[16];
             umma::tmem_ld16(trow + m * kBN + c0, a);
             umma::tmem_wait_ld();
+            float4* dst = reinterpret_cast<float4*>(part_at(c, m, c0));
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[m][i] = __uint_as_float(a[i]);
+            for (int q = 0; q < 4; ++q)
+              __stcg(dst + q, make_float4(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1]),
+                                          __uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])));
           }
-        } else {
+        }
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_free);
+        __threadfence();
+        named_bar(1, kDequant);
+        if (dt == 0) st_release_gpu(p.counters + c, 1u);
+        continue;
+      }
+      // whole tile, or the start of a tile finished here with the partials of CTAs c+1..cl
+      int cl = c;
+      if (finisher) {
+        cl = sk_owner(static_cast<int64_t>(sg.tile + 1) * p.upt - 1, total, G);
+        if (dt < cl - c) {
+          if (!wait_flag_eq(p.counters + c + 1 + dt, 1u, 2000000000ull)) atomicExch(p.status, PYRE_ETIMEOUT);
+        }
+        named_bar(1, kDequant);
+      }
+      for (int c0 = cbeg; c0 < cbeg + kColsPerWarp; c0 += 16) {
+        float acc[NMAT][16];
 #pragma unroll
-          for (int m = 0; m < NMAT; ++m)
+        for (int m = 0; m < NMAT; ++m) {
+          uint32_t a[16];
+          umma::tmem_ld16(trow + m * kBN + c0, a);
+          umma::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[m][i] = 0.f;
-          for (int sp = 0; sp < p.splits; ++sp) {
+          for (int q = 0; q < 16; ++q) acc[m][q] = __uint_as_float(a[q]);
+        }
+        for (int src = c + 1; src <= cl; ++src) {
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-              const float4* src = reinterpret_cast<const float4*>(part_at(sp, m, c0));
+          for (int m = 0; m < NMAT; ++m) {
+            const float4* pp = reinterpret_cast<const float4*>(part_at(src, m, c0));
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float4 v = __ldcg(src + i);
-                acc[m][4 * i] += v.x;
-                acc[m][4 * i + 1] += v.y;
-                acc[m][4 * i + 2] += v.z;
-                acc[m][4 * i + 3] += v.w;
-              }
+            for (int q = 0; q < 4; ++q) {
+              const float4 v = __ldcg(pp + q);
+              acc[m][4 * q] += v.x;
+              acc[m][4 * q + 1] += v.y;
+              acc[m][4 * q + 2] += v.z;
+              acc[m][4 * q + 3] += v.w;
             }
           }
         }
@@ -338,16 +386,23 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_c
         const int col0 = slab * kTileN + c0;
         float v[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int q = 0; q < 16; ++q) {
           if constexpr (EPI == ffn::EPI_SILU_MUL) {
-            v[i] = silu_f32(acc[0][i]) * acc[NMAT - 1][i];
+            v[q] = silu_f32(acc[0][q]) * acc[NMAT - 1][q];
           } else if constexpr (EPI == ffn::EPI_SILU) {
-            v[i] = silu_f32(acc[0][i]);
+            v[q] = silu_f32(acc[0][q]);
           } else {
-            v[i] = acc[0][i];
+            v[q] = acc[0][q];
           }
         }
         store_row16(p, t, col0, v);
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_free);
+      if (finisher) {
+        named_bar(1, kDequant);
+        if (dt < cl - c) p.counters[c + 1 + dt] = 0u;   // consumed: back to zero for the next call
       }
     }
   }
@@ -385,33 +440,27 @@ int launch(Params p, const void* a_f16, cudaStream_t s) {
   p.upt = (p.K + C::R - 1) / C::R;
   p.tiles = tiles_of(p.N);
   p.mtiles = (p.T + kBM - 1) / kBM;
-  const int64_t tiles = static_cast<int64_t>(p.tiles) * p.mtiles;
-  if (tiles > 0x7fffffff / kMaxSplits) return set_error(PYRE_EINVAL, "q80_gemm_tc_kernel: too many tiles");
-  // split K when the tiles alone leave SMs idle (one CTA per SM), keeping >= 8 k-steps per
-  // split and the partial tiles within the workspace
-  int splits = 1;
-  const int sms = sm_count();
-  if (tiles < sms && tiles <= kMaxTiles && p.partial != nullptr) {
-    splits = static_cast<int>(sms / tiles);
-    if (splits > kMaxSplits) splits = kMaxSplits;
-    while (splits > 1 && (p.upt / splits < 8 || tiles * splits * kPartBytes<NMAT>() > p.partial_cap)) --splits;
-  }
-  p.splits = splits;
-  kern<<<static_cast<int>(tiles * splits), kThreads, C::kSmemBytes, s>>>(p);
+  const int64_t steps = static_cast<int64_t>(p.tiles) * p.mtiles * p.upt;
+  // stream-K over at most one CTA per SM (all resident: the finishing CTAs wait for the
+  // partials of the next ones), at least kMinSteps k-steps each, slots within the workspace
+  int64_t G = sm_count();
+  if (G > kMaxCtas) G = kMaxCtas;
+  if (G > steps / kMinSteps) G = steps / kMinSteps;
+  if (G < 1) G = 1;
+  if (p.partial == nullptr || G * kPartBytes<NMAT>() > p.partial_cap)
+    return set_error(PYRE_ENOMEM, "q80_gemm_tc_kernel: workspace too small for the stream-K partial tiles");
+  kern<<<static_cast<int>(G), kThreads, C::kSmemBytes, s>>>(p);
   PYRE_LAUNCH_CHECK("q80_gemm_tc_kernel");
   return PYRE_OK;
 }
 
 }  // namespace tc
 
-// Bytes of split-K partial tiles the GEMM over [T, K] x [K, N] may use (0 when the tiles
-// alone can fill the GPU): at most 160 CTAs (>= the SM count of a B200) of partial tiles.
+// Bytes of stream-K partial tiles the GEMM over [T, K] x [K, N] uses: one tile slot per CTA.
 int64_t ffn_gemm_partial_bytes(int T, int N, int nmat) {
-  const int64_t tiles = static_cast<int64_t>(gemv::tiles_of(N)) * ((T + tc::kBM - 1) / tc::kBM);
-  if (tiles >= 160) return 0;
-  int64_t ctas = tiles * tc::kMaxSplits;
-  if (ctas > 160) ctas = 160;
-  return ctas * nmat * 256 * 128 * 4;
+  (void)T;
+  (void)N;
+  return static_cast<int64_t>(tc::kMaxCtas) * nmat * 256 * 128 * 4;
 }
 
 // Tensor-core GEMM form of the FFN halves for T > 4 (used by ffn.cu).
