@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
-    ap.add_argument("--no-attention", action="store_true", help="skip the attention measurements")
+    ap.add_argument("--no-attention", action="store_true", help="skip the attention and lm_head measurements")
     return ap.parse_args()
 
 
@@ -194,6 +194,44 @@ def attention_bench(dev, stream, hbm, tf_burst):
                     "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / tf_burst, 4),
                     "kernel": "attn_prefill_tc_kernel (tcgen05, S and O in tensor memory, TMA-fed) + rope_append_kernel"},
     }
+
+
+def lmhead_bench(dev, stream, hbm):
+    """Mistral-7B shape last decode step: final RMSNorm + lm_head (f16 [32768, 4096], 268 MB,
+    larger than L2) + greedy token, T = 1, one launch per token."""
+    import torch
+    from pyre_b200.lmhead import LmHeadOp
+    V, Hh = 32768, 4096
+    gen = torch.Generator(device=dev).manual_seed(7)
+    table = (torch.randn((V, Hh), generator=gen, device=dev) * 0.02).to(torch.float16)
+    norm = 1 + 0.1 * torch.randn(Hh, generator=gen, device=dev)
+    op = LmHeadOp(table, norm, max_tokens=1)
+    h = torch.randn((1, Hh), generator=gen, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            op(h, stream=stream)
+    stream.synchronize()
+    reps = 20
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(reps):
+            op(h, stream=stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    e1.record(stream)
+    stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    nbytes = V * Hh * 2
+    del g
+    return {"shape": "Mistral-7B lm_head: vocab 32768, hidden 4096, f16 table, final RMSNorm, greedy token",
+            "us_per_token": round(us, 2), "table_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "frac_of_hbm": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
+            "kernel": "lm_head_kernel (norm + f16 GEMV + argmax key, one launch)"}
 
 
 # ---------------------------------------------------------------------------------------
@@ -431,6 +469,7 @@ def run_ours(args):
         check_status(op, "prefill")
 
     attn = None if args.no_attention else attention_bench(dev, stream, hbm, tf_burst)
+    lmh = None if args.no_attention else lmhead_bench(dev, stream, hbm)
     barrier()
 
     # max over ranks
@@ -469,7 +508,9 @@ def run_ours(args):
             "gpu_launches": args.steps * op.launches(T),
             "e2e": {"value": round(e2e_steps * T / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": e2e_runners[0].h2d_bytes, "d2h_bytes_per_step": e2e_runners[0].d2h_bytes,
-                    "how": "CapturedFfn.execute(host x) per call: pinned H2D, graph of the op, D2H, stream sync"},
+                    "how": "CapturedFfn.execute(host x) per call: one native call (host copy into the pinned input, "
+                           "graph launch: H2D copy, the op storing its result into pinned host memory "
+                           "over PCIe; stream wait)"},
             "clocks": clocks,
         }
         if prefill:
@@ -480,6 +521,8 @@ def run_ours(args):
                               "frac_of_bf16_peak": round(flops / (pf_ms * 1e-3) / 1e12 / (tf_burst * world), 4)}
         if attn:
             res["attention"] = attn
+        if lmh:
+            res["lm_head"] = lmh
         if not args.no_cpu:
             _, cpu = cpu_reference_leg(T, args.cpu_seconds)
             res["cpu_baseline"] = cpu

@@ -260,6 +260,22 @@ PYRE_API int pyre_attn_decode_step(const float* q, const float* k, const float* 
                                    uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo, int mask_hi,
                                    float* out, void* workspace, int64_t ws_bytes, void* stream);
 
+/* ---- last decode step: final norm, lm_head, greedy token ------------------------------
+ * Replaces Generator._rms_norm / _compute_logits / _sample at temperature < 0.01
+ * (src/orchestrator/generator.py:40-53): rows of h f32 [T, H] (T <= 4) are normalised
+ * (f64 mean of squares, x / sqrt(var + eps) in f64, times norm_w f32 [H]; norm_w NULL: no
+ * norm), logits = h_norm . lm_head^T with the f16 table lm_head [V, H] (f32 accumulation),
+ * token[t] = index of the largest logit of row t (the first among equal maxima, like
+ * np.argmax). Rows of lm_head are the global vocabulary indices v0 .. v0 + V - 1 (a
+ * vocab-sharded table: one shard per rank). logits f32 [T, V] and key [T] may be NULL; key
+ * gets an int64 that orders (value, lower index) like the argmax, so the shards' keys combine
+ * with a signed max reduction (index = 0xFFFFFFFF - (low 32 bits)). workspace:
+ * pyre_lm_head_workspace_bytes, zeroed once, reused call after call on one stream. */
+PYRE_API int pyre_lm_head_workspace_bytes(int T, int64_t* bytes);
+PYRE_API int pyre_lm_head_argmax(const float* h, int T, int H, const float* norm_w, double eps,
+                                 const uint16_t* lm_head, int V, int64_t v0, float* logits, int* token,
+                                 long long* key, void* workspace, int64_t ws_bytes, void* stream);
+
 /* ---- Ulysses sequence parallelism over NVLink (one process per GPU, P <= 16) ----------
  * Replaces the gather of every node's q/k/v at the root over TCP and the full-sequence
  * attention there (src/orchestrator/root_node.py:250-314; Ulysses mode :110): rank r owns

@@ -74,6 +74,8 @@ _SIGNATURES = {
                             _vp, _vp, _vp, _i, _vp],
     "pyre_attn_status": [ctypes.POINTER(_i)],
     "pyre_graph_run": [_vp, _vp, _vp, _vp, _c_i64],
+    "pyre_lm_head_workspace_bytes": [_i, ctypes.POINTER(_c_i64)],
+    "pyre_lm_head_argmax": [_vp, _i, _i, _vp, ctypes.c_double, _vp, _i, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _vp],
     "pyre_attn_prefill": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp],
     "pyre_attn_decode_workspace_bytes": [_i, _i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_attn_decode": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _c_i64, _vp],

@@ -35,10 +35,17 @@ class CapturedFfn:
             op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
         self.stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
+        # decode path (one streaming launch): its kernel stores the result straight into the
+        # pinned host buffer over PCIe (zero-copy), so the graph has no device->host copy node;
+        # larger T keep the device output and a copy node
+        self.zero_copy_out = tokens <= N.PYRE_FUSED_REDUCE_MAX_T and op.fused
         with torch.cuda.graph(self.graph, stream=self.stream):
             self.x_dev.copy_(self.x_host, non_blocking=True)
-            op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
-            self.out_host.copy_(self.out_dev, non_blocking=True)
+            if self.zero_copy_out:
+                op.run(self.x_dev, weights, out=self.out_host, stream=self.stream)
+            else:
+                op.run(self.x_dev, weights, out=self.out_dev, stream=self.stream)
+                self.out_host.copy_(self.out_dev, non_blocking=True)
         # the instantiated graph, launched by the library's native runner
         lib = N.load()
         self._exec = self.graph.raw_cuda_graph_exec()

@@ -24,6 +24,11 @@ Run in a container that has the reference checkout (read-only) at /root/referenc
                          concatenation order, layout, RoPE position, clipping, GQA, scale,
                          causal and padding masks.
 
+* lmhead_golden.npz    — reference ``Generator._compute_logits`` / ``_rms_norm`` /
+                         ``_sample`` at temperature 0 (src/orchestrator/generator.py:40-53):
+                         final RMSNorm, logits against the f16 lm_head table, greedy token,
+                         including rows with tied maxima.
+
 Only this script touches /root/reference; tests read the fixtures.
 """
 from __future__ import annotations
@@ -283,13 +288,40 @@ def make_attention() -> None:
     print("attn_golden.npz written")
 
 
+def make_lmhead() -> None:
+    import types
+    from src.orchestrator.generator import Generator
+    rng = np.random.default_rng(31)
+    out = {}
+    for name, (T, H, V) in {"small": (1, 64, 1000), "rows": (3, 96, 517)}.items():
+        h = (rng.standard_normal((T, H)) * 3).astype(np.float32)
+        w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        E = (rng.standard_normal((V, H)) * 0.05).astype(np.float16)
+        if name == "rows":
+            E[200] = E[7]                      # tied maxima: the first index wins
+            E[301] = E[7]
+            h[1] = E[7].astype(np.float32) * 40.0
+        fake = types.SimpleNamespace(final_norm=w.astype(np.float16), lm_head=E)
+        fake._rms_norm = lambda x, eps=1e-6, fake=fake: Generator._rms_norm(fake, x, eps)
+        logits = Generator._compute_logits(fake, h)
+        tok = np.concatenate([Generator._sample(logits[t:t + 1], temperature=0.0) for t in range(T)], axis=0)
+        out[f"{name}__h"], out[f"{name}__w"], out[f"{name}__E"] = h, w.astype(np.float16), E
+        out[f"{name}__logits"], out[f"{name}__token"] = logits.astype(np.float32), tok.astype(np.int64)
+    np.savez_compressed(HERE / "lmhead_golden.npz", **out)
+    print("lmhead_golden.npz written")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default=None, help="write one fixture: q80, ffn, partition, attention or lmhead")
     args = ap.parse_args()
     ref = Path(args.ref)
     sys.path.insert(0, str(HERE / "max_shim"))
     sys.path.insert(0, str(ref))
+    if args.only == "lmhead":
+        make_lmhead()
+        return
     quantizer = _load_module(ref / "src" / "orchestrator" / "quantizer.py", "ref_quantizer")
     make_q80(quantizer)
     make_ffn(ref, quantizer)
@@ -298,6 +330,7 @@ def main() -> None:
         make_partition()
     print("partition_golden.json written")
     make_attention()
+    make_lmhead()
 
 
 if __name__ == "__main__":

@@ -264,7 +264,7 @@ def test_prefill_split_k_deterministic():
     assert rel_err(outs[0].cpu().numpy(), offn.ffn_shard_f64(x, gd, ud, dd)) < TOL_BF16
 
 
-@pytest.mark.parametrize("T", [1, 3])
+@pytest.mark.parametrize("T", [1, 3, 6])
 def test_captured_ffn_host_in_host_out(T):
     """CapturedFfn.execute (host input -> native graph run -> pinned host output) equals the
     op on device tensors, for a same-dtype host tensor (copied by the native runner) and for a
@@ -276,9 +276,10 @@ def test_captured_ffn_host_in_host_out(T):
     g, _ = make_weight((H, W), rng, torch.float16)
     u, _ = make_weight((H, W), rng, torch.float16)
     d, _ = make_weight((W, H), rng, torch.float16)
-    op = FfnShardOp(H, W, max_tokens=4)
+    op = FfnShardOp(H, W, max_tokens=max(T, 4))
     fw = FfnWeights.prepare(g, u, d)
     run = CapturedFfn(op, fw, tokens=T)
+    assert run.zero_copy_out == (T <= 4)     # decode: the kernel writes the pinned output itself
     for i in range(3):
         x = torch.from_numpy(bf16_round(rng.standard_normal((T, H)))).to(torch.bfloat16)
         want = op.run(x.cuda(), fw).cpu()
