@@ -38,6 +38,27 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
   return PYRE_OK;
 }
 
+// The T > 4 path keeps its f16 activation staging and stream-K partial tiles at the END of
+// the workspace, clear of the decode accumulators at its start (which must be zero on entry
+// to a decode call), so one workspace serves prefill and decode calls in any order.
+struct GemmRegion {
+  char* stage;
+  int64_t stage_bytes;
+  char* part;
+  int64_t part_bytes;
+};
+
+int gemm_region(void* workspace, int64_t ws_bytes, int T, int K, int N, int nmat, GemmRegion* r, const char* f) {
+  const int64_t stage = ffn_gemm_staging_bytes(T, K, N);
+  const int64_t part = ffn_gemm_partial_bytes(T, N, nmat);
+  const int64_t base = (ws_bytes - stage - part) / 256 * 256;
+  if (base < gemv::kHeaderBytes)
+    return set_error(PYRE_ENOMEM, std::string(f) + ": workspace smaller than pyre_ffn_workspace_bytes()");
+  char* wsc = static_cast<char*>(workspace);
+  *r = GemmRegion{wsc + base, stage, wsc + base + stage, part};
+  return PYRE_OK;
+}
+
 }  // namespace pyre
 
 using namespace pyre;
@@ -56,9 +77,11 @@ extern "C" int pyre_ffn_gateup_silu_q80(const void* x, int x_dtype, int T, int H
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_gateup(x, x_dtype, T, H, wgu, gated, scale_dtype, W, h, h_dtype, workspace, ws_bytes, s);
   char* wsc = static_cast<char*>(workspace);
-  const int64_t stage = ffn_gemm_staging_bytes(T, H, W);
+  GemmRegion g;
+  rc = gemm_region(workspace, ws_bytes, T, H, W, gated ? 2 : 1, &g, "pyre_ffn_gateup_silu_q80");
+  if (rc) return rc;
   return ffn_gemm_tc(x, x_dtype, T, H, wgu, gated ? 2 : 1, gated ? EPI_SILU_MUL : EPI_SILU, scale_dtype, W, h,
-                     h_dtype, wsc + kHeaderBytes, stage, wsc + kHeaderBytes + stage, ws_bytes - kHeaderBytes - stage,
+                     h_dtype, g.stage, g.stage_bytes, g.part, g.part_bytes,
                      reinterpret_cast<unsigned int*>(wsc + kHdrCntA), reinterpret_cast<int*>(wsc + kHdrStatus), s);
 }
 
@@ -76,10 +99,12 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_down(h, h_dtype, T, W, wd, scale_dtype, H, out, workspace, ws_bytes, comm, s);
   char* wsc = static_cast<char*>(workspace);
-  const int64_t stage = ffn_gemm_staging_bytes(T, H, W);
-  rc = ffn_gemm_tc(h, h_dtype, T, W, wd, 1, EPI_STORE, scale_dtype, H, out, PYRE_F32, wsc + kHeaderBytes, stage,
-                   wsc + kHeaderBytes + stage, ws_bytes - kHeaderBytes - stage,
-                   reinterpret_cast<unsigned int*>(wsc + kHdrCntA), reinterpret_cast<int*>(wsc + kHdrStatus), s);
+  GemmRegion g;
+  rc = gemm_region(workspace, ws_bytes, T, W, H, 1, &g, "pyre_ffn_down_q80");
+  if (rc) return rc;
+  rc = ffn_gemm_tc(h, h_dtype, T, W, wd, 1, EPI_STORE, scale_dtype, H, out, PYRE_F32, g.stage, g.stage_bytes, g.part,
+                   g.part_bytes, reinterpret_cast<unsigned int*>(wsc + kHdrCntA),
+                   reinterpret_cast<int*>(wsc + kHdrStatus), s);
   const bool tp = comm != nullptr && comm->world > 1;
   if (rc || !tp) return rc;
   return allreduce_sum_f32(comm, out, static_cast<int64_t>(T) * H, s);
@@ -95,8 +120,10 @@ extern "C" int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const v
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
     return ffn_stream_down(x, x_dtype, T, K, w, scale_dtype, N, out, workspace, ws_bytes, nullptr, s);
   char* wsc = static_cast<char*>(workspace);
-  const int64_t stage = ffn_gemm_staging_bytes(T, K, N);
-  return ffn_gemm_tc(x, x_dtype, T, K, w, 1, EPI_STORE, scale_dtype, N, out, PYRE_F32, wsc + kHeaderBytes, stage,
-                     wsc + kHeaderBytes + stage, ws_bytes - kHeaderBytes - stage,
-                     reinterpret_cast<unsigned int*>(wsc + kHdrCntA), reinterpret_cast<int*>(wsc + kHdrStatus), s);
+  GemmRegion g;
+  rc = gemm_region(workspace, ws_bytes, T, K, N, 1, &g, "pyre_q80_linear");
+  if (rc) return rc;
+  return ffn_gemm_tc(x, x_dtype, T, K, w, 1, EPI_STORE, scale_dtype, N, out, PYRE_F32, g.stage, g.stage_bytes, g.part,
+                     g.part_bytes, reinterpret_cast<unsigned int*>(wsc + kHdrCntA),
+                     reinterpret_cast<int*>(wsc + kHdrStatus), s);
 }

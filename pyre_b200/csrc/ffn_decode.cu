@@ -15,7 +15,10 @@ int64_t stream_acc_bytes(int T, int N, int nmat) {
 
 // Workspace layouts (after the kHeaderBytes header):
 //   MODE_A / MODE_B : accumulators of that phase
-//   MODE_AB         : h [T, W] f32 | accumulators A | accumulators B
+//   MODE_AB         : accumulators A | accumulators B | ... | h [T, W] f32 at the end
+// The accumulators must be zero when a call starts (each call zeroes what it used); h and the
+// tensor-core GEMM's staging and partial tiles are plain data and sit at the END of the
+// workspace, so calls with any T (and of either path) can share one workspace.
 int64_t decode_ws_bytes(int T, int H, int W, int na) {
   return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + stream_acc_bytes(T, W, na) +
          stream_acc_bytes(T, H, 1);
@@ -180,14 +183,14 @@ using namespace pyre::ffn;
 extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   PYRE_CHECK_ARG(bytes != nullptr, "pyre_ffn_workspace_bytes: null bytes");
   PYRE_CHECK_ARG(T >= 1 && H >= 1 && W >= 1, "pyre_ffn_workspace_bytes: sizes must be positive");
-  // decode (T <= 4, also the two-call forms) and, for larger T, the bf16 copy of f32
-  // activations that the tensor-core GEMM reads
+  // decode (T <= 4, also the two-call forms) at the start and, for larger T, the tensor-core
+  // GEMM's f16 activation staging and partial tiles after it (placed from the end by the
+  // GEMM calls): the two never overlap, so calls of either kind can follow each other
   const int td = T < PYRE_FUSED_REDUCE_MAX_T ? T : PYRE_FUSED_REDUCE_MAX_T;
   int64_t need = decode_ws_bytes(td, H, W, 2);
   if (T > PYRE_FUSED_REDUCE_MAX_T) {
     const int64_t pg = ffn_gemm_partial_bytes(T, W, 2), pd = ffn_gemm_partial_bytes(T, H, 1);
-    const int64_t gemm = kHeaderBytes + ffn_gemm_staging_bytes(T, H, W) + (pg > pd ? pg : pd);
-    if (gemm > need) need = gemm;
+    need += ffn_gemm_staging_bytes(T, H, W) + (pg > pd ? pg : pd) + 256;
   }
   *bytes = need;
   return PYRE_OK;
@@ -221,11 +224,13 @@ extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, con
   p.wb = static_cast<const uint8_t*>(wd);
   fill_phase(p, false, H, W, na);
   fill_phase(p, true, W, H, 1);
-  p.outA = wsc + kHeaderBytes;   // h [T, W] f32
+  // accumulators (zero on entry, zeroed again by the kernel) right after the header; h, plain
+  // data, at the end of the workspace, where a call with another T finds no accumulator of its own
+  p.accA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
+  p.accB = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(p.accA) + stream_acc_bytes(T, W, na));
+  p.outA = wsc + (ws_bytes - align256(static_cast<int64_t>(T) * W * 4)) / 256 * 256;   // h [T, W] f32
   p.outA_bf16 = 0;
   p.outB = out;
-  p.accA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4));
-  p.accB = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(p.accA) + stream_acc_bytes(T, W, na));
   fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);
   StreamArgs a{MODE_AB, tp, x, x_dtype, nullptr, PYRE_F32};

@@ -88,9 +88,35 @@ def test_ffn_deterministic_and_workspace_reuse():
     assert int(hdr[2]) == 0                                  # status word
     assert int(hdr[4]) == 0                                  # chunk queue position reset
     assert int(hdr[256:256 + 2 * 2048].abs().sum()) == 0     # per-slab chunk counters reset
-    # after the h buffer ([2, 3072] f32) come the fixed-point slab accumulators: cleared
-    acc = op.workspace[32768 + 2 * 3072 * 4:]
+    # the fixed-point slab accumulators follow the header and are cleared; the h buffer
+    # ([2, 3072] f32, plain data) is the last part of the workspace
+    acc = op.workspace[32768:op.workspace.numel() - 2 * 3072 * 4]
     assert int(acc.count_nonzero()) == 0
+
+
+def test_one_workspace_serves_prefill_and_decode_calls():
+    """A prefill call (T > 4: tensor-core GEMM) followed by decode calls (T <= 4: the streaming
+    kernel, whose fixed-point accumulators must be zero on entry) on the same op and the same
+    workspace, in both orders: every call equals a fresh op's result."""
+    from pyre_b200.attention.ops import Q80Linear
+    from pyre_b200.ffn import FfnShardOp, FfnWeights
+    rng = np.random.default_rng(21)
+    H, W = 576, 1536
+    g, gd = make_weight((H, W), rng, torch.float16)
+    u, ud = make_weight((H, W), rng, torch.float16)
+    d, dd = make_weight((W, H), rng, torch.float16)
+    fw = FfnWeights.prepare(g, u, d)
+    op = FfnShardOp(H, W, max_tokens=64)
+    lin = Q80Linear(u, max_tokens=64)
+    for T in (8, 1, 1, 64, 3, 17, 1):
+        x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).cuda()
+        out = op.run(x, fw).cpu().numpy()
+        assert op.status() == 0, T
+        ref = offn.ffn_shard_f64(x.cpu().numpy(), gd, ud, dd)
+        assert rel_err(out, ref) < (TOL_F32 if T <= 4 else TOL_BF16), T
+        y = lin(x).cpu().numpy()
+        yref = x.cpu().numpy().astype(np.float64) @ ud
+        assert rel_err(y, yref) < (TOL_F32 if T <= 4 else TOL_BF16), T
 
 
 def test_ffn_range_status_and_reset():
