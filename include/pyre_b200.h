@@ -205,6 +205,14 @@ PYRE_API int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const voi
  * [rows, H]; w: f32 [H]. */
 PYRE_API int pyre_rms_norm(const float* x, int rows, int H, const float* w, double eps, float* out, void* stream);
 
+/* h = x + delta (f32, the residual adds h = x + attn_out and out = h + ffn_out of
+ * src/orchestrator/root_node.py:947, :997), then norm = rms_norm(h, w) exactly as
+ * pyre_rms_norm (the next RMSNorm, root_node.py:951 / :752): one launch for the glue between
+ * the attention, the FFN and the next layer. h may alias x. w and norm both null: add only.
+ * x, delta, h, norm: f32 [rows, H]; w: f32 [H]. */
+PYRE_API int pyre_add_rms_norm(const float* x, const float* delta, int rows, int H, const float* w, double eps,
+                               float* h, float* norm, void* stream);
+
 /* Softmax over the last axis of an f32 [rows, cols] matrix, max initialised to -1e10 and
  * exp(x - max) * (1 / sum) (pyre_kernels.mojo:39-58). */
 PYRE_API int pyre_softmax_rows(const float* x, int64_t rows, int cols, float* out, void* stream);
@@ -271,10 +279,71 @@ PYRE_API int pyre_attn_decode_step(const float* q, const float* k, const float* 
  * gets an int64 that orders (value, lower index) like the argmax, so the shards' keys combine
  * with a signed max reduction (index = 0xFFFFFFFF - (low 32 bits)). workspace:
  * pyre_lm_head_workspace_bytes, zeroed once, reused call after call on one stream. */
+/* x[t, :] = f32(table[ids[t], :]) for T token ids (Generator._embed,
+ * src/orchestrator/generator.py:38-39, on the f16 table), then norm = rms_norm(x, w) as
+ * pyre_rms_norm (the first layer's input RMSNorm, root_node.py:752); w and norm both null:
+ * gather only. ids: int32 on the device. An id outside [0, V) gives a zero row and writes
+ * PYRE_EINVAL to *status (when status is not null). */
+PYRE_API int pyre_embed_rms_norm(const int* ids, int T, const void* table, int V, int H, const float* w, double eps,
+                                 float* x, float* norm, int* status, void* stream);
 PYRE_API int pyre_lm_head_workspace_bytes(int T, int64_t* bytes);
 PYRE_API int pyre_lm_head_argmax(const float* h, int T, int H, const float* norm_w, double eps,
                                  const uint16_t* lm_head, int V, int64_t v0, float* logits, int* token,
                                  long long* key, void* workspace, int64_t ws_bytes, void* stream);
+
+/* ---- decode step of a whole decoder ----------------------------------------------------
+ * One greedy token of a Llama-style decoder (src/orchestrator/generator.py:117-131 over
+ * RootNode._decode_single_layer, root_node.py:739-1007, head-partitioned with every head
+ * local) as the launch sequence embed_rms_norm -> per layer {q80_linear [Wq|Wk|Wv],
+ * attn_decode_step, q80_linear Wo, add_rms_norm, ffn_decode_q80, add_rms_norm} ->
+ * lm_head_argmax, issued from one host call. All pointers are device memory the caller
+ * allocated; the structs are read on every call (nothing is retained). */
+typedef struct pyre_decoder_layer {
+  const void* qkv_w;   /* packed single Q8_0 matrix [H, (nq + 2 nkv) hd] (pyre_q80_pack, M = 1) */
+  void* qkv_ws;        /* pyre_ffn_workspace_bytes(1, H, (nq + 2 nkv) hd), zeroed once */
+  int64_t qkv_ws_bytes;
+  const void* o_w;     /* packed [nq hd, H] */
+  void* o_ws;
+  int64_t o_ws_bytes;
+  const void* gateup_w; /* FFN gate/up pair (or up alone) and down, as pyre_ffn_decode_q80 */
+  const void* down_w;
+  int gated;
+  void* ffn_ws;
+  int64_t ffn_ws_bytes;
+  const float* ln1;    /* input_layernorm [H] */
+  const float* ln2;    /* post_attention_layernorm [H] */
+  uint16_t* k_cache;   /* f16 [nkv, max_t, hd] */
+  uint16_t* v_cache;
+  const float* rope;   /* pyre_rope_table for max_t positions */
+  void* attn_ws;       /* pyre_attn_decode_workspace_bytes */
+  int64_t attn_ws_bytes;
+} pyre_decoder_layer;
+
+typedef struct pyre_decoder_desc {
+  int n_layers, H, nq, nkv, hd, ffn_width, V, max_t;
+  int scale_dtype;     /* PYRE_F32 or PYRE_F16, every matrix */
+  double eps, rope_fraction;
+  const pyre_decoder_layer* layers; /* host array of n_layers */
+  const void* embedding; /* f16 [V, H] */
+  const uint16_t* lm_head; /* f16 [V, H] (the embedding when tied) */
+  const float* final_norm; /* [H] or NULL */
+  void* lm_ws;         /* pyre_lm_head_workspace_bytes(1) */
+  int64_t lm_ws_bytes;
+  float *x, *xn, *hn, *qkv, *attn, *ao, *f; /* scratch: [H] x3, [(nq + 2 nkv) hd], [nq hd], [H] x2 */
+  int* status;         /* embedding status word */
+  long long* key;      /* [1] */
+} pyre_decoder_desc;
+
+/* One decode step: token_in (int32 [1], device) at position pos (= tokens already in the
+ * caches), positions [mask_lo, mask_hi) masked (the reference's padded prefill; 0, 0: none).
+ * Writes the greedy token to token_out (int32 [1], device) and, when logits is not NULL, the
+ * logits f32 [V]. */
+/* sizeof(pyre_decoder_layer) and sizeof(pyre_decoder_desc), for bindings that lay the
+ * structs out themselves (ctypes, cgo) to check their layout against. */
+PYRE_API int pyre_decoder_struct_sizes(int64_t* layer_bytes, int64_t* desc_bytes);
+
+PYRE_API int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in, int pos, int mask_lo, int mask_hi,
+                               int* token_out, float* logits, void* stream);
 
 /* ---- Ulysses sequence parallelism over NVLink (one process per GPU, P <= 16) ----------
  * Replaces the gather of every node's q/k/v at the root over TCP and the full-sequence

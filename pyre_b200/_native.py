@@ -68,6 +68,10 @@ _SIGNATURES = {
     "pyre_allreduce_sum_f32": [_vp, _vp, _c_i64, _vp],
     "pyre_q80_linear": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp],
     "pyre_rms_norm": [_vp, _i, _i, _vp, ctypes.c_double, _vp, _vp],
+    "pyre_add_rms_norm": [_vp, _vp, _i, _i, _vp, ctypes.c_double, _vp, _vp, _vp],
+    "pyre_decoder_step": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp],
+    "pyre_decoder_struct_sizes": [_vp, _vp],
+    "pyre_embed_rms_norm": [_vp, _i, _vp, _i, _i, _vp, ctypes.c_double, _vp, _vp, _vp, _vp],
     "pyre_softmax_rows": [_vp, _c_i64, _i, _vp, _vp],
     "pyre_rope_table": [ctypes.c_double, ctypes.c_double, _i, _i, _vp],
     "pyre_rope_kv_append": [_vp, _vp, _vp, _c_i64, _c_i64, _i, _i, _i, _i, _i, _vp, ctypes.c_double,

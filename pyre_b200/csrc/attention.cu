@@ -58,6 +58,37 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
     out[row * H + i] = static_cast<float>(static_cast<double>(xr[i]) * rstd * static_cast<double>(w[i]));
 }
 
+// h = x + delta (the f32 residual add of root_node.py:947 / :997), then norm = rms_norm(h, w)
+// as rms_norm_kernel; one CTA per row. h may alias x; norm may be null (add only).
+__global__ void add_rms_norm_kernel(const float* x, const float* __restrict__ delta, float* h,
+                                    const float* __restrict__ w, float* __restrict__ norm, int H, double eps) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * H;
+  const float* dr = delta + row * H;
+  float* hr = h + row * H;
+  double sq = 0.0;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = __fadd_rn(xr[i], dr[i]);
+    hr[i] = v;
+    sq += static_cast<double>(v) * static_cast<double>(v);
+  }
+  if (norm == nullptr) return;
+  __shared__ double red[32];
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const double rstd = 1.0 / sqrt(red[0] / H + eps);
+  // each thread reads back only the elements it wrote above
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    norm[row * H + i] = static_cast<float>(static_cast<double>(hr[i]) * rstd * static_cast<double>(w[i]));
+}
+
 // ---------------------------------------------------------------------------------------
 __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ out, int C) {
   const int64_t row = blockIdx.x;
@@ -967,6 +998,17 @@ extern "C" int pyre_rms_norm(const float* x, int rows, int H, const float* w, do
   if (rows == 0) return PYRE_OK;
   rms_norm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, w, out, H, eps);
   PYRE_LAUNCH_CHECK("rms_norm_kernel");
+  return PYRE_OK;
+}
+
+extern "C" int pyre_add_rms_norm(const float* x, const float* delta, int rows, int H, const float* w, double eps,
+                                 float* h, float* norm, void* stream) {
+  PYRE_CHECK_ARG(x != nullptr && delta != nullptr && h != nullptr, "pyre_add_rms_norm: null pointer");
+  PYRE_CHECK_ARG((norm == nullptr) == (w == nullptr), "pyre_add_rms_norm: norm and w go together");
+  PYRE_CHECK_ARG(rows >= 0 && H >= 1, "pyre_add_rms_norm: bad sizes");
+  if (rows == 0) return PYRE_OK;
+  add_rms_norm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, h, w, norm, H, eps);
+  PYRE_LAUNCH_CHECK("add_rms_norm_kernel");
   return PYRE_OK;
 }
 

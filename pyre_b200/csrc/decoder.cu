@@ -1,0 +1,60 @@
+// Host-side decode step of a Llama-style decoder: the launch sequence of one greedy token
+// in one C call, so a step costs ~6 launches per layer of host time instead of a Python
+// round trip per launch.
+//
+// One step (src/orchestrator/generator.py:117-131 over root_node.py:739-1007):
+//   embed_rms_norm                  x = f32(table[token]), xn = rms_norm(x, ln1[0])
+//   per layer:
+//     q80 linear                    qkv = xn @ [Wq | Wk | Wv]
+//     attention decode step         RoPE at `pos`, clip, KV append, flash-decoding, mask
+//     q80 linear                    ao = attn @ Wo
+//     add_rms_norm                  x += ao, hn = rms_norm(x, ln2)
+//     FFN decode                    f = down(silu(hn @ Wgate) * (hn @ Wup))
+//     add_rms_norm                  x += f, xn = rms_norm(x, ln1[next])   (add only after the last)
+//   lm_head argmax                  final RMSNorm, logits, greedy token
+// Every buffer is the caller's (device memory it allocated once); nothing is allocated here.
+#include "common.cuh"
+
+extern "C" int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in, int pos, int mask_lo, int mask_hi,
+                                 int* token_out, float* logits, void* stream) {
+  PYRE_CHECK_ARG(d != nullptr && d->layers != nullptr && token_in != nullptr && token_out != nullptr,
+                 "pyre_decoder_step: null pointer");
+  PYRE_CHECK_ARG(d->n_layers >= 1 && d->H >= 1 && d->nq >= 1 && d->nkv >= 1 && d->hd >= 1 && d->ffn_width >= 1 &&
+                     d->V >= 1,
+                 "pyre_decoder_step: bad sizes");
+  PYRE_CHECK_ARG(pos >= 0 && pos < d->max_t, "pyre_decoder_step: position outside the KV cache");
+  const int H = d->H, qw = d->nq * d->hd, kw = d->nkv * d->hd, nqkv = qw + 2 * kw;
+  int rc = pyre_embed_rms_norm(token_in, 1, d->embedding, d->V, H, d->layers[0].ln1, d->eps, d->x, d->xn, d->status,
+                               stream);
+  if (rc) return rc;
+  for (int i = 0; i < d->n_layers; ++i) {
+    const pyre_decoder_layer& L = d->layers[i];
+    rc = pyre_q80_linear(d->xn, PYRE_F32, 1, H, L.qkv_w, d->scale_dtype, nqkv, d->qkv, L.qkv_ws, L.qkv_ws_bytes,
+                         stream);
+    if (rc) return rc;
+    rc = pyre_attn_decode_step(d->qkv, d->qkv + qw, d->qkv + qw + kw, pos, L.rope, d->rope_fraction, d->nq, d->nkv,
+                               d->hd, L.k_cache, L.v_cache, d->max_t, mask_lo, mask_hi, d->attn, L.attn_ws,
+                               L.attn_ws_bytes, stream);
+    if (rc) return rc;
+    rc = pyre_q80_linear(d->attn, PYRE_F32, 1, qw, L.o_w, d->scale_dtype, H, d->ao, L.o_ws, L.o_ws_bytes, stream);
+    if (rc) return rc;
+    rc = pyre_add_rms_norm(d->x, d->ao, 1, H, L.ln2, d->eps, d->x, d->hn, stream);
+    if (rc) return rc;
+    rc = pyre_ffn_decode_q80(d->hn, PYRE_F32, 1, H, L.gateup_w, L.gated, L.down_w, d->scale_dtype, d->ffn_width, d->f,
+                             L.ffn_ws, L.ffn_ws_bytes, nullptr, stream);
+    if (rc) return rc;
+    const bool last = i + 1 == d->n_layers;
+    rc = pyre_add_rms_norm(d->x, d->f, 1, H, last ? nullptr : d->layers[i + 1].ln1, d->eps, d->x,
+                           last ? nullptr : d->xn, stream);
+    if (rc) return rc;
+  }
+  return pyre_lm_head_argmax(d->x, 1, H, d->final_norm, d->eps, d->lm_head, d->V, 0, logits, token_out, d->key,
+                             d->lm_ws, d->lm_ws_bytes, stream);
+}
+
+extern "C" int pyre_decoder_struct_sizes(int64_t* layer_bytes, int64_t* desc_bytes) {
+  PYRE_CHECK_ARG(layer_bytes != nullptr && desc_bytes != nullptr, "pyre_decoder_struct_sizes: null pointer");
+  *layer_bytes = static_cast<int64_t>(sizeof(pyre_decoder_layer));
+  *desc_bytes = static_cast<int64_t>(sizeof(pyre_decoder_desc));
+  return PYRE_OK;
+}

@@ -202,6 +202,40 @@ int grid_ctas() {
   return n < 1 ? 1 : n;
 }
 
+// x[t, :] = f32(table[ids[t], :]) (Generator._embed, generator.py:38-39), then
+// norm[t, :] = rms_norm(x[t, :], w) as pyre_rms_norm (the first layer's input RMSNorm,
+// root_node.py:752). One CTA per token; an id outside [0, V) yields a zero row and sets
+// *status to PYRE_EINVAL.
+__global__ void embed_rms_norm_kernel(const int* __restrict__ ids, const __half* __restrict__ table, int V, int H,
+                                      const float* __restrict__ w, double eps, float* __restrict__ x,
+                                      float* __restrict__ norm, int* status) {
+  const int64_t t = blockIdx.x;
+  const int id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && status != nullptr) atomicExch(status, PYRE_EINVAL);
+  const __half* row = table + static_cast<int64_t>(ok ? id : 0) * H;
+  double sq = 0.0;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = ok ? __half2float(row[i]) : 0.0f;
+    x[t * H + i] = v;
+    sq += static_cast<double>(v) * static_cast<double>(v);
+  }
+  if (norm == nullptr) return;
+  __shared__ double red[32];
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const double rstd = 1.0 / sqrt(red[0] / H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    norm[t * H + i] = static_cast<float>(static_cast<double>(x[t * H + i]) * rstd * static_cast<double>(w[i]));
+}
+
 }  // namespace lmh
 }  // namespace pyre
 
@@ -263,5 +297,17 @@ extern "C" int pyre_lm_head_argmax(const float* h, int T, int H, const float* no
   }
   if (rc) return rc;
   PYRE_LAUNCH_CHECK("lm_head_kernel");
+  return PYRE_OK;
+}
+
+extern "C" int pyre_embed_rms_norm(const int* ids, int T, const void* table, int V, int H, const float* w, double eps,
+                                   float* x, float* norm, int* status, void* stream) {
+  PYRE_CHECK_ARG(ids != nullptr && table != nullptr && x != nullptr, "pyre_embed_rms_norm: null pointer");
+  PYRE_CHECK_ARG((norm == nullptr) == (w == nullptr), "pyre_embed_rms_norm: norm and w go together");
+  PYRE_CHECK_ARG(T >= 0 && V >= 1 && H >= 1, "pyre_embed_rms_norm: bad sizes");
+  if (T == 0) return PYRE_OK;
+  lmh::embed_rms_norm_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __half*>(table), V, H, w, eps, x, norm, status);
+  PYRE_LAUNCH_CHECK("embed_rms_norm_kernel");
   return PYRE_OK;
 }

@@ -1,0 +1,301 @@
+"""Prefill + greedy decode of a Llama-style decoder on this library's kernels.
+
+Mirrors the reference's single-sequence generation loop, ``Generator.generate``
+(src/orchestrator/generator.py:60-145), over the head-partitioned root layer
+(``RootNode._decode_single_layer``, src/orchestrator/root_node.py:739-1007, and the prefill
+layer at :344-600): per layer
+
+    xn = rms_norm(x, input_layernorm)                     root_node.py:752
+    q, k, v = xn @ Wq, xn @ Wk, xn @ Wv                   :866-897   (one Q8_0 GEMM, [Wq|Wk|Wv])
+    a = attention(rope(q), rope(k) -> cache, v -> cache)  :899-945   (clip +-1000, causal / masked)
+    h = x + a @ Wo;  hn = rms_norm(h, post_attn_ln)       :940-951   (one add+norm launch)
+    f = down(silu(hn @ Wgate) * (hn @ Wup))               :953-979   (the FFN shard op)
+    x = h + f;  xn' = rms_norm(x, next input_ln)          :997       (one add+norm launch)
+
+and ``_embed`` / ``_compute_logits`` / ``_sample(temperature < 0.01)`` (generator.py:38-53) as
+one embedding-gather launch and one lm_head + argmax launch. The reference pads the prompt to
+``seq_len`` and masks the padding in every decode step (generator.py:77-85, root_node.py:
+1024-1025); padding sits after the prompt and attention is causal, so running the true
+prompt alone gives the same hidden states, and decode positions (RoPE angle = number of
+tokens so far, root_node.py:907-916) are the same.
+
+Weights per layer are given as the reference's root weight dict
+(``_get_root_layer_weights``, root_node.py:1033-1048): ``input_layernorm``,
+``post_attention_layernorm``, ``attn: {q, k, v, o}``, ``ffn: {gate, up, down}``; matrices are
+``[in, out]`` (``x @ W``) as :class:`~pyre_b200.quantizer.Q80Weight` (f16 scales) or float
+arrays, which are quantized to Q8_0 on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _device as D
+from . import _native as N
+from .attention.ops import AttentionOp, Q80Linear
+from .ffn.op import FfnShardOp, FfnWeights
+from .lmhead import LmHeadOp
+from .quantizer import Q80Weight
+
+
+class DecoderLayerDesc(ctypes.Structure):
+    """``pyre_decoder_layer`` of include/pyre_b200.h."""
+    _fields_ = [("qkv_w", ctypes.c_void_p), ("qkv_ws", ctypes.c_void_p), ("qkv_ws_bytes", ctypes.c_int64),
+                ("o_w", ctypes.c_void_p), ("o_ws", ctypes.c_void_p), ("o_ws_bytes", ctypes.c_int64),
+                ("gateup_w", ctypes.c_void_p), ("down_w", ctypes.c_void_p), ("gated", ctypes.c_int),
+                ("ffn_ws", ctypes.c_void_p), ("ffn_ws_bytes", ctypes.c_int64),
+                ("ln1", ctypes.c_void_p), ("ln2", ctypes.c_void_p), ("k_cache", ctypes.c_void_p),
+                ("v_cache", ctypes.c_void_p), ("rope", ctypes.c_void_p), ("attn_ws", ctypes.c_void_p),
+                ("attn_ws_bytes", ctypes.c_int64)]
+
+
+class DecoderDesc(ctypes.Structure):
+    """``pyre_decoder_desc`` of include/pyre_b200.h."""
+    _fields_ = [(n, ctypes.c_int) for n in ("n_layers", "H", "nq", "nkv", "hd", "ffn_width", "V", "max_t",
+                                             "scale_dtype")] + \
+               [("eps", ctypes.c_double), ("rope_fraction", ctypes.c_double),
+                ("layers", ctypes.POINTER(DecoderLayerDesc)), ("embedding", ctypes.c_void_p),
+                ("lm_head", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("lm_ws", ctypes.c_void_p),
+                ("lm_ws_bytes", ctypes.c_int64)] + \
+               [(n, ctypes.c_void_p) for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f", "status", "key")]
+
+
+def check_struct_layout() -> None:
+    """The ctypes structs above against the library's sizeof (raises on a mismatch)."""
+    lb, db = ctypes.c_int64(0), ctypes.c_int64(0)
+    N.call("pyre_decoder_struct_sizes", ctypes.byref(lb), ctypes.byref(db))
+    if (lb.value, db.value) != (ctypes.sizeof(DecoderLayerDesc), ctypes.sizeof(DecoderDesc)):
+        raise RuntimeError(f"decoder struct layout differs from the library's: {(lb.value, db.value)} vs "
+                           f"{(ctypes.sizeof(DecoderLayerDesc), ctypes.sizeof(DecoderDesc))}")
+
+
+def _q80(w, device) -> Q80Weight:
+    if isinstance(w, Q80Weight):
+        return Q80Weight(w.q.to(device), w.scale.to(device, torch.float16))
+    t = torch.as_tensor(np.asarray(w, dtype=np.float32)) if not isinstance(w, torch.Tensor) else w.float()
+    return Q80Weight.from_float(t.to(device), scale_dtype=torch.float16)
+
+
+def _concat_n(ws: list[Q80Weight]) -> Q80Weight:
+    """[K, N1] | [K, N2] | ... -> [K, N1 + N2 + ...]: Q8_0 blocks run along N in 32s, so with
+    every N a multiple of 32 the blocks (and scales) of the parts are the blocks of the whole."""
+    return Q80Weight(torch.cat([w.q for w in ws], dim=1).contiguous(), torch.cat([w.scale for w in ws], dim=1).contiguous())
+
+
+def _vec(v, H, device) -> torch.Tensor:
+    t = torch.as_tensor(np.asarray(v, dtype=np.float32)).reshape(-1)
+    if t.numel() != H:
+        raise ValueError(f"norm weight must have {H} elements")
+    return t.to(device).contiguous()
+
+
+class _Layer:
+    def __init__(self, lw: dict, H: int, nq: int, nkv: int, hd: int, max_seq: int, max_prompt: int, theta: float,
+                 frac: float, device):
+        attn, ffn = lw["attn"], lw["ffn"]
+        q, k, v, o = (_q80(attn[n], device) for n in ("q", "k", "v", "o"))
+        if q.shape != (H, nq * hd) or k.shape != (H, nkv * hd) or v.shape != (H, nkv * hd) or o.shape != (nq * hd, H):
+            raise ValueError("attention weights do not match the head counts")
+        self.qkv = Q80Linear(_concat_n([q, k, v]), max_prompt, device)
+        self.o = Q80Linear(o, max_prompt, device)
+        gate = _q80(ffn["gate"], device) if ffn.get("gate") is not None else None
+        self.ffn_w = FfnWeights.prepare(gate, _q80(ffn["up"], device), _q80(ffn["down"], device))
+        self.ffn = FfnShardOp(H, self.ffn_w.width, max_prompt, gated=gate is not None, device=device)
+        self.ln1 = _vec(lw["input_layernorm"], H, device)
+        self.ln2 = _vec(lw["post_attention_layernorm"], H, device)
+        self.attn = AttentionOp(nq, nkv, hd, max_seq, rope_theta=theta, rope_fraction=frac, device=device)
+
+
+class Generator:
+    """Greedy generation over token ids (the tokenizer stays with the caller)."""
+
+    def __init__(self, layers: list[dict], embedding, final_norm=None, *, n_heads: int, n_kv_heads: int,
+                 head_dim: int, rope_theta: float = 10000.0, rope_fraction: float = 1.0, eps: float = 1e-6,
+                 lm_head=None, max_seq: int = 4096, max_prompt: int = 64, device=None):
+        D.require_cuda()
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        # the reference keeps embedding, lm_head and final norm as f16 (generator.py:31-34)
+        emb = torch.as_tensor(np.asarray(embedding)) if not isinstance(embedding, torch.Tensor) else embedding
+        self.embedding = emb.to(dev, torch.float16).contiguous()
+        self.V, self.H = self.embedding.shape
+        table = self.embedding if lm_head is None else torch.as_tensor(np.asarray(lm_head)).to(dev, torch.float16)
+        fn = None
+        if final_norm is not None:
+            fn = torch.as_tensor(np.asarray(final_norm, dtype=np.float32)).half().float()
+        self.lm_head = LmHeadOp(table.contiguous(), fn, eps)
+        self.eps = float(eps)
+        self.nq, self.nkv, self.hd = n_heads, n_kv_heads, head_dim
+        self.max_seq, self.max_prompt = int(max_seq), int(max_prompt)
+        self.layers = [_Layer(lw, self.H, n_heads, n_kv_heads, head_dim, self.max_seq, self.max_prompt, rope_theta,
+                              rope_fraction, dev) for lw in layers]
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.length = 0
+        self._desc = self._native_desc()
+        self.tokens = torch.zeros(self.max_seq + 1, dtype=torch.int32, device=dev)
+
+    def _native_desc(self) -> DecoderDesc:
+        """The descriptor of pyre_decoder_step: pointers into this object's buffers (which it
+        keeps alive), built once."""
+        check_struct_layout()
+        dev, H = self.device, self.H
+        codes = {c for L in self.layers for c in (L.qkv.w.scale_code, L.o.w.scale_code, L.ffn_w.gateup.scale_code)}
+        if len(codes) != 1:
+            raise ValueError("every matrix needs the same scale dtype")
+        widths = {L.ffn_w.width for L in self.layers}
+        if len(widths) != 1:
+            raise ValueError("every layer needs the same FFN width")
+        nqkv = (self.nq + 2 * self.nkv) * self.hd
+        self._buf = {n: torch.zeros(k, dtype=torch.float32, device=dev)
+                     for n, k in (("x", H), ("xn", H), ("hn", H), ("qkv", nqkv), ("attn", self.nq * self.hd),
+                                  ("ao", H), ("f", H))}
+        self._key = torch.zeros(1, dtype=torch.int64, device=dev)
+        arr = (DecoderLayerDesc * len(self.layers))()
+        for i, L in enumerate(self.layers):
+            arr[i] = DecoderLayerDesc(
+                L.qkv.w.data.data_ptr(), L.qkv.workspace.data_ptr(), L.qkv.workspace.numel(),
+                L.o.w.data.data_ptr(), L.o.workspace.data_ptr(), L.o.workspace.numel(),
+                L.ffn_w.gateup.data.data_ptr(), L.ffn_w.down.data.data_ptr(), int(L.ffn_w.gated),
+                L.ffn.workspace.data_ptr(), L.ffn.workspace.numel(), L.ln1.data_ptr(), L.ln2.data_ptr(),
+                L.attn.cache.k.data_ptr(), L.attn.cache.v.data_ptr(), L.attn.rope.data_ptr(),
+                L.attn.dec_ws.data_ptr(), L.attn.dec_ws.numel())
+        self._layer_arr = arr
+        lm = self.lm_head
+        d = DecoderDesc(len(self.layers), H, self.nq, self.nkv, self.hd, widths.pop(), self.V, self.max_seq,
+                        codes.pop(), self.eps, float(self.layers[0].attn.frac),
+                        ctypes.cast(arr, ctypes.POINTER(DecoderLayerDesc)), self.embedding.data_ptr(),
+                        lm.table.data_ptr(), lm.norm.data_ptr() if lm.norm is not None else None,
+                        lm.workspace.data_ptr(), lm.workspace.numel(),
+                        *(self._buf[n].data_ptr() for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f")),
+                        self.status.data_ptr(), self._key.data_ptr())
+        return d
+
+    # ---- one pass of the decoder over T new tokens ------------------------------------------
+    def _forward(self, ids: torch.Tensor, prefill: bool, stream=None) -> torch.Tensor:
+        """ids: int32 [T] on the device (the prompt, or one decode token). Returns the last
+        hidden state, f32 [1, H]."""
+        T, H = ids.numel(), self.H
+        s = D.stream_ptr(stream)
+        x = torch.empty((T, H), dtype=torch.float32, device=self.device)
+        xn = torch.empty_like(x)
+        hn = torch.empty_like(x)
+        first = self.layers[0]
+        N.call("pyre_embed_rms_norm", D.ptr(ids), T, D.ptr(self.embedding), self.V, H, D.ptr(first.ln1), self.eps,
+               D.ptr(x), D.ptr(xn), D.ptr(self.status), s)
+        nq_w, nkv_w = self.nq * self.hd, self.nkv * self.hd
+        for i, L in enumerate(self.layers):
+            qkv = L.qkv(xn, stream=stream)
+            q, k, v = qkv[:, :nq_w], qkv[:, nq_w:nq_w + nkv_w], qkv[:, nq_w + nkv_w:]
+            a = L.attn.prefill(q, k, v, stream=stream) if prefill else L.attn.decode(q, k, v, stream=stream)
+            ao = L.o(a, stream=stream)
+            N.call("pyre_add_rms_norm", D.ptr(x), D.ptr(ao), T, H, D.ptr(L.ln2), self.eps, D.ptr(x), D.ptr(hn), s)
+            f = L.ffn.run(hn, L.ffn_w, stream=stream)
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            N.call("pyre_add_rms_norm", D.ptr(x), D.ptr(f), T, H, D.ptr(nxt.ln1) if nxt else None, self.eps, D.ptr(x),
+                   D.ptr(xn) if nxt else None, s)
+        return x[T - 1:T]
+
+    def reset(self) -> None:
+        for L in self.layers:
+            L.attn.reset()
+        self.length = 0
+
+    def prefill(self, ids, want_logits: bool = False, stream=None, stepwise: bool = False):
+        """Run the prompt (a fresh sequence) and return the first greedy token, int64 [1, 1] on
+        the device (and the logits f32 [1, V] of the last prompt position with want_logits).
+
+        By default the prompt is one pass with T = prompt length: for T > 4 the projections and
+        the FFN run on the tensor-core GEMM (f16 operands: activations rounded to f16, weights
+        dequantized to f16). ``stepwise`` instead feeds the prompt one token at a time through
+        the decode step, whose projections and FFN multiply f32 activations with the exact
+        dequantized weights (slower; the reference computes every prompt position in f32)."""
+        ids = np.asarray(ids).reshape(-1)
+        if ids.size < 1 or ids.size > self.max_prompt:
+            raise ValueError(f"prompt length {ids.size} outside [1, {self.max_prompt}]")
+        if ids.min() < 0 or ids.max() >= self.V:
+            raise ValueError(f"token ids must be in [0, {self.V})")
+        self.reset()
+        dev_ids = torch.as_tensor(ids.astype(np.int32)).to(self.device)
+        n = 1 if stepwise else int(ids.size)
+        h = self._forward(dev_ids[:n], True, stream)
+        self.length = n
+        if n == ids.size:
+            return self.lm_head(h, want_logits=want_logits, stream=stream)
+        scratch = torch.empty(1, dtype=torch.int32, device=self.device)
+        for i in range(1, int(ids.size) - 1):
+            self.step_into(dev_ids[i:i + 1], scratch, stream=stream)
+        logits = torch.empty((1, self.V), dtype=torch.float32, device=self.device) if want_logits else None
+        self.step_into(dev_ids[-1:], scratch, logits[0] if want_logits else None, stream=stream)
+        tok = scratch.to(torch.int64).view(1, 1)
+        return (tok, logits) if want_logits else tok
+
+    def step(self, token: torch.Tensor, want_logits: bool = False, stream=None):
+        """One decode step on the previous greedy token (int [1, 1] on the device), op by op
+        from Python (:meth:`step_into` is the same step in one native call)."""
+        if self.length == 0:
+            raise ValueError("step() needs a prefill() first")
+        if self.length + 1 > self.max_seq:
+            raise ValueError("sequence longer than max_seq")
+        ids = token.reshape(-1)[:1].to(torch.int32)
+        h = self._forward(ids, False, stream)
+        self.length += 1
+        return self.lm_head(h, want_logits=want_logits, stream=stream)
+
+    def step_into(self, token_in: torch.Tensor, token_out: torch.Tensor, logits: torch.Tensor | None = None,
+                  stream=None) -> None:
+        """One decode step through ``pyre_decoder_step``: reads int32 ``token_in`` [1] and writes
+        the greedy token to int32 ``token_out`` [1] (both on the device; may be views of one
+        buffer), and the logits f32 [V] when given. Nothing is synchronised."""
+        if self.length == 0:
+            raise ValueError("step_into() needs a prefill() first")
+        if self.length + 1 > self.max_seq:
+            raise ValueError("sequence longer than max_seq")
+        for t in (token_in, token_out):
+            if t.dtype != torch.int32 or not t.is_cuda:
+                raise ValueError("tokens must be int32 on the device")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() != self.V):
+            raise ValueError(f"logits must be f32 with {self.V} elements")
+        N.call("pyre_decoder_step", ctypes.byref(self._desc), D.ptr(token_in), self.length, 0, 0, D.ptr(token_out),
+               D.ptr(logits), D.stream_ptr(stream))
+        self.length += 1
+        for L in self.layers:
+            L.attn.cache.length = self.length
+
+    def check_status(self) -> None:
+        torch.cuda.synchronize(self.device)
+        if int(self.status.item()) != 0:
+            raise RuntimeError(f"embedding gather saw a token id outside [0, {self.V})")
+        for L in self.layers:
+            st = L.ffn.status()
+            if st != 0:
+                raise RuntimeError(f"FFN kernel status {st}")
+
+    def generate_ids(self, prompt_ids, max_tokens: int, want_logits: bool = False, native: bool = True,
+                     stepwise_prefill: bool = False):
+        """Greedy ids after the prompt (``Generator.generate`` at temperature 0 without the
+        tokenizer and EOS stop), as a list of ints; with want_logits also the f32 logits of
+        every step, [max_tokens, V] on the device. native: decode steps through
+        pyre_decoder_step (else op by op from Python); stepwise_prefill: see :meth:`prefill`."""
+        if max_tokens < 1 or max_tokens > self.max_seq + 1:
+            raise ValueError("max_tokens out of range")
+        out = self.prefill(prompt_ids, want_logits=want_logits, stepwise=stepwise_prefill)
+        tok, lg0 = (out if want_logits else (out, None))
+        logits = torch.empty((max_tokens, self.V), dtype=torch.float32, device=self.device) if want_logits else None
+        if want_logits:
+            logits[0].copy_(lg0[0])
+        toks = self.tokens
+        toks[0].copy_(tok.reshape(-1)[0])
+        for i in range(1, max_tokens):
+            if native:
+                self.step_into(toks[i - 1:i], toks[i:i + 1], logits[i] if want_logits else None)
+            else:
+                out = self.step(toks[i - 1:i], want_logits=want_logits)
+                t, lg = (out if want_logits else (out, None))
+                toks[i].copy_(t.reshape(-1)[0])
+                if want_logits:
+                    logits[i].copy_(lg[0])
+        self.check_status()
+        ids = toks[:max_tokens].cpu().tolist()
+        return (ids, logits) if want_logits else ids
