@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
     ap.add_argument("--no-attention", action="store_true", help="skip the attention and lm_head measurements")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder (7B shape) measurement")
     return ap.parse_args()
 
 
@@ -298,6 +299,74 @@ class ClockSampler:
 # GPU leg
 # ---------------------------------------------------------------------------------------
 
+def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
+    """Whole Mistral-7B-shaped decoder on one GPU: hidden 4096, 32 layers, 32 query / 8 KV heads,
+    head_dim 128, gated-SiLU 14336, vocab 32768 (untied f16 lm_head), RoPE theta 1e6; Q8_0
+    N(0, 0.02) weights (f16 scales) made on the device from seed 3, a uniform-random prompt of
+    `prompt` ids (seed 3), then `decode` greedy tokens at batch 1. Prefill: one pass of the
+    prompt (tensor-core GEMMs, causal attention); decode: pyre_decoder_step per token (no host
+    synchronisation between tokens). Both timed with CUDA events on the current stream."""
+    import numpy as np
+    import torch
+    from pyre_b200.generator import Generator
+    from pyre_b200.quantizer import Q80Weight
+    H, L, nq, nkv, hd, I, V = 4096, 32, 32, 8, 128, 14336, 32768
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def w(k, n):
+        return Q80Weight.from_float((torch.randn((k, n), generator=g, device=dev) * 0.02).to(torch.bfloat16).float(),
+                                    torch.float16)
+
+    ones = torch.ones(H, device=dev)
+    layers = [{"input_layernorm": ones, "post_attention_layernorm": ones,
+               "attn": {"q": w(H, nq * hd), "k": w(H, nkv * hd), "v": w(H, nkv * hd), "o": w(nq * hd, H)},
+               "ffn": {"gate": w(H, I), "up": w(H, I), "down": w(I, H)}} for _ in range(L)]
+    emb = (torch.randn((V, H), generator=g, device=dev) * 0.02).half()
+    head = (torch.randn((V, H), generator=g, device=dev) * 0.02).half()
+    gen = Generator(layers, emb, ones, n_heads=nq, n_kv_heads=nkv, head_dim=hd, rope_theta=1e6, lm_head=head,
+                    max_seq=prompt + decode + 1, max_prompt=prompt, device=dev)
+    del layers
+    ids = np.random.default_rng(3).integers(0, V, prompt)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    toks = torch.zeros(decode + 1, dtype=torch.int32, device=dev)
+    # warm-up: a prefill and a few decode steps
+    gen.prefill(ids)
+    for i in range(4):
+        gen.step_into(toks[i:i + 1], toks[i + 1:i + 2])
+    torch.cuda.synchronize()
+    pf = []
+    for _ in range(3):
+        e0.record()
+        tok = gen.prefill(ids)
+        e1.record()
+        torch.cuda.synchronize()
+        pf.append(e0.elapsed_time(e1))
+    toks[0] = tok.reshape(-1)[0]
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(decode - 1):
+        gen.step_into(toks[i:i + 1], toks[i + 1:i + 2])
+    e1.record()
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1) / (decode - 1)
+    gen.check_status()
+    pf_ms = min(pf)
+    layer_bytes = (H * (nq + 2 * nkv) * hd + nq * hd * H + 3 * H * I) * Q8_BYTES_PER_PARAM
+    step_bytes = L * layer_bytes + V * H * 2
+    flops = 2 * prompt * L * (H * (nq + 2 * nkv) * hd + nq * hd * H + 3 * H * I)
+    del gen
+    torch.cuda.empty_cache()
+    return {"shape": "Mistral-7B-shaped decoder: hidden 4096, 32 layers, 32/8 heads, hd 128, FFN 14336, vocab 32768",
+            "prompt_tokens": prompt, "decode_tokens": decode, "batch": 1,
+            "prefill_ms": round(pf_ms, 3), "prefill_tok_s": round(prompt / (pf_ms * 1e-3), 1),
+            "prefill_linear_tflops": round(flops / (pf_ms * 1e-3) / 1e12, 1),
+            "decode_ms_per_token": round(dec_ms, 4), "decode_tok_s": round(1e3 / dec_ms, 1),
+            "decode_weight_bytes_per_token": int(step_bytes),
+            "decode_frac_of_hbm": round(step_bytes / (dec_ms * 1e-3) / 1e9 / hbm, 4),
+            "launches_per_decode_token": 2 + 6 * L,
+            "how": "Generator.prefill (one pass) and Generator.step_into (pyre_decoder_step) per token; CUDA events"}
+
+
 def make_sets(rank, bounds, n_sets, device):
     """Per weight set (one per layer): full matrices from a seeded CUDA generator (identical
     on every rank), Q8_0 on the GPU, then this rank's shard."""
@@ -471,6 +540,7 @@ def run_ours(args):
     attn = None if args.no_attention else attention_bench(dev, stream, hbm, tf_burst)
     lmh = None if args.no_attention else lmhead_bench(dev, stream, hbm)
     barrier()
+    decoder = None if (args.no_decoder or world > 1) else decoder_bench(dev, hbm)
 
     # max over ranks
     vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(k_ms), prefill["ms_per_step"] if prefill else 0.0],
@@ -523,6 +593,8 @@ def run_ours(args):
             res["attention"] = attn
         if lmh:
             res["lm_head"] = lmh
+        if decoder:
+            res["decoder_7b"] = decoder
         if not args.no_cpu:
             _, cpu = cpu_reference_leg(T, args.cpu_seconds)
             res["cpu_baseline"] = cpu

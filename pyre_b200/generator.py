@@ -84,8 +84,12 @@ def _concat_n(ws: list[Q80Weight]) -> Q80Weight:
     return Q80Weight(torch.cat([w.q for w in ws], dim=1).contiguous(), torch.cat([w.scale for w in ws], dim=1).contiguous())
 
 
+def _f32(v) -> torch.Tensor:
+    return v.detach().float() if isinstance(v, torch.Tensor) else torch.as_tensor(np.asarray(v, dtype=np.float32))
+
+
 def _vec(v, H, device) -> torch.Tensor:
-    t = torch.as_tensor(np.asarray(v, dtype=np.float32)).reshape(-1)
+    t = _f32(v).reshape(-1)
     if t.numel() != H:
         raise ValueError(f"norm weight must have {H} elements")
     return t.to(device).contiguous()
@@ -121,10 +125,11 @@ class Generator:
         emb = torch.as_tensor(np.asarray(embedding)) if not isinstance(embedding, torch.Tensor) else embedding
         self.embedding = emb.to(dev, torch.float16).contiguous()
         self.V, self.H = self.embedding.shape
-        table = self.embedding if lm_head is None else torch.as_tensor(np.asarray(lm_head)).to(dev, torch.float16)
+        table = self.embedding if lm_head is None else (
+            lm_head if isinstance(lm_head, torch.Tensor) else torch.as_tensor(np.asarray(lm_head))).to(dev, torch.float16)
         fn = None
         if final_norm is not None:
-            fn = torch.as_tensor(np.asarray(final_norm, dtype=np.float32)).half().float()
+            fn = _f32(final_norm).half().float()
         self.lm_head = LmHeadOp(table.contiguous(), fn, eps)
         self.eps = float(eps)
         self.nq, self.nkv, self.hd = n_heads, n_kv_heads, head_dim
