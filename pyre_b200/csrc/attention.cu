@@ -89,6 +89,64 @@ __global__ void add_rms_norm_kernel(const float* x, const float* __restrict__ de
     norm[row * H + i] = static_cast<float>(static_cast<double>(hr[i]) * rstd * static_cast<double>(w[i]));
 }
 
+// add_rms_norm_kernel for H % 4 == 0 and H <= 4 * kNormVec * blockDim: every x and delta
+// value is loaded (16 bytes at a time) into registers before anything is stored, so the loads
+// of a row overlap instead of waiting one after another behind stores that may alias them.
+constexpr int kNormVec = 4;
+__global__ void __launch_bounds__(1024) add_rms_norm_vec_kernel(const float* x, const float* __restrict__ delta,
+                                                                float* h, const float* __restrict__ w,
+                                                                float* __restrict__ norm, int H, double eps) {
+  const int64_t row = blockIdx.x;
+  const int n4 = H >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * H);
+  const float4* dr = reinterpret_cast<const float4*>(delta + row * H);
+  float4 v[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      const float4 a = xr[i], b = __ldg(dr + i);
+      v[j] = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+    }
+  }
+  double sq = 0.0;
+  float4* hr = reinterpret_cast<float4*>(h + row * H);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      hr[i] = v[j];
+      sq += static_cast<double>(v[j].x) * v[j].x + static_cast<double>(v[j].y) * v[j].y +
+            static_cast<double>(v[j].z) * v[j].z + static_cast<double>(v[j].w) * v[j].w;
+    }
+  }
+  if (norm == nullptr) return;
+  __shared__ double red[32];
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const double rstd = 1.0 / sqrt(red[0] / H + eps);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4* nr = reinterpret_cast<float4*>(norm + row * H);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      const float4 g = __ldg(wr + i);
+      nr[i] = make_float4(static_cast<float>(static_cast<double>(v[j].x) * rstd * static_cast<double>(g.x)),
+                          static_cast<float>(static_cast<double>(v[j].y) * rstd * static_cast<double>(g.y)),
+                          static_cast<float>(static_cast<double>(v[j].z) * rstd * static_cast<double>(g.z)),
+                          static_cast<float>(static_cast<double>(v[j].w) * rstd * static_cast<double>(g.w)));
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ out, int C) {
   const int64_t row = blockIdx.x;
@@ -1007,7 +1065,17 @@ extern "C" int pyre_add_rms_norm(const float* x, const float* delta, int rows, i
   PYRE_CHECK_ARG((norm == nullptr) == (w == nullptr), "pyre_add_rms_norm: norm and w go together");
   PYRE_CHECK_ARG(rows >= 0 && H >= 1, "pyre_add_rms_norm: bad sizes");
   if (rows == 0) return PYRE_OK;
-  add_rms_norm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, h, w, norm, H, eps);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto a16 = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const int n4 = H / 4;
+  if (H % 4 == 0 && n4 <= 1024 * kNormVec && a16(x) && a16(delta) && a16(h) && a16(w) && a16(norm)) {
+    int threads = (n4 + kNormVec - 1) / kNormVec;
+    threads = std::min(1024, std::max(32, (threads + 31) / 32 * 32));
+    add_rms_norm_vec_kernel<<<rows, threads, 0, s>>>(x, delta, h, w, norm, H, eps);
+    PYRE_LAUNCH_CHECK("add_rms_norm_vec_kernel");
+    return PYRE_OK;
+  }
+  add_rms_norm_kernel<<<rows, 256, 0, s>>>(x, delta, h, w, norm, H, eps);
   PYRE_LAUNCH_CHECK("add_rms_norm_kernel");
   return PYRE_OK;
 }

@@ -236,6 +236,69 @@ __global__ void embed_rms_norm_kernel(const int* __restrict__ ids, const __half*
     norm[t * H + i] = static_cast<float>(static_cast<double>(x[t * H + i]) * rstd * static_cast<double>(w[i]));
 }
 
+// embed_rms_norm_kernel for H % 4 == 0 and H <= 4 * kEmbVec * blockDim: each thread loads its
+// groups of 4 table entries (8 bytes) into registers up front.
+constexpr int kEmbVec = 4;
+__global__ void __launch_bounds__(1024) embed_rms_norm_vec_kernel(const int* __restrict__ ids,
+                                                                  const __half* __restrict__ table, int V, int H,
+                                                                  const float* __restrict__ w, double eps,
+                                                                  float* __restrict__ x, float* __restrict__ norm,
+                                                                  int* status) {
+  const int64_t t = blockIdx.x;
+  const int id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && status != nullptr) atomicExch(status, PYRE_EINVAL);
+  const uint2* row = reinterpret_cast<const uint2*>(table + static_cast<int64_t>(ok ? id : 0) * H);
+  const int n4 = H >> 2;
+  float4 v[kEmbVec];
+#pragma unroll
+  for (int j = 0; j < kEmbVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      const uint2 u = __ldg(row + i);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[j] = ok ? make_float4(a.x, a.y, b.x, b.y) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  double sq = 0.0;
+  float4* xr = reinterpret_cast<float4*>(x + t * H);
+#pragma unroll
+  for (int j = 0; j < kEmbVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      xr[i] = v[j];
+      sq += static_cast<double>(v[j].x) * v[j].x + static_cast<double>(v[j].y) * v[j].y +
+            static_cast<double>(v[j].z) * v[j].z + static_cast<double>(v[j].w) * v[j].w;
+    }
+  }
+  if (norm == nullptr) return;
+  __shared__ double red[32];
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double r = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (threadIdx.x == 0) red[0] = r;
+  }
+  __syncthreads();
+  const double rstd = 1.0 / sqrt(red[0] / H + eps);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4* nr = reinterpret_cast<float4*>(norm + t * H);
+#pragma unroll
+  for (int j = 0; j < kEmbVec; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      const float4 g = __ldg(wr + i);
+      nr[i] = make_float4(static_cast<float>(static_cast<double>(v[j].x) * rstd * static_cast<double>(g.x)),
+                          static_cast<float>(static_cast<double>(v[j].y) * rstd * static_cast<double>(g.y)),
+                          static_cast<float>(static_cast<double>(v[j].z) * rstd * static_cast<double>(g.z)),
+                          static_cast<float>(static_cast<double>(v[j].w) * rstd * static_cast<double>(g.w)));
+    }
+  }
+}
+
 }  // namespace lmh
 }  // namespace pyre
 
@@ -306,8 +369,19 @@ extern "C" int pyre_embed_rms_norm(const int* ids, int T, const void* table, int
   PYRE_CHECK_ARG((norm == nullptr) == (w == nullptr), "pyre_embed_rms_norm: norm and w go together");
   PYRE_CHECK_ARG(T >= 0 && V >= 1 && H >= 1, "pyre_embed_rms_norm: bad sizes");
   if (T == 0) return PYRE_OK;
-  lmh::embed_rms_norm_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, static_cast<const __half*>(table), V, H, w, eps, x, norm, status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto a16 = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const int n4 = H / 4;
+  if (H % 4 == 0 && n4 <= 1024 * lmh::kEmbVec && reinterpret_cast<uintptr_t>(table) % 8 == 0 && a16(w) && a16(x) &&
+      a16(norm)) {
+    int threads = (n4 + lmh::kEmbVec - 1) / lmh::kEmbVec;
+    threads = threads < 32 ? 32 : (threads + 31) / 32 * 32;
+    lmh::embed_rms_norm_vec_kernel<<<T, threads, 0, s>>>(ids, static_cast<const __half*>(table), V, H, w, eps, x,
+                                                          norm, status);
+    PYRE_LAUNCH_CHECK("embed_rms_norm_vec_kernel");
+    return PYRE_OK;
+  }
+  lmh::embed_rms_norm_kernel<<<T, 256, 0, s>>>(ids, static_cast<const __half*>(table), V, H, w, eps, x, norm, status);
   PYRE_LAUNCH_CHECK("embed_rms_norm_kernel");
   return PYRE_OK;
 }
