@@ -304,8 +304,8 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
     head_dim 128, gated-SiLU 14336, vocab 32768 (untied f16 lm_head), RoPE theta 1e6; Q8_0
     N(0, 0.02) weights (f16 scales) made on the device from seed 3, a uniform-random prompt of
     `prompt` ids (seed 3), then `decode` greedy tokens at batch 1. Prefill: one pass of the
-    prompt (tensor-core GEMMs, causal attention); decode: pyre_decoder_step per token (no host
-    synchronisation between tokens). Both timed with CUDA events on the current stream."""
+    prompt (tensor-core GEMMs, causal attention); decode: pyre_decoder_step replayed from CUDA
+    graphs (no host synchronisation between tokens). Timed with CUDA events."""
     import numpy as np
     import torch
     from pyre_b200.generator import Generator
@@ -348,7 +348,20 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
         gen.step_into(toks[i:i + 1], toks[i + 1:i + 2])
     e1.record()
     torch.cuda.synchronize()
+    call_ms = e0.elapsed_time(e1) / (decode - 1)
+    # the same steps replayed from captured CUDA graphs (16 steps per replay; the first pass
+    # captures and is not timed)
+    tok = gen.prefill(ids)
+    gen.decode_graphed(tok, decode - 1)
+    torch.cuda.synchronize()
+    tok = gen.prefill(ids)
+    torch.cuda.synchronize()
+    e0.record()
+    hist = gen.decode_graphed(tok, decode - 1)
+    e1.record()
+    torch.cuda.synchronize()
     dec_ms = e0.elapsed_time(e1) / (decode - 1)
+    same = bool(torch.equal(hist[prompt:prompt + decode], toks[:decode]))
     gen.check_status()
     pf_ms = min(pf)
     layer_bytes = (H * (nq + 2 * nkv) * hd + nq * hd * H + 3 * H * I) * Q8_BYTES_PER_PARAM
@@ -361,10 +374,14 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
             "prefill_ms": round(pf_ms, 3), "prefill_tok_s": round(prompt / (pf_ms * 1e-3), 1),
             "prefill_linear_tflops": round(flops / (pf_ms * 1e-3) / 1e12, 1),
             "decode_ms_per_token": round(dec_ms, 4), "decode_tok_s": round(1e3 / dec_ms, 1),
+            "decode_ms_per_token_one_call_per_token": round(call_ms, 4),
+            "graphed_tokens_equal_per_call_tokens": same,
             "decode_weight_bytes_per_token": int(step_bytes),
             "decode_frac_of_hbm": round(step_bytes / (dec_ms * 1e-3) / 1e9 / hbm, 4),
-            "launches_per_decode_token": 2 + 6 * L,
-            "how": "Generator.prefill (one pass) and Generator.step_into (pyre_decoder_step) per token; CUDA events"}
+            "launches_per_decode_token": 3 + 6 * L,
+            "how": "Generator.prefill (one pass); decode: Generator.decode_graphed (pyre_decoder_step with the "
+                   "position on the device, 16 tokens per CUDA-graph replay), and one pyre_decoder_step call per "
+                   "token for comparison; CUDA events"}
 
 
 def make_sets(rank, bounds, n_sets, device):

@@ -332,12 +332,27 @@ typedef struct pyre_decoder_desc {
   float *x, *xn, *hn, *qkv, *attn, *ao, *f; /* scratch: [H] x3, [(nq + 2 nkv) hd], [nq hd], [H] x2 */
   int* status;         /* embedding status word */
   long long* key;      /* [1] */
+  int* pos_dev;        /* NULL, or int32 [1] on the device: the step's position is read there
+                        * (the pos argument only plans the attention grid and must not exceed
+                        * it), and the step ends with history[*pos_dev + 1] = token_out and
+                        * *pos_dev += 1, so the step can be captured once in a CUDA graph and
+                        * replayed for positions pos, pos + 1, ... */
+  int* history;        /* with pos_dev: int32 [max_t + 1], token at each position */
 } pyre_decoder_desc;
 
 /* One decode step: token_in (int32 [1], device) at position pos (= tokens already in the
  * caches), positions [mask_lo, mask_hi) masked (the reference's padded prefill; 0, 0: none).
  * Writes the greedy token to token_out (int32 [1], device) and, when logits is not NULL, the
  * logits f32 [V]. */
+/* The fused attention decode step of pyre_attn_decode_step with the position in device memory
+ * (int32 *pos_dev, read by the kernel): valid for every position p with plan_pos <= p < max_t,
+ * the grid being planned for plan_pos. A position outside that range makes the kernel do
+ * nothing and report PYRE_EINVAL through pyre_attn_status. For steps captured in CUDA graphs. */
+PYRE_API int pyre_attn_decode_step_dev(const float* q, const float* k, const float* v, const int* pos_dev,
+                                       int plan_pos, const float* rope_table, double rope_fraction, int nq, int nkv,
+                                       int hd, uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo,
+                                       int mask_hi, float* out, void* workspace, int64_t ws_bytes, void* stream);
+
 /* sizeof(pyre_decoder_layer) and sizeof(pyre_decoder_desc), for bindings that lay the
  * structs out themselves (ctypes, cgo) to check their layout against. */
 PYRE_API int pyre_decoder_struct_sizes(int64_t* layer_bytes, int64_t* desc_bytes);

@@ -362,6 +362,9 @@ constexpr int kDecMaxGroups = 8;       // X, clusters per kv head
 constexpr int kDecMinChunk = 128;      // positions per CTA at least (one batch per warp)
 constexpr int kDecGroupChunk = 2048;   // positions per cluster before another cluster is added
 
+// Status word of the attention kernels (read and cleared by pyre_attn_status).
+__device__ int g_attn_status;
+
 struct DecodeParams {
   const __half* q;       // [nq, hd] rotated, clipped (attention alone)
   const __half* kc;      // [nkv, max_t, hd]
@@ -378,6 +381,10 @@ struct DecodeParams {
   unsigned* count;       // [nkv] arrival counters, zero between launches
   int nq, nkv, t, max_t, mask_lo, mask_hi;
   float scale2;          // log2(e) / sqrt(hd): exponentials are taken base 2
+  const int* pos_dev;    // fused step with the position in device memory (a step captured in
+                         // a CUDA graph): t = *pos_dev + 1, rope row *pos_dev of rope_base;
+                         // t and rope above are then only the host's plan of the grid
+  const float2* rope_base;
 };
 
 // Shared memory: the static part below, then (dynamic) the warps' rescaled partials
@@ -533,15 +540,31 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
-  if (C > 1) cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on below)
   const int split = blockIdx.x, S = gridDim.x, g = blockIdx.y;
+  int t = p.t;
+  const float2* rope = p.rope;
+  (void)rope;
+  if constexpr (FUSED) {
+    if (p.pos_dev != nullptr) {
+      // every CTA reads the same position, so all of them take the same branch, before any
+      // cluster barrier, counter or cache write
+      const int pos = *p.pos_dev;
+      if (pos < 0 || pos >= p.max_t || pos + 1 < S) {
+        if (threadIdx.x == 0 && split == 0 && g == 0) atomicExch(&g_attn_status, PYRE_EINVAL);
+        return;
+      }
+      t = pos + 1;
+      rope = p.half ? p.rope_base + static_cast<int64_t>(pos) * p.half : nullptr;
+    }
+  }
+  if (C > 1) cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on below)
   const int X = S / C, grp = split / C;
   const int rep = p.nq / p.nkv;
   const int E = rep * HD;
   float* wo = reinterpret_cast<float*>(dec_dyn);                 // [kDecWarps][rep][WP]
   float* co = wo + kDecWarps * rep * WP;                         // [kDecCluster][rep][HD]
-  const int c0 = static_cast<int>(static_cast<int64_t>(p.t) * split / S);
-  const int c1 = static_cast<int>(static_cast<int64_t>(p.t) * (split + 1) / S);
+  const int c0 = static_cast<int>(static_cast<int64_t>(t) * split / S);
+  const int c1 = static_cast<int>(static_cast<int64_t>(t) * (split + 1) / S);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, lg = lane >> 2, lc = lane & 3;
 
   uint4 qv[KQ];
@@ -549,17 +572,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
     // RoPE + clip of this kv head's query heads into shared memory; the last split appends
     // the token's rotated k and clipped v at row t - 1 before any of its warps reads it
     __shared__ __align__(16) __half qs[kDecMaxRep * HD];
-    const int pos = p.t - 1;
+    const int pos = t - 1;
     for (int e = threadIdx.x; e < E; e += kDecThreads) {
       const int r = e / HD, i = e - r * HD;
       const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
-      const float2 cs = p.half ? __ldg(p.rope + jj) : make_float2(0.f, 0.f);
+      const float2 cs = p.half ? __ldg(rope + jj) : make_float2(0.f, 0.f);
       qs[e] = __float2half_rn(rope_clip(p.qf + (static_cast<int64_t>(g) * rep + r) * HD, i, p.half, cs.x, cs.y));
     }
     if (split == S - 1) {
       for (int i = threadIdx.x; i < HD; i += kDecThreads) {
         const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
-        const float2 cs = p.half ? __ldg(p.rope + jj) : make_float2(0.f, 0.f);
+        const float2 cs = p.half ? __ldg(rope + jj) : make_float2(0.f, 0.f);
         const int64_t row = (static_cast<int64_t>(g) * p.max_t + pos) * HD;
         p.kw[row + i] = __float2half_rn(rope_clip(p.kf + static_cast<int64_t>(g) * HD, i, p.half, cs.x, cs.y));
         p.vw[row + i] = __float2half_rn(fminf(fmaxf(__ldg(p.vf + static_cast<int64_t>(g) * HD + i), -1000.f), 1000.f));
@@ -785,8 +808,6 @@ struct TcLayout {
   static constexpr int kBar = kP + 2 * 2 * kRegion;
   static constexpr int kBytes = 1024 + kBar + 256;             // alignment slack, barriers
 };
-
-__device__ int g_attn_status;
 
 // Waits for the tensor-memory loads in flight; r is passed through so that no use of the
 // loaded registers is scheduled before the wait.
@@ -1288,20 +1309,25 @@ extern "C" int pyre_attn_decode(const uint16_t* q, const uint16_t* k_cache, cons
                   : launch_decode<128, false>(p, workspace, ws_bytes, st);
 }
 
-extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float* v, int start_pos,
-                                     const float* rope_table, double rope_fraction, int nq, int nkv, int hd,
-                                     uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo, int mask_hi,
-                                     float* out, void* workspace, int64_t ws_bytes, void* stream) {
-  PYRE_CHECK_ARG(q && k && v && k_cache && v_cache && out, "pyre_attn_decode_step: null pointer");
+namespace pyre {
+namespace attn {
+// The fused decode step; pos_dev null: position start_pos; else the position is read from
+// *pos_dev on the device and start_pos only plans the grid.
+int decode_step(const float* q, const float* k, const float* v, int start_pos, const int* pos_dev,
+                const float* rope_table, double rope_fraction, int nq, int nkv, int hd, uint16_t* k_cache,
+                uint16_t* v_cache, int max_t, int mask_lo, int mask_hi, float* out, void* workspace,
+                int64_t ws_bytes, void* stream, const char* f) {
+  const std::string fn(f);
+  PYRE_CHECK_ARG(q && k && v && k_cache && v_cache && out, fn + ": null pointer");
   PYRE_CHECK_ARG(start_pos >= 0 && start_pos < max_t && nkv >= 1 && nq % nkv == 0 && nq / nkv <= kDecMaxRep,
-                 "pyre_attn_decode_step: bad sizes (cache full, or more than 8 query heads per kv head)");
-  PYRE_CHECK_ARG(hd == 64 || hd == 128, "pyre_attn_decode_step: head dim must be 64 or 128");
+                 fn + ": bad sizes (cache full, or more than 8 query heads per kv head)");
+  PYRE_CHECK_ARG(hd == 64 || hd == 128, fn + ": head dim must be 64 or 128");
   PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(k_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(v_cache) % 16 == 0,
-                 "pyre_attn_decode_step: the caches must be 16-byte aligned");
+                 fn + ": the caches must be 16-byte aligned");
   const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
-  PYRE_CHECK_ARG(dims >= 0 && dims <= hd, "pyre_attn_decode_step: rope_fraction must be in [0, 1]");
+  PYRE_CHECK_ARG(dims >= 0 && dims <= hd, fn + ": rope_fraction must be in [0, 1]");
   const int half = dims >= 2 ? dims / 2 : 0;
-  PYRE_CHECK_ARG(rope_table != nullptr || half == 0, "pyre_attn_decode_step: null RoPE table");
+  PYRE_CHECK_ARG(rope_table != nullptr || half == 0, fn + ": null RoPE table");
   DecodeParams p{};
   p.kc = reinterpret_cast<const __half*>(k_cache);
   p.vc = reinterpret_cast<const __half*>(v_cache);
@@ -1311,6 +1337,8 @@ extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float
   p.kf = k;
   p.vf = v;
   p.rope = half ? reinterpret_cast<const float2*>(rope_table) + static_cast<int64_t>(start_pos) * half : nullptr;
+  p.rope_base = reinterpret_cast<const float2*>(rope_table);
+  p.pos_dev = pos_dev;
   p.half = half;
   p.out = out;
   p.nq = nq;
@@ -1322,6 +1350,25 @@ extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return hd == 64 ? launch_decode<64, true>(p, workspace, ws_bytes, st)
                   : launch_decode<128, true>(p, workspace, ws_bytes, st);
+}
+}  // namespace attn
+}  // namespace pyre
+
+extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float* v, int start_pos,
+                                     const float* rope_table, double rope_fraction, int nq, int nkv, int hd,
+                                     uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo, int mask_hi,
+                                     float* out, void* workspace, int64_t ws_bytes, void* stream) {
+  return attn::decode_step(q, k, v, start_pos, nullptr, rope_table, rope_fraction, nq, nkv, hd, k_cache, v_cache,
+                           max_t, mask_lo, mask_hi, out, workspace, ws_bytes, stream, "pyre_attn_decode_step");
+}
+
+extern "C" int pyre_attn_decode_step_dev(const float* q, const float* k, const float* v, const int* pos_dev,
+                                         int plan_pos, const float* rope_table, double rope_fraction, int nq, int nkv,
+                                         int hd, uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo,
+                                         int mask_hi, float* out, void* workspace, int64_t ws_bytes, void* stream) {
+  PYRE_CHECK_ARG(pos_dev != nullptr, "pyre_attn_decode_step_dev: null position");
+  return attn::decode_step(q, k, v, plan_pos, pos_dev, rope_table, rope_fraction, nq, nkv, hd, k_cache, v_cache,
+                           max_t, mask_lo, mask_hi, out, workspace, ws_bytes, stream, "pyre_attn_decode_step_dev");
 }
 
 namespace pyre {

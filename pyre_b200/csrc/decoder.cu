@@ -13,7 +13,20 @@
 //     add_rms_norm                  x += f, xn = rms_norm(x, ln1[next])   (add only after the last)
 //   lm_head argmax                  final RMSNorm, logits, greedy token
 // Every buffer is the caller's (device memory it allocated once); nothing is allocated here.
+// With desc->pos_dev the position is read on the device and advanced by the step itself, so
+// one captured step replays for consecutive positions.
 #include "common.cuh"
+
+namespace {
+// End of a step whose position lives on the device: record the token and advance.
+__global__ void decoder_advance_kernel(int* pos, const int* token, int* history, int max_t) {
+  const int p = *pos;
+  if (p >= 0 && p < max_t) {
+    history[p + 1] = *token;
+    *pos = p + 1;
+  }
+}
+}  // namespace
 
 extern "C" int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in, int pos, int mask_lo, int mask_hi,
                                  int* token_out, float* logits, void* stream) {
@@ -32,9 +45,13 @@ extern "C" int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in
     rc = pyre_q80_linear(d->xn, PYRE_F32, 1, H, L.qkv_w, d->scale_dtype, nqkv, d->qkv, L.qkv_ws, L.qkv_ws_bytes,
                          stream);
     if (rc) return rc;
-    rc = pyre_attn_decode_step(d->qkv, d->qkv + qw, d->qkv + qw + kw, pos, L.rope, d->rope_fraction, d->nq, d->nkv,
-                               d->hd, L.k_cache, L.v_cache, d->max_t, mask_lo, mask_hi, d->attn, L.attn_ws,
-                               L.attn_ws_bytes, stream);
+    rc = d->pos_dev == nullptr
+             ? pyre_attn_decode_step(d->qkv, d->qkv + qw, d->qkv + qw + kw, pos, L.rope, d->rope_fraction, d->nq,
+                                     d->nkv, d->hd, L.k_cache, L.v_cache, d->max_t, mask_lo, mask_hi, d->attn,
+                                     L.attn_ws, L.attn_ws_bytes, stream)
+             : pyre_attn_decode_step_dev(d->qkv, d->qkv + qw, d->qkv + qw + kw, d->pos_dev, pos, L.rope,
+                                         d->rope_fraction, d->nq, d->nkv, d->hd, L.k_cache, L.v_cache, d->max_t,
+                                         mask_lo, mask_hi, d->attn, L.attn_ws, L.attn_ws_bytes, stream);
     if (rc) return rc;
     rc = pyre_q80_linear(d->attn, PYRE_F32, 1, qw, L.o_w, d->scale_dtype, H, d->ao, L.o_ws, L.o_ws_bytes, stream);
     if (rc) return rc;
@@ -48,8 +65,13 @@ extern "C" int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in
                            last ? nullptr : d->xn, stream);
     if (rc) return rc;
   }
-  return pyre_lm_head_argmax(d->x, 1, H, d->final_norm, d->eps, d->lm_head, d->V, 0, logits, token_out, d->key,
-                             d->lm_ws, d->lm_ws_bytes, stream);
+  rc = pyre_lm_head_argmax(d->x, 1, H, d->final_norm, d->eps, d->lm_head, d->V, 0, logits, token_out, d->key,
+                           d->lm_ws, d->lm_ws_bytes, stream);
+  if (rc || d->pos_dev == nullptr) return rc;
+  PYRE_CHECK_ARG(d->history != nullptr, "pyre_decoder_step: pos_dev needs a history buffer");
+  decoder_advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(d->pos_dev, token_out, d->history, d->max_t);
+  PYRE_LAUNCH_CHECK("decoder_advance_kernel");
+  return PYRE_OK;
 }
 
 extern "C" int pyre_decoder_struct_sizes(int64_t* layer_bytes, int64_t* desc_bytes) {

@@ -59,7 +59,8 @@ class DecoderDesc(ctypes.Structure):
                 ("layers", ctypes.POINTER(DecoderLayerDesc)), ("embedding", ctypes.c_void_p),
                 ("lm_head", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("lm_ws", ctypes.c_void_p),
                 ("lm_ws_bytes", ctypes.c_int64)] + \
-               [(n, ctypes.c_void_p) for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f", "status", "key")]
+               [(n, ctypes.c_void_p) for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f", "status", "key",
+                                                "pos_dev", "history")]
 
 
 def check_struct_layout() -> None:
@@ -268,6 +269,59 @@ class Generator:
         for L in self.layers:
             L.attn.cache.length = self.length
 
+    def decode_graphed(self, first_token: torch.Tensor, n_steps: int, steps_per_graph: int = 16,
+                       bucket: int = 512) -> torch.Tensor:
+        """``n_steps`` greedy steps after a prefill as replays of captured CUDA graphs: each
+        graph holds ``steps_per_graph`` decode steps whose position is read and advanced on
+        the device (``pyre_decoder_step`` with ``pos_dev``), so a replay issues that many
+        tokens with one host call. The attention grids of a graph are planned for the first
+        position of its ``bucket``-wide position range and the graph is replayed for every
+        position in that range (captured graphs are cached on this object). first_token: the
+        prefill's greedy token. Returns the int32 device tensor of all tokens by position
+        (entries prompt length .. prompt length + n_steps)."""
+        if self.length == 0:
+            raise ValueError("decode_graphed() needs a prefill() first")
+        if self.length + n_steps > self.max_seq:
+            raise ValueError("sequence longer than max_seq")
+        dev = self.device
+        if not hasattr(self, "_gdesc"):
+            self._gpos = torch.zeros(1, dtype=torch.int32, device=dev)
+            self._gslot = torch.zeros(1, dtype=torch.int32, device=dev)
+            self._ghist = torch.zeros(self.max_seq + 1, dtype=torch.int32, device=dev)
+            self._gdesc = DecoderDesc.from_buffer_copy(self._desc)
+            self._gdesc.pos_dev = self._gpos.data_ptr()
+            self._gdesc.history = self._ghist.data_ptr()
+            self._gstream = torch.cuda.Stream(dev)
+            self._graphs = {}
+        start = self.length
+        self._gpos.fill_(start)
+        self._gslot.copy_(first_token.reshape(-1)[:1].to(torch.int32))
+        self._ghist[start:start + 1].copy_(self._gslot)
+        cur = torch.cuda.current_stream(dev)
+        self._gstream.wait_stream(cur)
+        pos, left = start, n_steps
+        while left > 0:
+            plan = pos // bucket * bucket          # every step of the graph has plan <= position
+            k = min(left, steps_per_graph, plan + bucket - pos)
+            g = self._graphs.get((plan, k))
+            if g is None:
+                # capture-time host work (grid plans, tensor maps) happens here; nothing runs
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self._gstream, capture_error_mode="thread_local"):
+                    for _ in range(k):
+                        N.call("pyre_decoder_step", ctypes.byref(self._gdesc), D.ptr(self._gslot), plan, 0, 0,
+                               D.ptr(self._gslot), None, D.stream_ptr(self._gstream))
+                self._graphs[(plan, k)] = g
+            with torch.cuda.stream(self._gstream):
+                g.replay()
+            pos += k
+            left -= k
+        cur.wait_stream(self._gstream)
+        self.length = pos
+        for L in self.layers:
+            L.attn.cache.length = pos
+        return self._ghist
+
     def check_status(self) -> None:
         torch.cuda.synchronize(self.device)
         if int(self.status.item()) != 0:
@@ -278,15 +332,23 @@ class Generator:
                 raise RuntimeError(f"FFN kernel status {st}")
 
     def generate_ids(self, prompt_ids, max_tokens: int, want_logits: bool = False, native: bool = True,
-                     stepwise_prefill: bool = False):
+                     stepwise_prefill: bool = False, graphed: bool = False):
         """Greedy ids after the prompt (``Generator.generate`` at temperature 0 without the
         tokenizer and EOS stop), as a list of ints; with want_logits also the f32 logits of
         every step, [max_tokens, V] on the device. native: decode steps through
-        pyre_decoder_step (else op by op from Python); stepwise_prefill: see :meth:`prefill`."""
+        pyre_decoder_step (else op by op from Python); stepwise_prefill: see :meth:`prefill`;
+        graphed: decode steps as CUDA-graph replays (:meth:`decode_graphed`, no logits)."""
         if max_tokens < 1 or max_tokens > self.max_seq + 1:
             raise ValueError("max_tokens out of range")
+        if graphed and want_logits:
+            raise ValueError("graphed decoding returns no logits")
         out = self.prefill(prompt_ids, want_logits=want_logits, stepwise=stepwise_prefill)
         tok, lg0 = (out if want_logits else (out, None))
+        if graphed:
+            start = self.length
+            hist = self.decode_graphed(tok, max_tokens - 1)
+            self.check_status()
+            return hist[start:start + max_tokens].cpu().tolist()
         logits = torch.empty((max_tokens, self.V), dtype=torch.float32, device=self.device) if want_logits else None
         if want_logits:
             logits[0].copy_(lg0[0])

@@ -83,18 +83,38 @@ CASES = [("greedy_golden.npz", 0.02, True, False), ("greedy_golden.npz", 0.02, F
          ("greedy_golden_std07.npz", 0.07, False, True)]
 
 
+def _generator(std):
+    import torch
+    from pyre_b200.generator import Generator
+    emb, layers, final_norm = _weights(std)
+    C = gm.CFG
+    return Generator(layers, emb, final_norm, n_heads=C["n_heads"], n_kv_heads=C["n_kv"], head_dim=C["head_dim"],
+                     rope_theta=C["theta"], eps=C["eps"], max_seq=128, max_prompt=64, device=torch.device("cuda", 0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,std,stepwise", [("greedy_golden.npz", 0.02, False), ("greedy_golden_std07.npz", 0.07, True)])
+def test_greedy_tokens_graphed_decode(name, std, stepwise):
+    """Decode steps replayed from captured CUDA graphs (position read and advanced on the
+    device), with graphs of 5 steps over 16-position buckets so that the run crosses bucket
+    boundaries and replans the attention grid: the same 32 tokens, twice in a row (the
+    second run replays the cached graphs)."""
+    g = _golden(name)
+    gen = _generator(std)
+    for _ in range(2):
+        ids = gen.generate_ids(g["prompt"], gm.N_GREEDY, stepwise_prefill=stepwise, graphed=True)
+        assert ids == g["tokens"].tolist()
+    tok = gen.prefill(g["prompt"], stepwise=stepwise)
+    hist = gen.decode_graphed(tok, gm.N_GREEDY - 1, steps_per_graph=5, bucket=16)
+    n0 = len(g["prompt"])
+    assert hist[n0:n0 + gm.N_GREEDY].cpu().tolist() == g["tokens"].tolist()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,std,native,stepwise", CASES)
 def test_greedy_tokens_match_reference(name, std, native, stepwise):
-    import torch
-    from pyre_b200.generator import Generator
-
     g = _golden(name)
-    emb, layers, final_norm = _weights(std)
-    C = gm.CFG
-    gen = Generator(layers, emb, final_norm, n_heads=C["n_heads"], n_kv_heads=C["n_kv"], head_dim=C["head_dim"],
-                    rope_theta=C["theta"], eps=C["eps"], max_seq=128, max_prompt=64,
-                    device=torch.device("cuda", 0))
+    gen = _generator(std)
     ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=native,
                                    stepwise_prefill=stepwise)
     lg = logits.cpu().numpy()
