@@ -62,6 +62,8 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
 // as rms_norm_kernel; one CTA per row. h may alias x; norm may be null (add only).
 __global__ void add_rms_norm_kernel(const float* x, const float* __restrict__ delta, float* h,
                                     const float* __restrict__ w, float* __restrict__ norm, int H, double eps) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const float* xr = x + row * H;
   const float* dr = delta + row * H;
@@ -96,6 +98,8 @@ constexpr int kNormVec = 4;
 __global__ void __launch_bounds__(1024) add_rms_norm_vec_kernel(const float* x, const float* __restrict__ delta,
                                                                 float* h, const float* __restrict__ w,
                                                                 float* __restrict__ norm, int H, double eps) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const int n4 = H >> 2;
   const float4* xr = reinterpret_cast<const float4*>(x + row * H);
@@ -541,6 +545,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   const int C = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
   const int split = blockIdx.x, S = gridDim.x, g = blockIdx.y;
+  pdl_wait();      // q, k, v (and the position) come from the previous kernels of the stream
+  pdl_trigger();
   int t = p.t;
   const float2* rope = p.rope;
   (void)rope;
@@ -1092,12 +1098,12 @@ extern "C" int pyre_add_rms_norm(const float* x, const float* delta, int rows, i
   if (H % 4 == 0 && n4 <= 1024 * kNormVec && a16(x) && a16(delta) && a16(h) && a16(w) && a16(norm)) {
     int threads = (n4 + kNormVec - 1) / kNormVec;
     threads = std::min(1024, std::max(32, (threads + 31) / 32 * 32));
-    add_rms_norm_vec_kernel<<<rows, threads, 0, s>>>(x, delta, h, w, norm, H, eps);
-    PYRE_LAUNCH_CHECK("add_rms_norm_vec_kernel");
+    PYRE_CUDA_TRY(launch_pdl(add_rms_norm_vec_kernel, dim3(static_cast<unsigned>(rows)), dim3(threads), 0, s, x,
+                             delta, h, w, norm, H, eps));
     return PYRE_OK;
   }
-  add_rms_norm_kernel<<<rows, 256, 0, s>>>(x, delta, h, w, norm, H, eps);
-  PYRE_LAUNCH_CHECK("add_rms_norm_kernel");
+  PYRE_CUDA_TRY(launch_pdl(add_rms_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s, x, delta, h, w,
+                           norm, H, eps));
   return PYRE_OK;
 }
 
@@ -1269,13 +1275,15 @@ int launch_decode(DecodeParams p, void* workspace, int64_t ws_bytes, cudaStream_
   cfg.blockDim = dim3(kDecThreads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(dec_dyn_bytes<HD>(p.nq / p.nkv));
   cfg.stream = stream;
-  cudaLaunchAttribute attr{};
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = static_cast<unsigned>(C);
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2]{};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see pdl_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, FUSED>, p));
   PYRE_LAUNCH_CHECK("attn_decode_kernel");
   return PYRE_OK;

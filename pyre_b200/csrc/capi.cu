@@ -1,4 +1,5 @@
 // Library-wide C ABI pieces: version, per-thread error text, device queries.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -36,6 +37,14 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("PYRE_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
 }
 
 int set_smem_limit(const void* kernel, int bytes) {

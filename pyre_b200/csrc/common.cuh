@@ -38,6 +38,36 @@ int set_smem_limit(const void* kernel, int bytes);
     if (_e != cudaSuccess) return ::pyre::cuda_status(_e, what);    \
   } while (0)
 
+// ---- programmatic dependent launch ----------------------------------------------------
+// A kernel launched with launch_pdl may start while the previous kernel of its stream is still
+// running. Before pdl_wait() it may only read data no earlier kernel is still writing (weights,
+// its own scratch) and write nothing another kernel reads; pdl_wait() returns once the previous
+// kernel has finished and its writes are visible (at once when launched without the
+// attribute). pdl_trigger() lets the next kernel start; every kernel here calls it only after
+// its own pdl_wait(), so at most two kernels of a stream overlap.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether launch_pdl sets the attribute: on unless the environment sets PYRE_PDL=0 (read once;
+// the kernels are the same either way, pdl_wait() then returns at once).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ---- element loads ------------------------------------------------------------------
 
 __device__ __forceinline__ float to_f32(float v) { return v; }

@@ -20,6 +20,8 @@
 namespace {
 // End of a step whose position lives on the device: record the token and advance.
 __global__ void decoder_advance_kernel(int* pos, const int* token, int* history, int max_t) {
+  pyre::pdl_wait();
+  pyre::pdl_trigger();
   const int p = *pos;
   if (p >= 0 && p < max_t) {
     history[p + 1] = *token;
@@ -69,8 +71,8 @@ extern "C" int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in
                            d->lm_ws, d->lm_ws_bytes, stream);
   if (rc || d->pos_dev == nullptr) return rc;
   PYRE_CHECK_ARG(d->history != nullptr, "pyre_decoder_step: pos_dev needs a history buffer");
-  decoder_advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(d->pos_dev, token_out, d->history, d->max_t);
-  PYRE_LAUNCH_CHECK("decoder_advance_kernel");
+  PYRE_CUDA_TRY(pyre::launch_pdl(decoder_advance_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream),
+                                 d->pos_dev, static_cast<const int*>(token_out), d->history, d->max_t));
   return PYRE_OK;
 }
 

@@ -267,10 +267,18 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
     fence_mbar_init();
   }
   __syncthreads();
-  // epoch of this call (tags the per-slab ready flags); published by the last CTA to exit
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
-  uint32_t cepoch = 0;
-  if constexpr (TP) cepoch = comm::epoch_begin(p.comm);
+  // Programmatic dependent launch: every thread but the producer's waits here until the
+  // previous kernel of the stream has finished. The producer first issues the weight copies
+  // of its first chunk (weights are constant; the chunk is this CTA's fixed first item, so
+  // the workspace is not touched), then waits before any activation load or workspace access.
+  const bool producer = warp == kConsumerWarps && lane == 0;
+  uint32_t epoch = 0, cepoch = 0;
+  if (!producer) {
+    pdl_wait();
+    // epoch of this call (tags the per-slab ready flags); published by the last CTA to exit
+    epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
+    if constexpr (TP) cepoch = comm::epoch_begin(p.comm);
+  }
 
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
@@ -279,6 +287,27 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       if constexpr (kHasB) prefetch_tmap(&p.txb);
       int s = 0;
       uint32_t ph = 0;
+      // activation loads of the stages issued before pdl_wait (at most one ring of stages)
+      bool dep = false;
+      int ndef = 0;
+      int def_s[C::kStages], def_k[C::kStages];
+      bool def_b[C::kStages];
+      auto resolve = [&]() {
+        if (dep) return;
+        pdl_wait();
+        pdl_trigger();
+        dep = true;
+        epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
+        for (int i = 0; i < ndef; ++i) {
+          uint8_t* st = stages + def_s[i] * C::kStageBytes;
+          if (def_b[i]) {
+            if constexpr (kHasB) tma_load_2d(st + LB::kXOff, &p.txb, def_k[i], 0, &full[def_s[i]]);
+          } else {
+            if constexpr (kHasA) tma_load_2d(st + LA::kXOff, &p.txa, def_k[i], 0, &full[def_s[i]]);
+          }
+        }
+        ndef = 0;
+      };
       // Failure handling: after any wait runs out (here or in another CTA, seen as
       // PYRE_ETIMEOUT in the status word) the producer issues no more copies, still tries to hand the consumers
       // their end marker, and waits (bounded) for the copies it already issued, so that no
@@ -306,12 +335,20 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
             const int u0 = chunk * kChunk;
             const int u1 = min(u0 + kChunk, p.uptA);
             for (int u = u0; u < u1; ++u) {
+              if (ndef == C::kStages) resolve();   // the ring is full of stages waiting for x
               if (!acquire()) return false;
               meta[s] = StageMeta{0, tile, chunk, u + 1 == u1};
               uint8_t* st = stages + s * C::kStageBytes;
               mbar_arrive_expect_tx(&full[s], LA::kTxBytes);
               bulk_load(st, p.wa + (static_cast<int64_t>(tile) * p.uptA + u) * LA::kWBytes, LA::kWBytes, &full[s]);
-              tma_load_2d(st + LA::kXOff, &p.txa, u * LA::kRows, 0, &full[s]);
+              if (dep) {
+                tma_load_2d(st + LA::kXOff, &p.txa, u * LA::kRows, 0, &full[s]);
+              } else {
+                def_s[ndef] = s;
+                def_k[ndef] = u * LA::kRows;
+                def_b[ndef] = false;
+                ++ndef;
+              }
               issue_done();
             }
           }
@@ -319,13 +356,24 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
           if constexpr (kHasB) {
             const int u0 = chunk * kChunk;
             const int u1 = min(u0 + kChunk, p.uptB);
+            // MODE_AB: h is this kernel's own phase-A output, read only after the wait
+            if (MODE == MODE_AB) resolve();
             for (int u = u0; u < u1; ++u) {
+              if (ndef == C::kStages) resolve();
               if (!acquire()) return false;
               meta[s] = StageMeta{1, tile, chunk, u + 1 == u1};
               uint8_t* st = stages + s * C::kStageBytes;
               mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
               bulk_load(st, p.wb + (static_cast<int64_t>(tile) * p.uptB + u) * LB::kWBytes, LB::kWBytes, &full[s]);
               const int k0 = u * LB::kRows;
+              if (!dep) {
+                def_s[ndef] = s;
+                def_k[ndef] = k0;
+                def_b[ndef] = true;
+                ++ndef;
+                issue_done();
+                continue;
+              }
               bool rdy = true;
               if constexpr (MODE == MODE_AB) {
                 // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256)
@@ -341,12 +389,20 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
         }
         return true;
       };
+      // queue items: blockIdx.x first (fixed, so it can be issued before the wait), then
+      // gridDim.x + the shared counter's values
+      bool first = true;
       while (ok) {
-        if (failed()) {
-          ok = false;
-          break;
+        int pos = static_cast<int>(blockIdx.x);
+        if (!first) {
+          resolve();
+          if (failed()) {
+            ok = false;
+            break;
+          }
+          pos = static_cast<int>(gridDim.x + atomicAdd(p.next, 1u));
         }
-        const int pos = static_cast<int>(atomicAdd(p.next, 1u));
+        first = false;
         int phase, tile, chunk;
         if constexpr (MODE == MODE_AB) {
           if (!ab_item(p, pos, phase, tile, chunk)) break;
@@ -365,6 +421,7 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
         }
         ok = issue_chunk(phase, tile, chunk);
       }
+      resolve();   // deferred activation loads, and the wait, even for a CTA with no item
       // end marker for the consumers
       if (acquire()) {
         meta[s] = StageMeta{-1, 0, 0, 0};

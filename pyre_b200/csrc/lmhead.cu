@@ -62,6 +62,8 @@ __device__ __forceinline__ void f16x8_to_f32(const uint4& u, float (&f)[8]) {
 
 template <int T>
 __global__ void __launch_bounds__(kThreads, 1) lm_head_kernel(const Params p) {
+  pdl_wait();      // h comes from the previous kernel of the stream
+  pdl_trigger();
   extern __shared__ float hs[];            // [T][H] normalised rows
   __shared__ double red[kWarps];
   __shared__ long long wkey[kWarps][kMaxT];
@@ -209,6 +211,8 @@ int grid_ctas() {
 __global__ void embed_rms_norm_kernel(const int* __restrict__ ids, const __half* __restrict__ table, int V, int H,
                                       const float* __restrict__ w, double eps, float* __restrict__ x,
                                       float* __restrict__ norm, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   const int id = ids[t];
   const bool ok = id >= 0 && id < V;
@@ -244,6 +248,8 @@ __global__ void __launch_bounds__(1024) embed_rms_norm_vec_kernel(const int* __r
                                                                   const float* __restrict__ w, double eps,
                                                                   float* __restrict__ x, float* __restrict__ norm,
                                                                   int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   const int id = ids[t];
   const bool ok = id >= 0 && id < V;
@@ -343,19 +349,19 @@ extern "C" int pyre_lm_head_argmax(const float* h, int T, int H, const float* no
   switch (T) {
     case 1:
       rc = set_smem_limit(reinterpret_cast<const void*>(lmh::lm_head_kernel<1>), 1 * lmh::kMaxH * 4);
-      if (!rc) lmh::lm_head_kernel<1><<<G, lmh::kThreads, smem, s>>>(p);
+      if (!rc) rc = cuda_status(launch_pdl(lmh::lm_head_kernel<1>, dim3(G), dim3(lmh::kThreads), smem, s, p), "lm_head_kernel");
       break;
     case 2:
       rc = set_smem_limit(reinterpret_cast<const void*>(lmh::lm_head_kernel<2>), 2 * lmh::kMaxH * 4);
-      if (!rc) lmh::lm_head_kernel<2><<<G, lmh::kThreads, smem, s>>>(p);
+      if (!rc) rc = cuda_status(launch_pdl(lmh::lm_head_kernel<2>, dim3(G), dim3(lmh::kThreads), smem, s, p), "lm_head_kernel");
       break;
     case 3:
       rc = set_smem_limit(reinterpret_cast<const void*>(lmh::lm_head_kernel<3>), 3 * lmh::kMaxH * 4);
-      if (!rc) lmh::lm_head_kernel<3><<<G, lmh::kThreads, smem, s>>>(p);
+      if (!rc) rc = cuda_status(launch_pdl(lmh::lm_head_kernel<3>, dim3(G), dim3(lmh::kThreads), smem, s, p), "lm_head_kernel");
       break;
     default:
       rc = set_smem_limit(reinterpret_cast<const void*>(lmh::lm_head_kernel<4>), 4 * lmh::kMaxH * 4);
-      if (!rc) lmh::lm_head_kernel<4><<<G, lmh::kThreads, smem, s>>>(p);
+      if (!rc) rc = cuda_status(launch_pdl(lmh::lm_head_kernel<4>, dim3(G), dim3(lmh::kThreads), smem, s, p), "lm_head_kernel");
       break;
   }
   if (rc) return rc;
@@ -376,12 +382,11 @@ extern "C" int pyre_embed_rms_norm(const int* ids, int T, const void* table, int
       a16(norm)) {
     int threads = (n4 + lmh::kEmbVec - 1) / lmh::kEmbVec;
     threads = threads < 32 ? 32 : (threads + 31) / 32 * 32;
-    lmh::embed_rms_norm_vec_kernel<<<T, threads, 0, s>>>(ids, static_cast<const __half*>(table), V, H, w, eps, x,
-                                                          norm, status);
-    PYRE_LAUNCH_CHECK("embed_rms_norm_vec_kernel");
+    PYRE_CUDA_TRY(launch_pdl(lmh::embed_rms_norm_vec_kernel, dim3(static_cast<unsigned>(T)), dim3(threads), 0, s,
+                             ids, static_cast<const __half*>(table), V, H, w, eps, x, norm, status));
     return PYRE_OK;
   }
-  lmh::embed_rms_norm_kernel<<<T, 256, 0, s>>>(ids, static_cast<const __half*>(table), V, H, w, eps, x, norm, status);
-  PYRE_LAUNCH_CHECK("embed_rms_norm_kernel");
+  PYRE_CUDA_TRY(launch_pdl(lmh::embed_rms_norm_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, s, ids,
+                           static_cast<const __half*>(table), V, H, w, eps, x, norm, status));
   return PYRE_OK;
 }
