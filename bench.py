@@ -54,6 +54,10 @@ def parse():
     ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
     ap.add_argument("--no-attention", action="store_true", help="skip the attention and lm_head measurements")
     ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder (7B shape) measurement")
+    ap.add_argument("--decoder-only", action="store_true",
+                    help="run only the whole-decoder measurement (1 GPU) and print its JSON object")
+    ap.add_argument("--decoder-prompt", type=int, default=2048)
+    ap.add_argument("--decoder-tokens", type=int, default=256)
     return ap.parse_args()
 
 
@@ -328,7 +332,7 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
     del layers
     ids = np.random.default_rng(3).integers(0, V, prompt)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    toks = torch.zeros(decode + 1, dtype=torch.int32, device=dev)
+    toks = torch.zeros(max(decode, 8) + 1, dtype=torch.int32, device=dev)
     # warm-up: a prefill and a few decode steps
     gen.prefill(ids)
     for i in range(4):
@@ -345,7 +349,9 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
     torch.cuda.synchronize()
     e0.record()
     for i in range(decode - 1):
+        torch.cuda.nvtx.range_push("decode")   # one step per range (ncu --nvtx-include "decode/")
         gen.step_into(toks[i:i + 1], toks[i + 1:i + 2])
+        torch.cuda.nvtx.range_pop()
     e1.record()
     torch.cuda.synchronize()
     call_ms = e0.elapsed_time(e1) / (decode - 1)
@@ -557,7 +563,8 @@ def run_ours(args):
     attn = None if args.no_attention else attention_bench(dev, stream, hbm, tf_burst)
     lmh = None if args.no_attention else lmhead_bench(dev, stream, hbm)
     barrier()
-    decoder = None if (args.no_decoder or world > 1) else decoder_bench(dev, hbm)
+    decoder = None if (args.no_decoder or world > 1) else decoder_bench(dev, hbm, args.decoder_prompt,
+                                                                        args.decoder_tokens)
 
     # max over ranks
     vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(k_ms), prefill["ms_per_step"] if prefill else 0.0],
@@ -654,6 +661,13 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.decoder_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        hbm, _, _, _ = peaks()
+        print(json.dumps({"decoder_7b": decoder_bench(dev, hbm, args.decoder_prompt, args.decoder_tokens)}), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
