@@ -37,6 +37,9 @@ METRIC = "Q8_0 7B-shape decode tok/s + prefill tok/s at 1/2/4/8 B200; FFN % HBM 
 H, I = 4096, 14336
 N_SETS = 32
 Q8_BYTES_PER_PARAM = 34 / 32          # int8 + one f16 scale per 32
+# DRAM bytes (read + write) per launch of the decode FFN kernel on the whole 4096 x 14336 shard,
+# from one ncu capture (187.6 MB read, 0.7-3.3 MB written; algorithmic 187.3 MB)
+FFN_DECODE_TRAFFIC_BYTES = 189_634_688
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -594,7 +597,10 @@ def run_ours(args):
             "roofline": {"bound": "hbm",
                          "kernel": "q80_ffn_stream_kernel (gate/up + SiLU\u00b7mul + down [+ NVLink reduce], one launch, chunk-scheduled), rank 0 shard",
                          "achieved": round(k_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind, "traffic": FFN_DECODE_TRAFFIC_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 2 launches of "
+                                           "q80_ffn_stream_kernel (whole shard, T=1), "
+                                           "profiles/q80_ffn_stream_kernel_7b_decode_T1.md",
                          "algorithmic_bytes_per_launch": int(k_bytes), "avg_launch_us": round(k_avg * 1e3, 3),
                          "step_aggregate": {"bytes_all_ranks": int(step_bytes_all),
                                             "achieved_per_gpu": round(step_bytes_all / world / (ms_step * 1e-3) / 1e9, 1),
