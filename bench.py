@@ -250,7 +250,7 @@ class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
 
-    def __init__(self, dev_index: int, period_s: float = 0.005):
+    def __init__(self, dev_index: int, period_s: float = 0.001):
         self.samples = []
         self.period = period_s
         self._stop = threading.Event()
