@@ -393,6 +393,66 @@ def decoder_bench(dev, hbm, prompt: int = 2048, decode: int = 256):
                    "token for comparison; CUDA events"}
 
 
+def smollm_bench(dev, reps: int = 5):
+    """The SmolLM-135M-shaped decoder (hidden 576, 30 layers, 9/3 heads, hd 64, FFN 1536, vocab
+    49152, tied f16 embedding, RoPE theta 1e4): 8 prompt ids from default_rng(0), 10 greedy
+    tokens, end to end through Generator.generate_ids (host ids in, host ids out: prefill,
+    graphed decode steps, the copies), Q8_0 N(0, 0.02) weights made on the device. Beside it,
+    the oracle's numpy greedy loop (oracle/decoder.py, the reference's arithmetic) on the host
+    cores for the same shapes, as the CPU baseline."""
+    import numpy as np
+    import torch
+    from oracle import decoder as OD
+    from pyre_b200.generator import Generator
+    from pyre_b200.quantizer import Q80Weight
+    H, L, nq, nkv, hd, I, V = 576, 30, 9, 3, 64, 1536, 49152
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def w(k, n):
+        return Q80Weight.from_float(torch.randn((k, n), generator=g, device=dev) * 0.02, torch.float16)
+    ones = torch.ones(H, device=dev)
+    layers = [{"input_layernorm": ones, "post_attention_layernorm": ones,
+               "attn": {"q": w(H, nq * hd), "k": w(H, nkv * hd), "v": w(H, nkv * hd), "o": w(nq * hd, H)},
+               "ffn": {"gate": w(H, I), "up": w(H, I), "down": w(I, H)}} for _ in range(L)]
+    emb = (torch.randn((V, H), generator=g, device=dev) * 0.02).half()
+    gen = Generator(layers, emb, ones, n_heads=nq, n_kv_heads=nkv, head_dim=hd, rope_theta=1e4, max_seq=128,
+                    max_prompt=64, device=dev)
+    ids = np.random.default_rng(0).integers(0, V, 8)
+    n_tok = 10
+    for _ in range(2):
+        gen.generate_ids(ids, n_tok, graphed=True)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        out = gen.generate_ids(ids, n_tok, graphed=True)
+        times.append(time.perf_counter() - t0)
+    gpu_s = statistics.median(times)
+    del gen, layers
+    torch.cuda.empty_cache()
+    # CPU: the oracle's greedy loop, f32 numpy, all host threads
+    rng = np.random.default_rng(0)
+
+    def wn(shape):
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+    lw = [{"q": wn((H, nq * hd)), "k": wn((H, nkv * hd)), "v": wn((H, nkv * hd)), "o": wn((nq * hd, H)),
+           "gate": wn((H, I)), "up": wn((H, I)), "down": wn((I, H)), "ln1": np.ones(H, np.float32),
+           "ln2": np.ones(H, np.float32)} for _ in range(L)]
+    emb_np = (rng.standard_normal((V, H), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    t0 = time.perf_counter()
+    OD.greedy(emb_np, lw, np.ones(H, np.float32), ids, n_tok, nq, nkv, hd, 1e4)
+    cpu_s = time.perf_counter() - t0
+    return {"shape": "SmolLM-135M-shaped decoder: hidden 576, 30 layers, 9/3 heads, hd 64, FFN 1536, vocab 49152, "
+                     "tied embeddings",
+            "prompt_tokens": len(ids), "greedy_tokens": n_tok, "tokens": out,
+            "e2e_s": round(gpu_s, 5), "e2e_tok_s": round(n_tok / gpu_s, 1),
+            "how": "Generator.generate_ids(host ids, 10, graphed=True): prefill + CUDA-graph decode + copies, "
+                   "median of 5 after 2 warm-up runs",
+            "cpu_baseline": {"value": round(n_tok / cpu_s, 2), "unit": "tok/s", "cores": os.cpu_count(),
+                             "kind": "port", "sample": "oracle/decoder.py greedy loop (numpy f32), same shapes, "
+                                                       "one run of the 8-token prompt + 10 tokens"}}
+
+
 def make_sets(rank, bounds, n_sets, device):
     """Per weight set (one per layer): full matrices from a seeded CUDA generator (identical
     on every rank), Q8_0 on the GPU, then this rank's shard."""
@@ -568,6 +628,7 @@ def run_ours(args):
     barrier()
     decoder = None if (args.no_decoder or world > 1) else decoder_bench(dev, hbm, args.decoder_prompt,
                                                                         args.decoder_tokens)
+    smollm = None if (args.no_decoder or world > 1) else smollm_bench(dev)
 
     # max over ranks
     vals = torch.tensor([elapsed_ms, e2e_s, statistics.mean(k_ms), prefill["ms_per_step"] if prefill else 0.0],
@@ -625,6 +686,8 @@ def run_ours(args):
             res["lm_head"] = lmh
         if decoder:
             res["decoder_7b"] = decoder
+        if smollm:
+            res["decoder_smollm135m"] = smollm
         if not args.no_cpu:
             _, cpu = cpu_reference_leg(T, args.cpu_seconds)
             res["cpu_baseline"] = cpu
