@@ -323,13 +323,18 @@ class Generator:
         return self._ghist
 
     def check_status(self) -> None:
-        torch.cuda.synchronize(self.device)
-        if int(self.status.item()) != 0:
-            raise RuntimeError(f"embedding gather saw a token id outside [0, {self.V})")
+        """Raise if a kernel reported a problem: the embedding gather's status word and the
+        status words of every layer's Q8_0 kernels (QKV, O, FFN workspaces), read in one copy."""
+        words = [self.status[0]]
         for L in self.layers:
-            st = L.ffn.status()
-            if st != 0:
-                raise RuntimeError(f"FFN kernel status {st}")
+            for ws in (L.qkv.workspace, L.o.workspace, L.ffn.workspace):
+                words.append(ws[8:12].view(torch.int32)[0])
+        vals = torch.stack(words).cpu().tolist()
+        if vals[0] != 0:
+            raise RuntimeError(f"embedding gather saw a token id outside [0, {self.V})")
+        for i, v in enumerate(vals[1:]):
+            if v != 0:
+                raise RuntimeError(f"layer {i // 3} {('QKV', 'O', 'FFN')[i % 3]} kernel status {v}")
 
     def generate_ids(self, prompt_ids, max_tokens: int, want_logits: bool = False, native: bool = True,
                      stepwise_prefill: bool = False, graphed: bool = False):
