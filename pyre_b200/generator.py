@@ -208,7 +208,40 @@ class Generator:
             L.attn.reset()
         self.length = 0
 
-    def prefill(self, ids, want_logits: bool = False, stream=None, stepwise: bool = False):
+    def _prefill_graphed(self, ids: np.ndarray) -> torch.Tensor:
+        """The one-pass prefill plus lm_head replayed from a CUDA graph captured once per prompt
+        length (the ids are copied into a fixed device buffer first; the graph writes the
+        caches in place and leaves the first greedy token in its own output buffer)."""
+        T = int(ids.size)
+        dev = self.device
+        if not hasattr(self, "_pf_graphs"):
+            self._pf_graphs = {}
+            self._pf_ids = torch.zeros(self.max_prompt, dtype=torch.int32, device=dev)
+            self._pf_stream = torch.cuda.Stream(dev)
+        self._pf_ids[:T].copy_(torch.from_numpy(ids.astype(np.int32)))
+        cur = torch.cuda.current_stream(dev)
+        entry = self._pf_graphs.get(T)
+        if entry is None:
+            # one eager pass first: the ops' host-side set-up (tensor maps, limits) happens there
+            self.reset()
+            self.lm_head(self._forward(self._pf_ids[:T], True))
+            self.reset()
+            self._pf_stream.wait_stream(cur)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self._pf_stream, capture_error_mode="thread_local"):
+                tok = self.lm_head(self._forward(self._pf_ids[:T], True))
+            entry = self._pf_graphs[T] = (g, tok)
+        g, tok = entry
+        self._pf_stream.wait_stream(cur)
+        with torch.cuda.stream(self._pf_stream):
+            g.replay()
+        cur.wait_stream(self._pf_stream)
+        self.length = T
+        for L in self.layers:
+            L.attn.cache.length = T
+        return tok
+
+    def prefill(self, ids, want_logits: bool = False, stream=None, stepwise: bool = False, graphed: bool = False):
         """Run the prompt (a fresh sequence) and return the first greedy token, int64 [1, 1] on
         the device (and the logits f32 [1, V] of the last prompt position with want_logits).
 
@@ -216,12 +249,18 @@ class Generator:
         the FFN run on the tensor-core GEMM (f16 operands: activations rounded to f16, weights
         dequantized to f16). ``stepwise`` instead feeds the prompt one token at a time through
         the decode step, whose projections and FFN multiply f32 activations with the exact
-        dequantized weights (slower; the reference computes every prompt position in f32)."""
+        dequantized weights (slower; the reference computes every prompt position in f32).
+        ``graphed`` replays the one-pass prefill from a CUDA graph captured per prompt length
+        (no logits; the returned token tensor is reused by the next graphed prefill)."""
         ids = np.asarray(ids).reshape(-1)
         if ids.size < 1 or ids.size > self.max_prompt:
             raise ValueError(f"prompt length {ids.size} outside [1, {self.max_prompt}]")
         if ids.min() < 0 or ids.max() >= self.V:
             raise ValueError(f"token ids must be in [0, {self.V})")
+        if graphed:
+            if want_logits or stepwise or stream is not None:
+                raise ValueError("graphed prefill takes no logits, stepwise or stream")
+            return self._prefill_graphed(ids)
         self.reset()
         dev_ids = torch.as_tensor(ids.astype(np.int32)).to(self.device)
         n = 1 if stepwise else int(ids.size)
@@ -347,7 +386,8 @@ class Generator:
             raise ValueError("max_tokens out of range")
         if graphed and want_logits:
             raise ValueError("graphed decoding returns no logits")
-        out = self.prefill(prompt_ids, want_logits=want_logits, stepwise=stepwise_prefill)
+        out = self.prefill(prompt_ids, want_logits=want_logits, stepwise=stepwise_prefill,
+                           graphed=graphed and not stepwise_prefill)
         tok, lg0 = (out if want_logits else (out, None))
         if graphed:
             start = self.length
