@@ -363,7 +363,14 @@ class Generator:
 
     def check_status(self) -> None:
         """Raise if a kernel reported a problem: the embedding gather's status word and the
-        status words of every layer's Q8_0 kernels (QKV, O, FFN workspaces), read in one copy."""
+        status words of every layer's Q8_0 kernels (QKV, O, FFN workspaces), read in one copy,
+        and the attention kernels' status (a position outside the cache in a graphed decode
+        step, a timed-out wait), which pyre_attn_status reads and clears."""
+        torch.cuda.synchronize(self.device)
+        att = ctypes.c_int(0)
+        N.call("pyre_attn_status", ctypes.byref(att))
+        if att.value != 0:
+            raise RuntimeError(f"attention kernel status {att.value}")
         words = [self.status[0]]
         for L in self.layers:
             for ws in (L.qkv.workspace, L.o.workspace, L.ffn.workspace):
