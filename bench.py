@@ -79,6 +79,17 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), else the machine type."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or platform.machine()
+
+
 # ---------------------------------------------------------------------------------------
 # CPU leg: the reference's own per-call FFN arithmetic (oracle restatement).
 # ---------------------------------------------------------------------------------------
@@ -112,7 +123,7 @@ def cpu_reference_leg(tokens: int, budget_s: float, steps: int | None = None):
         "value": tokens / step, "unit": "tok/s", "cores": cores, "kind": "port",
         "sample": f"{len(times)} reference-worker FFN calls (Q8_0 dequantize + f32 gated FFN, numpy BLAS "
                   f"with {cores} threads) on the full 4096x14336 shard at T={tokens}; median {step * 1e3:.1f} ms/call",
-        "cpu_model": platform.processor() or platform.machine(),
+        "cpu_model": cpu_model(),
     }
 
 
@@ -660,8 +671,7 @@ def run_ours(args):
                          "achieved": round(k_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(k_gbs / hbm, 4),
                          "peak_kind": peak_kind, "traffic": FFN_DECODE_TRAFFIC_BYTES,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 2 launches of "
-                                           "q80_ffn_stream_kernel (whole shard, T=1), "
-                                           "profiles/q80_ffn_stream_kernel_7b_decode_T1.md",
+                                           "q80_ffn_stream_kernel on the whole 4096x14336 shard at T=1 (one GPU)",
                          "algorithmic_bytes_per_launch": int(k_bytes), "avg_launch_us": round(k_avg * 1e3, 3),
                          "step_aggregate": {"bytes_all_ranks": int(step_bytes_all),
                                             "achieved_per_gpu": round(step_bytes_all / world / (ms_step * 1e-3) / 1e9, 1),

@@ -145,12 +145,21 @@ PYRE_API int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H,
  *   - every GPU that loads the library holds the array until the process exits;
  *   - the first call on a device looks up the array's address on that device (with that
  *     device current); make it before any stream capture;
- *   - calls on one device share the array: each call clears it on its stream first, and
- *     calls that overlap on the GPU race (serialise them on one stream). */
+ *   - calls on one device share the array: each call clears it on its stream first (after
+ *     its argument checks pass; a rejected call queues nothing), and calls that overlap on
+ *     the GPU race (serialise them on one stream);
+ *   - the kernel's status word is not cleared by the calls: it keeps the first problem since
+ *     it was last read (PYRE_ERANGE: a partial sum was not finite or too large and that
+ *     call's out is wrong; PYRE_ETIMEOUT: a bounded wait ran out, and calls return incomplete
+ *     output until the word is read). Read it with pyre_ffn_decode_q80_noalloc_status. */
 #define PYRE_NOALLOC_SCRATCH_BYTES (4 << 20)
 PYRE_API int pyre_ffn_decode_q80_noalloc(const void* x, int x_dtype, int T, int H,
                                          const void* wgu, int gated, const void* wd, int scale_dtype,
                                          int W, float* out, void* stream);
+/* No counterpart in the reference. Synchronises stream, then returns in *status the status
+ * word of pyre_ffn_decode_q80_noalloc's static scratch on the current device (PYRE_OK,
+ * PYRE_ERANGE or PYRE_ETIMEOUT, the first since the last read) and clears it. */
+PYRE_API int pyre_ffn_decode_q80_noalloc_status(int* status, void* stream);
 
 /* out[T, H] = h @ Wd   (src/ffn/builder.py:44), and with comm != NULL also the sum of
  * that partial over every rank of comm (src/orchestrator/root_node.py:582-594 and

@@ -56,6 +56,7 @@ _SIGNATURES = {
     "pyre_ffn_down_q80": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
     "pyre_ffn_decode_q80": [_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp, _vp],
     "pyre_ffn_decode_q80_noalloc": [_vp, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _vp],
+    "pyre_ffn_decode_q80_noalloc_status": [ctypes.POINTER(_i), _vp],
     "pyre_comm_buffer_bytes": [_i, _i, _i, ctypes.POINTER(_c_i64)],
     "pyre_comm_alloc": [_c_i64, ctypes.POINTER(_vp), _vp],
     "pyre_comm_free": [_vp],

@@ -205,27 +205,41 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   return PYRE_OK;
 }
 
+namespace pyre {
+// Every argument check of pyre_ffn_decode_q80, before anything is queued on the stream.
+int ffn_decode_check(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, const void* wd,
+                     int scale_dtype, int W, const float* out, const void* workspace, int64_t ws_bytes,
+                     const pyre_comm_t* comm, const char* fn) {
+  using namespace ffn;
+  const std::string f(fn);
+  int rc = ffn_check_common(x, x_dtype, T, H, W, scale_dtype, out, workspace, ws_bytes, fn);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(T <= PYRE_FUSED_REDUCE_MAX_T, f + ": T must be <= PYRE_FUSED_REDUCE_MAX_T");
+  PYRE_CHECK_ARG(H % 32 == 0 && W % 32 == 0, f + ": H and W must be multiples of 32");
+  PYRE_CHECK_ARG(wgu != nullptr && wd != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(wd) % 16 == 0,
+                 f + ": packed weights must be non-null and 16-byte aligned");
+  PYRE_CHECK_ARG(tiles_of(H) <= kMaxTiles && tiles_of(W) <= kMaxTiles, f + ": dims too large");
+  if (comm != nullptr) {
+    const bool tp = comm->world > 1;
+    PYRE_CHECK_ARG(comm->hidden == H, f + ": communicator hidden size differs from H");
+    PYRE_CHECK_ARG(T <= comm->max_tokens, f + ": T exceeds the communicator's max_tokens");
+    PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, f + ": H too large for the fused reduce");
+  }
+  if (ws_bytes < decode_ws_bytes(T, H, W, gated ? 2 : 1))
+    return set_error(PYRE_ENOMEM, f + ": workspace smaller than pyre_ffn_workspace_bytes()");
+  return PYRE_OK;
+}
+}  // namespace pyre
+
 extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, const void* wgu, int gated,
                                    const void* wd, int scale_dtype, int W, float* out, void* workspace,
                                    int64_t ws_bytes, pyre_comm_t* comm, void* stream) {
-  int rc = ffn_check_common(x, x_dtype, T, H, W, scale_dtype, out, workspace, ws_bytes, "pyre_ffn_decode_q80");
+  int rc = ffn_decode_check(x, x_dtype, T, H, wgu, gated, wd, scale_dtype, W, out, workspace, ws_bytes, comm,
+                            "pyre_ffn_decode_q80");
   if (rc) return rc;
-  PYRE_CHECK_ARG(T <= PYRE_FUSED_REDUCE_MAX_T, "pyre_ffn_decode_q80: T must be <= PYRE_FUSED_REDUCE_MAX_T");
-  PYRE_CHECK_ARG(H % 32 == 0 && W % 32 == 0, "pyre_ffn_decode_q80: H and W must be multiples of 32");
-  PYRE_CHECK_ARG(wgu != nullptr && wd != nullptr && reinterpret_cast<uintptr_t>(wgu) % 16 == 0 &&
-                     reinterpret_cast<uintptr_t>(wd) % 16 == 0,
-                 "pyre_ffn_decode_q80: packed weights must be non-null and 16-byte aligned");
-  PYRE_CHECK_ARG(tiles_of(H) <= kMaxTiles && tiles_of(W) <= kMaxTiles, "pyre_ffn_decode_q80: dims too large");
   const bool tp = comm != nullptr && comm->world > 1;
-  if (comm != nullptr) {
-    PYRE_CHECK_ARG(comm->hidden == H, "pyre_ffn_decode_q80: communicator hidden size differs from H");
-    PYRE_CHECK_ARG(T <= comm->max_tokens, "pyre_ffn_decode_q80: T exceeds the communicator's max_tokens");
-    PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, "pyre_ffn_decode_q80: H too large for the fused reduce");
-  }
   const int na = gated ? 2 : 1;
-  const int64_t need = decode_ws_bytes(T, H, W, na);
-  if (ws_bytes < need)
-    return set_error(PYRE_ENOMEM, "pyre_ffn_decode_q80: workspace smaller than pyre_ffn_workspace_bytes()");
   char* wsc = static_cast<char*>(workspace);
   StreamParams p{};
   p.T = T;

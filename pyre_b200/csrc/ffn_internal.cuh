@@ -88,6 +88,11 @@ int set_smem_once(K kern, int bytes) {
 int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_dtype, const void* out,
                      const void* ws, int64_t ws_bytes, const char* fn);
 // Streaming-kernel forms of the two-call entry points for T <= 4 (defined in ffn_decode.cu).
+// Every argument check of pyre_ffn_decode_q80 (defined in ffn_decode.cu); fn names the caller
+// in the error text.
+int ffn_decode_check(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, const void* wd,
+                     int scale_dtype, int W, const float* out, const void* workspace, int64_t ws_bytes,
+                     const pyre_comm_t* comm, const char* fn);
 int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
                 void* out, int out_dtype, void* staging, int64_t staging_bytes, void* partial, int64_t partial_bytes,
                 unsigned int* counters, int* status, cudaStream_t s);

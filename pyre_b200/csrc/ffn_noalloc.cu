@@ -16,15 +16,20 @@
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that first call
 //     before any stream capture.
 //   - All calls on one device share the array and it keeps the last call's contents. Every
-//     call therefore clears the parts that must start at zero (status word, counters, flags,
-//     slab accumulators) with a cudaMemsetAsync on the call's stream before the launch.
-//     Calls that overlap on the GPU (different streams, or host threads without ordering)
+//     call therefore clears the parts that must start at zero (counters, flags, slab
+//     accumulators) with cudaMemsetAsync on the call's stream before the launch, after all
+//     of its argument checks have passed (a rejected call queues nothing).
+//   - The kernel's status word (PYRE_ERANGE for a partial sum that is not finite or too
+//     large, PYRE_ETIMEOUT for a bounded wait that ran out) is NOT cleared by the calls: it
+//     keeps the first problem since it was last read. pyre_ffn_decode_q80_noalloc_status()
+//     synchronises the stream, returns the word and clears it.
+//   - Calls that overlap on the GPU (different streams, or host threads without ordering)
 //     race on the array and give wrong results; serialise them on one stream.
 //   - Single GPU only (no tensor-parallel reduce: a communicator needs allocated buffers).
 #include <mutex>
 #include <string>
 
-#include "common.cuh"
+#include "ffn_internal.cuh"
 
 namespace pyre {
 namespace {
@@ -76,8 +81,32 @@ extern "C" int pyre_ffn_decode_q80_noalloc(const void* x, int x_dtype, int T, in
   void* scratch = nullptr;
   rc = scratch_on_current_device(&scratch);
   if (rc) return rc;
+  // every check the launch will make, before the shared array is touched
+  rc = ffn_decode_check(x, x_dtype, T, H, wgu, gated, wd, scale_dtype, W, out, scratch, need, nullptr,
+                        "pyre_ffn_decode_q80_noalloc");
+  if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The workspace needs zeros except in the h rows; clearing all of it is one small memset.
-  PYRE_CUDA_TRY(cudaMemsetAsync(scratch, 0, static_cast<size_t>(need), s));
+  // zeros everywhere but the status word (kept until read) and the h rows (plain data, but
+  // clearing them with the rest is one memset either way)
+  char* sc = static_cast<char*>(scratch);
+  constexpr int64_t kStatusEnd = gemv::kHdrStatus + 4;
+  PYRE_CUDA_TRY(cudaMemsetAsync(sc, 0, static_cast<size_t>(gemv::kHdrStatus), s));
+  PYRE_CUDA_TRY(cudaMemsetAsync(sc + kStatusEnd, 0, static_cast<size_t>(need - kStatusEnd), s));
   return pyre_ffn_decode_q80(x, x_dtype, T, H, wgu, gated, wd, scale_dtype, W, out, scratch, need, nullptr, stream);
+}
+
+extern "C" int pyre_ffn_decode_q80_noalloc_status(int* status, void* stream) {
+  using namespace pyre;
+  PYRE_CHECK_ARG(status != nullptr, "pyre_ffn_decode_q80_noalloc_status: null status");
+  void* scratch = nullptr;
+  int rc = scratch_on_current_device(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* word = reinterpret_cast<int*>(static_cast<char*>(scratch) + gemv::kHdrStatus);
+  int h = 0;
+  PYRE_CUDA_TRY(cudaStreamSynchronize(s));
+  PYRE_CUDA_TRY(cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost));
+  PYRE_CUDA_TRY(cudaMemset(word, 0, sizeof(int)));
+  *status = h;
+  return PYRE_OK;
 }

@@ -208,29 +208,42 @@ class Generator:
             L.attn.reset()
         self.length = 0
 
+    # captured prefill graphs kept at once (least recently used dropped first)
+    PREFILL_GRAPHS = 8
+
     def _prefill_graphed(self, ids: np.ndarray) -> torch.Tensor:
         """The one-pass prefill plus lm_head replayed from a CUDA graph captured once per prompt
         length (the ids are copied into a fixed device buffer first; the graph writes the
-        caches in place and leaves the first greedy token in its own output buffer)."""
+        caches in place and leaves the first greedy token in its own output buffer).
+
+        Memory: every captured graph draws its activations ([T, H] rows, the QKV / attention /
+        FFN intermediates of one prompt length) from one memory pool shared by all of this
+        object's prefill graphs (they only ever replay one at a time, on one stream), and at
+        most PREFILL_GRAPHS lengths are kept, so serving many prompt lengths holds about the
+        activations of the longest prompt, not one set per length."""
         T = int(ids.size)
         dev = self.device
         if not hasattr(self, "_pf_graphs"):
-            self._pf_graphs = {}
+            self._pf_graphs = {}                 # insertion order = least recently used first
+            self._pf_pool = torch.cuda.graph_pool_handle()
             self._pf_ids = torch.zeros(self.max_prompt, dtype=torch.int32, device=dev)
             self._pf_stream = torch.cuda.Stream(dev)
         self._pf_ids[:T].copy_(torch.from_numpy(ids.astype(np.int32)))
         cur = torch.cuda.current_stream(dev)
-        entry = self._pf_graphs.get(T)
+        entry = self._pf_graphs.pop(T, None)
         if entry is None:
+            while len(self._pf_graphs) >= self.PREFILL_GRAPHS:
+                self._pf_graphs.pop(next(iter(self._pf_graphs)))
             # one eager pass first: the ops' host-side set-up (tensor maps, limits) happens there
             self.reset()
             self.lm_head(self._forward(self._pf_ids[:T], True))
             self.reset()
             self._pf_stream.wait_stream(cur)
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=self._pf_stream, capture_error_mode="thread_local"):
+            with torch.cuda.graph(g, pool=self._pf_pool, stream=self._pf_stream, capture_error_mode="thread_local"):
                 tok = self.lm_head(self._forward(self._pf_ids[:T], True))
-            entry = self._pf_graphs[T] = (g, tok)
+            entry = (g, tok)
+        self._pf_graphs[T] = entry
         g, tok = entry
         self._pf_stream.wait_stream(cur)
         with torch.cuda.stream(self._pf_stream):
@@ -368,7 +381,8 @@ class Generator:
         step, a timed-out wait), which pyre_attn_status reads and clears."""
         torch.cuda.synchronize(self.device)
         att = ctypes.c_int(0)
-        N.call("pyre_attn_status", ctypes.byref(att))
+        with torch.cuda.device(self.device):     # pyre_attn_status reads the current device
+            N.call("pyre_attn_status", ctypes.byref(att))
         if att.value != 0:
             raise RuntimeError(f"attention kernel status {att.value}")
         words = [self.status[0]]

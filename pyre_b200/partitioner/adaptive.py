@@ -1,12 +1,29 @@
 """Adaptive non-uniform FFN partitioner and drift detector.
 
-Restates ``AdaptivePartitioner`` (src/orchestrator/cluster.py:228-403) and
-``ClusterOrchestrator.detect_drift`` (cluster.py:217-225) with the same names, defaults
-(EMA alpha 0.3, drift threshold 1.15, width clamp [0.25, 1.75] x base) and partition dict
-format (``ffn_start/ffn_end/seq_start/seq_end``, root_node.py:202-207). The timings it
-consumes here are per-rank CUDA-event durations of the FFN kernels instead of TCP
-receive wall times. ``block`` > 1 rounds widths to whole Q8_0 blocks after the
-reference's allocation (the reference itself uses block = 1).
+Behaviour (the reference's ``AdaptivePartitioner``, src/orchestrator/cluster.py:228-403, and
+``ClusterOrchestrator.detect_drift``, cluster.py:217-225), stated as rules:
+
+* Timings. ``update({node: seconds})`` appends one FFN time per node for the current pass
+  (unknown node ids are ignored); ``reset_pass()`` starts a new pass.
+* Speed estimate. Folding a pass into the estimate takes each node's mean time m_i over the
+  pass (nodes without timings are skipped), their plain mean M, and moves node i's relative
+  speed e_i towards M / m_i: ``e_i <- e_i * (1 - alpha) + (M / max(m_i, 1e-9)) * alpha``,
+  alpha = 0.3, all e_i starting at 1. Both ``drift_detected()`` (when the pass has timings)
+  and ``get_partitions()`` fold the current pass in, each time they are called, as the
+  reference does.
+* Drift: some e_i above ``threshold`` (1.15) or below 1 / threshold.
+* Widths. Node 0 (the root, whose time the reference cannot isolate) keeps
+  ``units // n``. The other nodes split the rest R in proportion to e_i (``int(R * e_i /
+  sum e)``; an even split if the sum is not positive), each clamped to [lo, R - (n - 2) lo]
+  with lo = max(1, int(units * min_fraction / n)); a positive leftover goes to the fastest
+  node (first of equals), an overdraft is taken from the slowest (first of equals) down to
+  lo at most.
+* Sequence split of the partition dicts (root_node.py:202-207): ``seq_len // n`` per node,
+  the last node up to ``seq_len``.
+
+Units are Q8_0 blocks of ``block`` elements (``block`` = 1 is the reference's element
+granularity; 32 keeps every shard boundary on a Q8_0 block, which the device format needs).
+The timings consumed here are per-rank CUDA-event FFN durations instead of TCP receive times.
 """
 from __future__ import annotations
 
@@ -14,143 +31,110 @@ from typing import Dict, List
 
 
 def detect_drift(execution_times: List[float], threshold: float = 1.15) -> bool:
-    """True when any time exceeds ``threshold`` x the mean (cluster.py:217-225)."""
+    """True when some time is above ``threshold`` x the mean of all of them."""
     if not execution_times:
         return False
-    avg_time = sum(execution_times) / len(execution_times)
-    for t in execution_times:
-        if t > avg_time * threshold:
-            return True
-    return False
+    limit = sum(execution_times) / len(execution_times) * threshold
+    return any(t > limit for t in execution_times)
+
+
+def _seq_range(node: int, n: int, seq_len: int) -> tuple:
+    chunk = seq_len // n
+    if node == n - 1:
+        return (n - 1) * chunk, seq_len
+    return node * chunk, (node + 1) * chunk
+
+
+def split_in_proportion(total: int, weights: List[float], lo: int) -> List[int]:
+    """``total`` units over len(weights) parts in proportion to the weights, each part clamped
+    to [lo, total - (parts - 1) lo]; leftover units go to the heaviest part, an overdraft is
+    taken from the lightest (not below lo)."""
+    parts = len(weights)
+    hi = total - (parts - 1) * lo
+    wsum = sum(weights)
+    shares = [int(total * w / wsum) for w in weights] if wsum > 0 else [total // parts] * parts
+    shares = [max(lo, min(s, hi)) for s in shares]
+    left = total - sum(shares)
+    if left > 0:
+        shares[weights.index(max(weights))] += left
+    elif left < 0:
+        k = weights.index(min(weights))
+        shares[k] = max(lo, shares[k] + left)
+    return shares
 
 
 class AdaptivePartitioner:
-    """EMA of per-node relative speed -> non-uniform FFN widths (cluster.py:228-403)."""
+    """Relative node speeds (an exponential moving average over passes) -> FFN shard widths."""
 
-    def __init__(self, ffn_dim: int, num_nodes: int, seq_len: int = 64,
-                 min_fraction: float = 0.25, max_fraction: float = 1.75,
-                 ema_alpha: float = 0.3, block: int = 1):
-        self.ffn_dim = ffn_dim
-        self.num_nodes = num_nodes
-        self.seq_len = seq_len
-        self.block = block
-        self.base_width = ffn_dim // num_nodes
-        self.min_width = max(1, int(ffn_dim * min_fraction / num_nodes))
-        self.max_width = min(ffn_dim, int(ffn_dim * max_fraction / num_nodes))
-        self.max_width = min(self.max_width, ffn_dim - (num_nodes - 1) * self.min_width)
+    def __init__(self, ffn_dim: int, num_nodes: int, seq_len: int = 64, min_fraction: float = 0.25,
+                 max_fraction: float = 1.75, ema_alpha: float = 0.3, block: int = 1):
+        if num_nodes < 1 or ffn_dim < num_nodes * block:
+            raise ValueError("need at least one block of the FFN dim per node")
+        if ffn_dim % block:
+            raise ValueError(f"ffn_dim {ffn_dim} is not a multiple of the block {block}")
+        self.ffn_dim, self.num_nodes, self.seq_len, self.block = ffn_dim, num_nodes, seq_len, block
         self.alpha = ema_alpha
+        # max_fraction is accepted for signature parity: the reference derives an upper width
+        # from it but never applies it, so the widths here do not depend on it either
+        self.max_fraction = max_fraction
+        self.units = ffn_dim // block
+        self.min_units = max(1, int(self.units * min_fraction / num_nodes))
         self.ema: List[float] = [1.0] * num_nodes
-        self._layer_timings: Dict[int, List[float]] = {i: [] for i in range(num_nodes)}
-        self._drift_counter = 0
+        self._times: List[List[float]] = [[] for _ in range(num_nodes)]
 
-    def update(self, node_timings: Dict[int, float]):
-        for nid, t in node_timings.items():
-            if nid in self._layer_timings:
-                self._layer_timings[nid].append(t)
+    # ---- timings ------------------------------------------------------------------------
+    def update(self, node_timings: Dict[int, float]) -> None:
+        for node, t in node_timings.items():
+            if 0 <= node < self.num_nodes:
+                self._times[node].append(t)
 
-    def _recompute_ema(self):
-        timings = {nid: ts for nid, ts in self._layer_timings.items() if ts}
-        if not timings:
+    def reset_pass(self) -> None:
+        self._times = [[] for _ in range(self.num_nodes)]
+
+    def _fold_pass(self) -> None:
+        means = [(i, sum(ts) / len(ts)) for i, ts in enumerate(self._times) if ts]
+        if not means:
             return
-        avg_times = {nid: sum(ts) / len(ts) for nid, ts in timings.items()}
-        global_avg = sum(avg_times.values()) / len(avg_times)
-        for nid, t in avg_times.items():
-            relative = global_avg / max(t, 1e-9)
-            self.ema[nid] = self.ema[nid] * (1 - self.alpha) + relative * self.alpha
+        overall = sum(m for _, m in means) / len(means)
+        a = self.alpha
+        for i, m in means:
+            self.ema[i] = self.ema[i] * (1 - a) + (overall / max(m, 1e-9)) * a
 
+    # ---- decisions ----------------------------------------------------------------------
     def drift_detected(self, threshold: float = 1.15) -> bool:
-        if not self._has_data():
+        if not any(self._times):
             return False
-        self._recompute_ema()
-        for v in self.ema:
-            if v > threshold or v < 1.0 / threshold:
-                return True
-        return False
-
-    def _has_data(self) -> bool:
-        return any(len(ts) > 0 for ts in self._layer_timings.values())
+        self._fold_pass()
+        return any(e > threshold or e < 1.0 / threshold for e in self.ema)
 
     def get_partitions(self) -> Dict[int, dict]:
-        self._recompute_ema()
-        parts = self._allocate_partitions()
-        return self._round_to_blocks(parts) if self.block > 1 else parts
-
-    def _allocate_partitions(self) -> Dict[int, dict]:
-        total_nodes = self.num_nodes
-        seq_chunk = self.seq_len // total_nodes
-        if total_nodes == 1:
-            return {0: {"ffn_start": 0, "ffn_end": self.ffn_dim, "seq_start": 0, "seq_end": self.seq_len}}
-        root_base = self.base_width
-        remaining = self.ffn_dim - root_base
-        worker_emas = self.ema[1:]
-        total_worker_weight = sum(worker_emas)
-        raw_widths = []
-        for v in worker_emas:
-            w = int(remaining * v / total_worker_weight) if total_worker_weight > 0 else remaining // (total_nodes - 1)
-            raw_widths.append(max(self.min_width, min(w, remaining - (total_nodes - 2) * self.min_width)))
-        clamped = [max(self.min_width, min(w, remaining - (total_nodes - 2) * self.min_width)) for w in raw_widths]
-        allocated = sum(clamped)
-        residual = remaining - allocated
-        if residual > 0:
-            fastest_wi = max(range(len(clamped)), key=lambda i: worker_emas[i])
-            clamped[fastest_wi] += residual
-        elif residual < 0:
-            slowest_wi = min(range(len(clamped)), key=lambda i: worker_emas[i])
-            clamped[slowest_wi] = max(self.min_width, clamped[slowest_wi] + residual)
-        partitions: Dict[int, dict] = {0: {"ffn_start": 0, "ffn_end": root_base, "seq_start": 0, "seq_end": seq_chunk}}
-        offset = root_base
-        for wi, width in enumerate(clamped):
-            nid = wi + 1
-            partitions[nid] = {
-                "ffn_start": offset,
-                "ffn_end": offset + width,
-                "seq_start": nid * seq_chunk if nid < total_nodes - 1 else (total_nodes - 1) * seq_chunk,
-                "seq_end": (nid + 1) * seq_chunk if nid < total_nodes - 1 else self.seq_len,
-            }
-            offset += width
-        return partitions
-
-    def _round_to_blocks(self, parts: Dict[int, dict]) -> Dict[int, dict]:
-        """Snap every interior boundary to the nearest block edge (keeping each width
-        >= one block); the first start and the last end stay 0 and ffn_dim."""
-        b = self.block
-        ids = sorted(parts)
-        ends = [parts[i]["ffn_end"] for i in ids]
-        snapped = []
-        prev = 0
-        for k, e in enumerate(ends):
-            if k == len(ends) - 1:
-                e2 = self.ffn_dim
-            else:
-                e2 = int(round(e / b)) * b
-                e2 = max(e2, prev + b)
-                e2 = min(e2, self.ffn_dim - (len(ends) - 1 - k) * b)
-            snapped.append(e2)
-            prev = e2
-        out, start = {}, 0
-        for i, e in zip(ids, snapped):
-            d = dict(parts[i])
-            d["ffn_start"], d["ffn_end"] = start, e
-            out[i] = d
-            start = e
-        return out
+        """Partition dicts ``{node: {ffn_start, ffn_end, seq_start, seq_end}}`` for the next pass."""
+        self._fold_pass()
+        n = self.num_nodes
+        if n == 1:
+            widths = [self.units]
+        else:
+            root = self.units // n
+            widths = [root] + split_in_proportion(self.units - root, self.ema[1:], self.min_units)
+        parts, start = {}, 0
+        for node, w in enumerate(widths):
+            s0, s1 = _seq_range(node, n, self.seq_len)
+            end = self.ffn_dim if n == 1 else (start + w) * self.block
+            parts[node] = {"ffn_start": start * self.block, "ffn_end": end, "seq_start": s0, "seq_end": s1}
+            start += w
+        return parts
 
     def layer_partition(self, node_id: int, layer_idx: int) -> dict:
+        """This node's dict from :meth:`get_partitions` (the reference ignores ``layer_idx`` too)."""
         return self.get_partitions().get(node_id, {})
 
     @staticmethod
     def equal_partitions(ffn_dim: int, num_nodes: int, seq_len: int = 64) -> Dict[int, dict]:
-        seq_chunk = seq_len // num_nodes
-        ffn_chunk = ffn_dim // num_nodes
-        partitions = {}
+        """``ffn_dim // n`` per node, the last one up to ``ffn_dim`` (``RootNode._solve_partitions``)."""
+        chunk = ffn_dim // num_nodes
+        parts = {}
         for i in range(num_nodes):
-            partitions[i] = {
-                "ffn_start": i * ffn_chunk,
-                "ffn_end": (i + 1) * ffn_chunk if i < num_nodes - 1 else ffn_dim,
-                "seq_start": i * seq_chunk,
-                "seq_end": (i + 1) * seq_chunk if i < num_nodes - 1 else seq_len,
-            }
-        return partitions
-
-    def reset_pass(self):
-        self._layer_timings = {i: [] for i in range(self.num_nodes)}
+            s0, s1 = _seq_range(i, num_nodes, seq_len)
+            parts[i] = {"ffn_start": i * chunk, "ffn_end": ffn_dim if i == num_nodes - 1 else (i + 1) * chunk,
+                        "seq_start": s0, "seq_end": s1}
+        return parts
