@@ -199,6 +199,13 @@ PYRE_API int pyre_comm_check(pyre_comm_t* comm, int* status, void* stream);
 /* In-place sum over ranks of a f32 buffer of n elements (two-shot: reduce-scatter then
  * all-gather through peer memory), rank order 0..world-1. n <= max_tokens * hidden. */
 PYRE_API int pyre_allreduce_sum_f32(pyre_comm_t* comm, float* buf, int64_t n, void* stream);
+/* Greedy token over a vocabulary split across the ranks of comm (Generator._sample at
+ * temperature < 0.01, src/orchestrator/generator.py:51-53, np.argmax over the whole logit row):
+ * key[T] is this rank's best (value, index) key per row from pyre_lm_head_argmax on its rows of
+ * the table; every rank gets token[t] = the index of the largest key over the ranks (equal
+ * values: the lower index) and, when key_out is not NULL, that key. T <= 4. */
+PYRE_API int pyre_argmax_combine(pyre_comm_t* comm, const long long* key, int T, int* token, long long* key_out,
+                                 void* stream);
 
 /* ---- attention path ------------------------------------------------------------------
  * out[T, N] (f32) = x[T, K] @ W, W a packed single Q8_0 matrix [K, N] (pyre_q80_pack with
@@ -208,6 +215,12 @@ PYRE_API int pyre_allreduce_sum_f32(pyre_comm_t* comm, float* buf, int64_t n, vo
  * zero-initialised, pyre_ffn_workspace_bytes(T, K, N) bytes. */
 PYRE_API int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N,
                              float* out, void* workspace, int64_t ws_bytes, void* stream);
+/* The same with an f32 bias [N] added to every output row (bias may be NULL): the Q/K/V
+ * projections with q_bias / k_bias / v_bias that the reference adds right after x @ W, before
+ * RoPE (src/orchestrator/root_node.py:443-451 prefill, :786-799 decode; Qwen2-style models). The
+ * bias joins the finished f32 dot product in the kernel's epilogue. */
+PYRE_API int pyre_q80_linear_bias(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N,
+                                  const float* bias, float* out, void* workspace, int64_t ws_bytes, void* stream);
 
 /* out[r, :] = f32(x[r, :] * rstd_r * w) with rstd_r = 1 / sqrt(mean(x[r, :]^2) + eps), the sum
  * of squares in f64 (pyre_kernels.mojo:18-35; the reference uses eps = 1e-6). x, out: f32
@@ -326,6 +339,7 @@ typedef struct pyre_decoder_layer {
   const float* rope;   /* pyre_rope_table for max_t positions */
   void* attn_ws;       /* pyre_attn_decode_workspace_bytes */
   int64_t attn_ws_bytes;
+  const float* qkv_bias; /* f32 [(nq + 2 nkv) hd]: [q_bias | k_bias | v_bias], or NULL */
 } pyre_decoder_layer;
 
 typedef struct pyre_decoder_desc {
@@ -347,6 +361,15 @@ typedef struct pyre_decoder_desc {
                         * *pos_dev += 1, so the step can be captured once in a CUDA graph and
                         * replayed for positions pos, pos + 1, ... */
   int* history;        /* with pos_dev: int32 [max_t + 1], token at each position */
+  /* Tensor parallelism (NULL: one GPU). Rank r of comm holds heads nq, nkv of this struct (its
+   * share), the QKV columns and O rows of those heads, an FFN shard of ffn_width, and lm_head
+   * rows lm_v0 .. lm_v0 + lm_V - 1 of the vocabulary; the O projection and the FFN sum their
+   * partials over the ranks in their epilogues (NVLink peer stores), and the ranks' best
+   * (value, index) keys are combined over comm into the greedy token. Every rank makes the same
+   * calls in the same order. */
+  pyre_comm_t* comm;
+  int64_t lm_v0;       /* first vocabulary row of lm_head (0 without a vocabulary split) */
+  int lm_V;            /* rows of lm_head; 0: V (the whole table) */
 } pyre_decoder_desc;
 
 /* One decode step: token_in (int32 [1], device) at position pos (= tokens already in the

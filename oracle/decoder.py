@@ -30,12 +30,18 @@ from . import lmhead as OL
 def layer(x: np.ndarray, lw: dict, cache: dict, n_heads: int, n_kv: int, head_dim: int, theta: float,
           eps: float = 1e-6, prefill: bool = False) -> np.ndarray:
     """x: f32 [S, H] (the prompt with prefill, else one token). lw: ln1, ln2, q, k, v, o, gate,
-    up, down (f32, matrices [in, out]). cache: {"k": [1, n_kv, t, hd], "v": ...}, updated."""
+    up, down (f32, matrices [in, out]) and optionally q_bias, k_bias, v_bias (f32). cache: {"k": [1, n_kv, t, hd], "v": ...}, updated."""
     S = x.shape[0]
     xn = K.rms_norm(x, lw["ln1"], eps)
-    q = K.matmul_f32(xn, lw["q"]).reshape(1, S, n_heads, head_dim)
-    k = K.matmul_f32(xn, lw["k"]).reshape(1, S, n_kv, head_dim)
-    v = K.matmul_f32(xn, lw["v"]).reshape(1, S, n_kv, head_dim)
+    q, k, v = (K.matmul_f32(xn, lw[n]) for n in ("q", "k", "v"))
+    # optional f32 biases added right after the projections (root_node.py:443-451 prefill,
+    # :786-799 head-partitioned decode)
+    for t, n in ((q, "q_bias"), (k, "k_bias"), (v, "v_bias")):
+        if lw.get(n) is not None:
+            t += np.asarray(lw[n], np.float32).reshape(1, -1)
+    q = q.reshape(1, S, n_heads, head_dim)
+    k = k.reshape(1, S, n_kv, head_dim)
+    v = v.reshape(1, S, n_kv, head_dim)
     if prefill:
         a = OA.compute_attention([(q, k, v)], n_heads, n_kv, 1.0, theta)[0]
         cache["k"] = K.apply_rope(np.ascontiguousarray(k.transpose(0, 2, 1, 3)), theta, 0, 1.0)

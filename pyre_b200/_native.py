@@ -68,6 +68,8 @@ _SIGNATURES = {
     "pyre_comm_check": [_vp, ctypes.POINTER(_i), _vp],
     "pyre_allreduce_sum_f32": [_vp, _vp, _c_i64, _vp],
     "pyre_q80_linear": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp],
+    "pyre_q80_linear_bias": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _c_i64, _vp],
+    "pyre_argmax_combine": [_vp, _vp, _i, _vp, _vp, _vp],
     "pyre_rms_norm": [_vp, _i, _i, _vp, ctypes.c_double, _vp, _vp],
     "pyre_add_rms_norm": [_vp, _vp, _i, _i, _vp, ctypes.c_double, _vp, _vp, _vp],
     "pyre_decoder_step": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp],

@@ -26,10 +26,13 @@ def _workspace(tokens: int, k: int, n: int, device) -> torch.Tensor:
 
 
 class Q80Linear:
-    """``out[T, N] = x[T, K] @ W`` for a packed single Q8_0 matrix, up to ``max_tokens``
-    rows per call; holds the kernels' zero-initialised scratch."""
+    """``out[T, N] = x[T, K] @ W (+ bias)`` for a packed single Q8_0 matrix, up to
+    ``max_tokens`` rows per call; holds the kernels' zero-initialised scratch. ``bias`` (f32
+    [N], optional) is added to the finished f32 products in the kernels' epilogue, as the
+    reference adds q_bias / k_bias / v_bias right after the projections
+    (src/orchestrator/root_node.py:443-451)."""
 
-    def __init__(self, weight: Q80Weight | Q80Packed, max_tokens: int, device=None):
+    def __init__(self, weight: Q80Weight | Q80Packed, max_tokens: int, device=None, bias=None):
         self.w = weight if isinstance(weight, Q80Packed) else Q80Packed.pack(weight)
         if self.w.m != 1:
             raise ValueError("Q80Linear takes one matrix")
@@ -37,6 +40,12 @@ class Q80Linear:
         self.max_tokens = int(max_tokens)
         dev = device if device is not None else self.w.data.device
         self.workspace = _workspace(self.max_tokens, self.k, self.n, dev)
+        self.bias = None
+        if bias is not None:
+            b = torch.as_tensor(bias).detach().to(dev, torch.float32).reshape(-1).contiguous()
+            if b.numel() != self.n:
+                raise ValueError(f"bias must have {self.n} elements, got {b.numel()}")
+            self.bias = b
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         if x.dim() != 2 or x.shape[1] != self.k:
@@ -48,8 +57,9 @@ class Q80Linear:
         if out is None:
             out = torch.empty((T, self.n), dtype=torch.float32, device=x.device)
         ws = self.workspace
-        N.call("pyre_q80_linear", D.ptr(x), D.dtype_code(x), T, self.k, D.ptr(self.w.data), self.w.scale_code, self.n,
-               D.ptr(out), D.ptr(ws), ws.numel(), D.stream_ptr(stream))
+        N.call("pyre_q80_linear_bias", D.ptr(x), D.dtype_code(x), T, self.k, D.ptr(self.w.data), self.w.scale_code,
+               self.n, D.ptr(self.bias) if self.bias is not None else None, D.ptr(out), D.ptr(ws), ws.numel(),
+               D.stream_ptr(stream))
         return out
 
 

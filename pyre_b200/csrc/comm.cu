@@ -4,6 +4,7 @@
 // The reference gathers FFN partials at the root over TCP and sums them in worker order
 // (src/orchestrator/root_node.py:582-594, :982-995). Here every rank sums the same
 // partials in rank order 0..world-1, so all ranks hold bit-identical results.
+#include <climits>
 #include <vector>
 
 #include "comm.cuh"
@@ -76,7 +77,52 @@ __global__ void __launch_bounds__(512) allreduce_two_shot_kernel(DevComm c, floa
   comm::epoch_end(c, epoch);
 }
 
+// Greedy token over a vocabulary split across the ranks: each rank holds the best
+// (value, index) key of its vocabulary rows per token row (pyre_lm_head_argmax); the ranks
+// exchange them through peer memory and every rank takes the maximum key, whose low half
+// names the winning index (0xFFFFFFFF - low: equal values go to the lower index, as
+// np.argmax over the whole vocabulary would). One CTA, every wait bounded.
+__global__ void __launch_bounds__(32) key_max_kernel(DevComm c, const long long* __restrict__ key, int T,
+                                                     int* __restrict__ token, long long* __restrict__ key_out) {
+  const uint32_t epoch = comm::epoch_begin(c);
+  const int slot = epoch & 1u;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < c.world * T; i += 32) {
+    const int peer = i / T, t = i - peer * T;
+    reinterpret_cast<long long*>(comm::ar_slot(c, peer, slot, 0, c.rank))[t] = key[t];
+  }
+  __threadfence_system();
+  __syncwarp();
+  if (tid < c.world) st_release_sys(comm::ar_flag(c, tid, slot, 0, c.rank, 0), epoch);
+  if (tid < c.world) {
+    if (!wait_flag_eq(comm::ar_flag(c, c.rank, slot, 0, tid, 0), epoch, c.timeout_ns))
+      atomicExch(c.status, PYRE_ETIMEOUT);
+  }
+  __syncwarp();
+  if (tid < T) {
+    long long best = LLONG_MIN;
+    for (int src = 0; src < c.world; ++src) {
+      const long long k = __ldcg(reinterpret_cast<const long long*>(comm::ar_slot(c, c.rank, slot, 0, src)) + tid);
+      best = k > best ? k : best;
+    }
+    const unsigned long long u = static_cast<unsigned long long>(best) ^ 0x8000000000000000ull;
+    token[tid] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(u & 0xFFFFFFFFull));
+    if (key_out != nullptr) key_out[tid] = best;
+  }
+  comm::epoch_end(c, epoch);
+}
+
 }  // namespace
+
+int argmax_combine(pyre_comm* c, const long long* key, int T, int* token, long long* key_out, cudaStream_t stream) {
+  PYRE_CHECK_ARG(c != nullptr && key != nullptr && token != nullptr, "pyre_argmax_combine: null argument");
+  PYRE_CHECK_ARG(T >= 1 && T <= PYRE_FUSED_REDUCE_MAX_T, "pyre_argmax_combine: 1 <= T <= PYRE_FUSED_REDUCE_MAX_T");
+  PYRE_CHECK_ARG(2LL * T <= comm::layout(c->world, c->max_tokens, c->hidden).ar_chunk,
+                 "pyre_argmax_combine: communicator buffer too small");
+  key_max_kernel<<<1, 32, 0, stream>>>(comm::device_view(c), key, T, token, key_out);
+  PYRE_LAUNCH_CHECK("key_max_kernel");
+  return PYRE_OK;
+}
 
 int allreduce_sum_f32(pyre_comm* c, float* buf, int64_t n, cudaStream_t stream) {
   const comm::Layout L = comm::layout(c->world, c->max_tokens, c->hidden);
@@ -218,6 +264,11 @@ extern "C" int pyre_comm_check(pyre_comm_t* c, int* status, void* stream) {
   PYRE_CUDA_TRY(cudaMemset(c->d_status, 0, sizeof(int)));
   *status = h;
   return PYRE_OK;
+}
+
+extern "C" int pyre_argmax_combine(pyre_comm_t* c, const long long* key, int T, int* token, long long* key_out,
+                                   void* stream) {
+  return argmax_combine(c, key, T, token, key_out, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pyre_allreduce_sum_f32(pyre_comm_t* c, float* buf, int64_t n, void* stream) {

@@ -139,5 +139,8 @@ inline DevComm device_view(pyre_comm* c) {
 
 // Launches the two-shot all-reduce of n floats of buf over comm.
 int allreduce_sum_f32(pyre_comm* comm, float* buf, int64_t n, cudaStream_t stream);
+// Launches the cross-rank maximum of T orderable argmax keys (token[t] = its index).
+int argmax_combine(pyre_comm* comm, const long long* key, int T, int* token, long long* key_out,
+                   cudaStream_t stream);
 
 }  // namespace pyre

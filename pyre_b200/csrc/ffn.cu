@@ -110,20 +110,26 @@ extern "C" int pyre_ffn_down_q80(const void* h, int h_dtype, int T, int W, const
   return allreduce_sum_f32(comm, out, static_cast<int64_t>(T) * H, s);
 }
 
-extern "C" int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N,
-                               float* out, void* workspace, int64_t ws_bytes, void* stream) {
+extern "C" int pyre_q80_linear_bias(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype,
+                                    int N, const float* bias, float* out, void* workspace, int64_t ws_bytes,
+                                    void* stream) {
   int rc = ffn_check_common(x, x_dtype, T, K, N, scale_dtype, out, workspace, ws_bytes, "pyre_q80_linear");
   if (rc) return rc;
   PYRE_CHECK_ARG(w != nullptr && reinterpret_cast<uintptr_t>(w) % 16 == 0,
                  "pyre_q80_linear: packed weights must be non-null and 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (T <= PYRE_FUSED_REDUCE_MAX_T)
-    return ffn_stream_down(x, x_dtype, T, K, w, scale_dtype, N, out, workspace, ws_bytes, nullptr, s);
+    return ffn_stream_down(x, x_dtype, T, K, w, scale_dtype, N, out, workspace, ws_bytes, nullptr, s, bias);
   char* wsc = static_cast<char*>(workspace);
   GemmRegion g;
   rc = gemm_region(workspace, ws_bytes, T, K, N, 1, &g, "pyre_q80_linear");
   if (rc) return rc;
   return ffn_gemm_tc(x, x_dtype, T, K, w, 1, EPI_STORE, scale_dtype, N, out, PYRE_F32, g.stage, g.stage_bytes, g.part,
                      g.part_bytes, reinterpret_cast<unsigned int*>(wsc + kHdrCntA),
-                     reinterpret_cast<int*>(wsc + kHdrStatus), s);
+                     reinterpret_cast<int*>(wsc + kHdrStatus), s, bias);
+}
+
+extern "C" int pyre_q80_linear(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N,
+                               float* out, void* workspace, int64_t ws_bytes, void* stream) {
+  return pyre_q80_linear_bias(x, x_dtype, T, K, w, scale_dtype, N, nullptr, out, workspace, ws_bytes, stream);
 }

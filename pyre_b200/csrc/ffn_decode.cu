@@ -165,7 +165,7 @@ int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu,
 }
 
 int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,
-                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s) {
+                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s, const float* bias) {
   using namespace ffn;
   if (ws_bytes < kHeaderBytes + stream_acc_bytes(T, H, 1))
     return set_error(PYRE_ENOMEM, "pyre_ffn_down_q80: workspace smaller than pyre_ffn_workspace_bytes()");
@@ -177,6 +177,7 @@ int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, in
   p.wb = static_cast<const uint8_t*>(wd);
   fill_phase(p, true, W, H, 1);
   p.outB = out;
+  p.biasB = tp ? nullptr : bias;
   p.accB = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
   fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);

@@ -95,7 +95,7 @@ int ffn_decode_check(const void* x, int x_dtype, int T, int H, const void* wgu, 
                      const pyre_comm_t* comm, const char* fn);
 int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
                 void* out, int out_dtype, void* staging, int64_t staging_bytes, void* partial, int64_t partial_bytes,
-                unsigned int* counters, int* status, cudaStream_t s);
+                unsigned int* counters, int* status, cudaStream_t s, const float* bias = nullptr);
 int64_t ffn_gemm_partial_bytes(int T, int N, int nmat);
 // Workspace regions of the T > 4 path after the header: f16 staging of the activations,
 // then the stream-K partial tiles of the GEMM (one per CTA).
@@ -105,6 +105,7 @@ inline int64_t ffn_gemm_staging_bytes(int T, int H, int W) {
 int ffn_stream_gateup(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, int scale_dtype, int W,
                       void* h, int h_dtype, void* workspace, int64_t ws_bytes, cudaStream_t s);
 int ffn_stream_down(const void* h, int h_dtype, int T, int W, const void* wd, int scale_dtype, int H, float* out,
-                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s);
+                    void* workspace, int64_t ws_bytes, pyre_comm_t* comm, cudaStream_t s,
+                    const float* bias = nullptr);
 
 }  // namespace pyre

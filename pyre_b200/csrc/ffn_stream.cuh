@@ -53,6 +53,7 @@ struct alignas(64) StreamParams {
   void* outA;                // [T, NA]: h
   int outA_bf16;
   float* outB;               // [T, NB]
+  const float* biasB;        // MODE_B without tensor parallelism: f32 [NB] added to out, or null
   unsigned long long* accA;  // [tilesA, NMAT_A, T, 256] fixed-point slab sums (zero between calls)
   unsigned long long* accB;  // [tilesB, T, 256]
   unsigned int* cntA;        // [tilesA] finished chunks
@@ -582,8 +583,13 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
                 }
               } else {
                 const int col = job.tile * kTileN + c;
-                if (col < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col] = v[k][0].x;
-                if (col + 1 < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col + 1] = v[k][0].y;
+                float2 r = v[k][0];
+                if (p.biasB != nullptr) {   // x @ W + b: the bias joins the finished dot product
+                  if (col < p.NB) r.x += __ldg(p.biasB + col);
+                  if (col + 1 < p.NB) r.y += __ldg(p.biasB + col + 1);
+                }
+                if (col < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col] = r.x;
+                if (col + 1 < p.NB) p.outB[static_cast<int64_t>(t) * p.NB + col + 1] = r.y;
               }
             }
           }

@@ -74,6 +74,7 @@ struct Params {
   int64_t partial_cap;      // bytes available at partial
   float* partial;           // [CTAs][NMAT, 128 x 256] f32: stream-K partial tile of each CTA
   unsigned int* counters;   // [CTAs] partial-ready flags, zero between calls
+  const float* bias;        // EPI_STORE: f32 [N] added to every row, or null
 };
 
 // Stores 16 consecutive outputs of row t starting at column col0 (bounds-checked on N).
@@ -395,6 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1) q80_gemm_tc_kernel(const __grid_c
             v[q] = acc[0][q];
           }
         }
+        if constexpr (EPI == ffn::EPI_STORE) {
+          // the projection bias, added to the finished f32 dot product (x @ W + b)
+          if (p.bias != nullptr) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (col0 + q < p.N) v[q] += __ldg(p.bias + col0 + q);
+          }
+        }
         store_row16(p, t, col0, v);
       }
       umma::fence_before_sync();
@@ -466,10 +475,10 @@ int64_t ffn_gemm_partial_bytes(int T, int N, int nmat) {
 // Tensor-core GEMM form of the FFN halves for T > 4 (used by ffn.cu).
 //   nmat = 2: out = silu(a @ W0) * (a @ W1) (epi EPI_SILU_MUL); nmat = 1: EPI_SILU or EPI_STORE.
 // a: [T, K] f32, bf16 or f16; f32 and bf16 are converted to f16 in `staging` (>= T*K*2 bytes).
-// out: [T, N] of out_dtype (f32, bf16 or f16).
+// out: [T, N] of out_dtype (f32, bf16 or f16). bias (EPI_STORE only, nullable): f32 [N].
 int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
                 void* out, int out_dtype, void* staging, int64_t staging_bytes, void* partial, int64_t partial_bytes,
-                unsigned int* counters, int* status, cudaStream_t s) {
+                unsigned int* counters, int* status, cudaStream_t s, const float* bias) {
   const void* a_f16 = a;
   if (a_dtype != PYRE_F16) {
     const int64_t n = static_cast<int64_t>(T) * K;
@@ -498,6 +507,7 @@ int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nma
   p.partial = static_cast<float*>(partial);
   p.partial_cap = partial_bytes;
   p.counters = counters;
+  p.bias = epi == ffn::EPI_STORE ? bias : nullptr;
   const bool f16s = scale_dtype == PYRE_F16;
   if (nmat == 2)
     return f16s ? tc::launch<2, ffn::EPI_SILU_MUL, __half>(p, a_f16, s)

@@ -48,7 +48,7 @@ class DecoderLayerDesc(ctypes.Structure):
                 ("ffn_ws", ctypes.c_void_p), ("ffn_ws_bytes", ctypes.c_int64),
                 ("ln1", ctypes.c_void_p), ("ln2", ctypes.c_void_p), ("k_cache", ctypes.c_void_p),
                 ("v_cache", ctypes.c_void_p), ("rope", ctypes.c_void_p), ("attn_ws", ctypes.c_void_p),
-                ("attn_ws_bytes", ctypes.c_int64)]
+                ("attn_ws_bytes", ctypes.c_int64), ("qkv_bias", ctypes.c_void_p)]
 
 
 class DecoderDesc(ctypes.Structure):
@@ -60,7 +60,8 @@ class DecoderDesc(ctypes.Structure):
                 ("lm_head", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("lm_ws", ctypes.c_void_p),
                 ("lm_ws_bytes", ctypes.c_int64)] + \
                [(n, ctypes.c_void_p) for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f", "status", "key",
-                                                "pos_dev", "history")]
+                                                "pos_dev", "history", "comm")] + \
+               [("lm_v0", ctypes.c_int64), ("lm_V", ctypes.c_int)]
 
 
 def check_struct_layout() -> None:
@@ -89,6 +90,11 @@ def _f32(v) -> torch.Tensor:
     return v.detach().float() if isinstance(v, torch.Tensor) else torch.as_tensor(np.asarray(v, dtype=np.float32))
 
 
+def _ffn_dim(lw: dict) -> int:
+    up = lw["ffn"]["up"]
+    return int(up.shape[1])
+
+
 def _vec(v, H, device) -> torch.Tensor:
     t = _f32(v).reshape(-1)
     if t.numel() != H:
@@ -96,21 +102,91 @@ def _vec(v, H, device) -> torch.Tensor:
     return t.to(device).contiguous()
 
 
+def head_split(n_heads: int, n_kv: int, world: int) -> list[tuple]:
+    """Per rank ((q0, q1), (k0, k1)): the reference's head partition of a decode layer
+    (``RootNode._solve_partitions``, src/orchestrator/root_node.py:182-210): n_kv // world kv
+    heads per rank, one more for the first n_kv % world, and the query heads that share them
+    (n_heads // n_kv per kv head), contiguous in rank order."""
+    if n_heads % n_kv:
+        raise ValueError("n_heads must be a multiple of n_kv_heads")
+    if world > n_kv:
+        raise ValueError(f"head-parallel decode needs world <= n_kv_heads ({world} > {n_kv})")
+    per, extra = divmod(n_kv, world)
+    rep = n_heads // n_kv
+    out, k0 = [], 0
+    for r in range(world):
+        k1 = k0 + per + (1 if r < extra else 0)
+        out.append(((k0 * rep, k1 * rep), (k0, k1)))
+        k0 = k1
+    return out
+
+
+def vocab_split(V: int, world: int) -> list[tuple]:
+    """Contiguous lm_head row ranges per rank (V // world, the remainder to the first ranks)."""
+    per, extra = divmod(V, world)
+    out, v0 = [], 0
+    for r in range(world):
+        v1 = v0 + per + (1 if r < extra else 0)
+        out.append((v0, v1))
+        v0 = v1
+    return out
+
+
+def _bias_part(attn: dict, name: str, lo: int, hi: int):
+    b = attn.get(name)
+    if b is None:
+        return None
+    return _f32(b).reshape(-1)[lo:hi]
+
+
 class _Layer:
+    """One decoder layer on this rank: the QKV columns and O rows of its heads (all heads on one
+    GPU), its FFN shard, norms, KV cache and the kernels' scratch."""
+
     def __init__(self, lw: dict, H: int, nq: int, nkv: int, hd: int, max_seq: int, max_prompt: int, theta: float,
-                 frac: float, device):
+                 frac: float, device, heads=None, ffn_range=None, comm=None):
         attn, ffn = lw["attn"], lw["ffn"]
         q, k, v, o = (_q80(attn[n], device) for n in ("q", "k", "v", "o"))
         if q.shape != (H, nq * hd) or k.shape != (H, nkv * hd) or v.shape != (H, nkv * hd) or o.shape != (nq * hd, H):
             raise ValueError("attention weights do not match the head counts")
-        self.qkv = Q80Linear(_concat_n([q, k, v]), max_prompt, device)
+        (q0, q1), (k0, k1) = heads if heads is not None else ((0, nq), (0, nkv))
+        self.nq, self.nkv = q1 - q0, k1 - k0
+        if (q0, q1, k0, k1) != (0, nq, 0, nkv):
+            q, k, v = q.cols(q0 * hd, q1 * hd), k.cols(k0 * hd, k1 * hd), v.cols(k0 * hd, k1 * hd)
+            o = o.rows(q0 * hd, q1 * hd)
+        parts = [_bias_part(attn, "q_bias", q0 * hd, q1 * hd), _bias_part(attn, "k_bias", k0 * hd, k1 * hd),
+                 _bias_part(attn, "v_bias", k0 * hd, k1 * hd)]
+        bias = None
+        if any(b is not None for b in parts):
+            widths = ((q1 - q0) * hd, (k1 - k0) * hd, (k1 - k0) * hd)
+            bias = torch.cat([b if b is not None else torch.zeros(w) for b, w in zip(parts, widths)])
+        self.qkv = Q80Linear(_concat_n([q, k, v]), max_prompt, device, bias=bias)
         self.o = Q80Linear(o, max_prompt, device)
         gate = _q80(ffn["gate"], device) if ffn.get("gate") is not None else None
-        self.ffn_w = FfnWeights.prepare(gate, _q80(ffn["up"], device), _q80(ffn["down"], device))
-        self.ffn = FfnShardOp(H, self.ffn_w.width, max_prompt, gated=gate is not None, device=device)
+        up, down = _q80(ffn["up"], device), _q80(ffn["down"], device)
+        if ffn_range is not None:
+            s0, s1 = ffn_range
+            gate = gate.cols(s0, s1) if gate is not None else None
+            up, down = up.cols(s0, s1), down.rows(s0, s1)
+        self.ffn_w = FfnWeights.prepare(gate, up, down)
+        self.ffn = FfnShardOp(H, self.ffn_w.width, max_prompt, gated=gate is not None, comm=comm, device=device)
+        self.comm = comm
         self.ln1 = _vec(lw["input_layernorm"], H, device)
         self.ln2 = _vec(lw["post_attention_layernorm"], H, device)
-        self.attn = AttentionOp(nq, nkv, hd, max_seq, rope_theta=theta, rope_fraction=frac, device=device)
+        self.attn = AttentionOp(self.nq, self.nkv, hd, max_seq, rope_theta=theta, rope_fraction=frac, device=device)
+
+    def o_proj(self, a: torch.Tensor, stream=None) -> torch.Tensor:
+        """a @ Wo for this rank's heads; with tensor parallelism summed over the ranks (the
+        root's concatenation of every node's head outputs before Wo, root_node.py:851-858)."""
+        if self.comm is None:
+            return self.o(a, stream=stream)
+        T, H = a.shape[0], self.o.n
+        out = torch.empty((T, H), dtype=torch.float32, device=a.device)
+        ws = self.o.workspace
+        N.call("pyre_ffn_down_q80", D.ptr(a), D.dtype_code(a), T, self.o.k, D.ptr(self.o.w.data),
+               self.o.w.scale_code, H, D.ptr(out), D.ptr(ws), ws.numel(), ctypes.c_void_p(self.comm.handle),
+               D.stream_ptr(stream))
+        return out
 
 
 class Generator:
@@ -118,7 +194,13 @@ class Generator:
 
     def __init__(self, layers: list[dict], embedding, final_norm=None, *, n_heads: int, n_kv_heads: int,
                  head_dim: int, rope_theta: float = 10000.0, rope_fraction: float = 1.0, eps: float = 1e-6,
-                 lm_head=None, max_seq: int = 4096, max_prompt: int = 64, device=None):
+                 lm_head=None, max_seq: int = 4096, max_prompt: int = 64, device=None, comm=None, ffn_plan=None):
+        """``comm`` (a :class:`~pyre_b200.tp.TPComm` of hidden size H and at least ``max_prompt``
+        tokens) makes this object one rank of a tensor-parallel decoder: it keeps the heads
+        :func:`head_split` gives its rank (QKV columns, O rows, KV cache), the FFN columns
+        ``ffn_plan`` (a :class:`~pyre_b200.tp.ShardPlan`, default equal 32-blocks) gives it and
+        the lm_head rows of :func:`vocab_split`; every rank is given the same full weights and
+        runs the same calls. Without it the whole model runs on this GPU."""
         D.require_cuda()
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev = self.device
@@ -131,12 +213,27 @@ class Generator:
         fn = None
         if final_norm is not None:
             fn = _f32(final_norm).half().float()
-        self.lm_head = LmHeadOp(table.contiguous(), fn, eps)
+        self.comm = comm
+        rank, world = (comm.rank, comm.world) if comm is not None else (0, 1)
+        self.rank, self.world = rank, world
+        if comm is not None and (comm.hidden != self.H or comm.max_tokens < max_prompt):
+            raise ValueError("the communicator needs hidden = H and max_tokens >= max_prompt")
+        heads = head_split(n_heads, n_kv_heads, world)[rank]
+        ffn_dim = _ffn_dim(layers[0])
+        if ffn_plan is None:
+            from .tp import ShardPlan
+            ffn_plan = ShardPlan.equal(ffn_dim, world)
+        if ffn_plan.ffn_dim != ffn_dim or len(ffn_plan.widths) != world:
+            raise ValueError("ffn_plan does not match the FFN width or the world size")
+        ffn_range = ffn_plan.bounds[rank] if world > 1 else None
+        self.lm_v0, v1 = vocab_split(self.V, world)[rank]
+        self.lm_head = LmHeadOp(table[self.lm_v0:v1].contiguous(), fn, eps, vocab_start=self.lm_v0, comm=comm)
         self.eps = float(eps)
-        self.nq, self.nkv, self.hd = n_heads, n_kv_heads, head_dim
+        self.n_heads, self.n_kv_heads = n_heads, n_kv_heads
+        self.nq, self.nkv, self.hd = heads[0][1] - heads[0][0], heads[1][1] - heads[1][0], head_dim
         self.max_seq, self.max_prompt = int(max_seq), int(max_prompt)
         self.layers = [_Layer(lw, self.H, n_heads, n_kv_heads, head_dim, self.max_seq, self.max_prompt, rope_theta,
-                              rope_fraction, dev) for lw in layers]
+                              rope_fraction, dev, heads=heads, ffn_range=ffn_range, comm=comm) for lw in layers]
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.length = 0
         self._desc = self._native_desc()
@@ -166,7 +263,8 @@ class Generator:
                 L.ffn_w.gateup.data.data_ptr(), L.ffn_w.down.data.data_ptr(), int(L.ffn_w.gated),
                 L.ffn.workspace.data_ptr(), L.ffn.workspace.numel(), L.ln1.data_ptr(), L.ln2.data_ptr(),
                 L.attn.cache.k.data_ptr(), L.attn.cache.v.data_ptr(), L.attn.rope.data_ptr(),
-                L.attn.dec_ws.data_ptr(), L.attn.dec_ws.numel())
+                L.attn.dec_ws.data_ptr(), L.attn.dec_ws.numel(),
+                L.qkv.bias.data_ptr() if L.qkv.bias is not None else None)
         self._layer_arr = arr
         lm = self.lm_head
         d = DecoderDesc(len(self.layers), H, self.nq, self.nkv, self.hd, widths.pop(), self.V, self.max_seq,
@@ -175,7 +273,8 @@ class Generator:
                         lm.table.data_ptr(), lm.norm.data_ptr() if lm.norm is not None else None,
                         lm.workspace.data_ptr(), lm.workspace.numel(),
                         *(self._buf[n].data_ptr() for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f")),
-                        self.status.data_ptr(), self._key.data_ptr())
+                        self.status.data_ptr(), self._key.data_ptr(), None, None,
+                        self.comm.handle if self.comm is not None else None, self.lm_v0, lm.V)
         return d
 
     # ---- one pass of the decoder over T new tokens ------------------------------------------
@@ -195,7 +294,7 @@ class Generator:
             qkv = L.qkv(xn, stream=stream)
             q, k, v = qkv[:, :nq_w], qkv[:, nq_w:nq_w + nkv_w], qkv[:, nq_w + nkv_w:]
             a = L.attn.prefill(q, k, v, stream=stream) if prefill else L.attn.decode(q, k, v, stream=stream)
-            ao = L.o(a, stream=stream)
+            ao = L.o_proj(a, stream=stream)
             N.call("pyre_add_rms_norm", D.ptr(x), D.ptr(ao), T, H, D.ptr(L.ln2), self.eps, D.ptr(x), D.ptr(hn), s)
             f = L.ffn.run(hn, L.ffn_w, stream=stream)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
@@ -284,7 +383,7 @@ class Generator:
         scratch = torch.empty(1, dtype=torch.int32, device=self.device)
         for i in range(1, int(ids.size) - 1):
             self.step_into(dev_ids[i:i + 1], scratch, stream=stream)
-        logits = torch.empty((1, self.V), dtype=torch.float32, device=self.device) if want_logits else None
+        logits = torch.empty((1, self.lm_head.V), dtype=torch.float32, device=self.device) if want_logits else None
         self.step_into(dev_ids[-1:], scratch, logits[0] if want_logits else None, stream=stream)
         tok = scratch.to(torch.int64).view(1, 1)
         return (tok, logits) if want_logits else tok
@@ -313,8 +412,8 @@ class Generator:
         for t in (token_in, token_out):
             if t.dtype != torch.int32 or not t.is_cuda:
                 raise ValueError("tokens must be int32 on the device")
-        if logits is not None and (logits.dtype != torch.float32 or logits.numel() != self.V):
-            raise ValueError(f"logits must be f32 with {self.V} elements")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() != self.lm_head.V):
+            raise ValueError(f"logits must be f32 with {self.lm_head.V} elements (this rank's vocabulary rows)")
         N.call("pyre_decoder_step", ctypes.byref(self._desc), D.ptr(token_in), self.length, 0, 0, D.ptr(token_out),
                D.ptr(logits), D.stream_ptr(stream))
         self.length += 1
@@ -389,6 +488,8 @@ class Generator:
         for L in self.layers:
             for ws in (L.qkv.workspace, L.o.workspace, L.ffn.workspace):
                 words.append(ws[8:12].view(torch.int32)[0])
+        if self.comm is not None:
+            self.comm.check()          # raises PyreTimeout if a wait on a peer ran out
         vals = torch.stack(words).cpu().tolist()
         if vals[0] != 0:
             raise RuntimeError(f"embedding gather saw a token id outside [0, {self.V})")
@@ -402,7 +503,8 @@ class Generator:
         tokenizer and EOS stop), as a list of ints; with want_logits also the f32 logits of
         every step, [max_tokens, V] on the device. native: decode steps through
         pyre_decoder_step (else op by op from Python); stepwise_prefill: see :meth:`prefill`;
-        graphed: decode steps as CUDA-graph replays (:meth:`decode_graphed`, no logits)."""
+        graphed: decode steps as CUDA-graph replays (:meth:`decode_graphed`, no logits). With
+        tensor parallelism the logits are this rank's vocabulary rows (lm_v0 onwards)."""
         if max_tokens < 1 or max_tokens > self.max_seq + 1:
             raise ValueError("max_tokens out of range")
         if graphed and want_logits:
@@ -415,7 +517,8 @@ class Generator:
             hist = self.decode_graphed(tok, max_tokens - 1)
             self.check_status()
             return hist[start:start + max_tokens].cpu().tolist()
-        logits = torch.empty((max_tokens, self.V), dtype=torch.float32, device=self.device) if want_logits else None
+        logits = torch.empty((max_tokens, self.lm_head.V), dtype=torch.float32, device=self.device) \
+            if want_logits else None
         if want_logits:
             logits[0].copy_(lg0[0])
         toks = self.tokens

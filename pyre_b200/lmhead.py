@@ -4,8 +4,10 @@ Mirrors ``Generator._rms_norm`` / ``_compute_logits`` / ``_sample(temperature < 
 (src/orchestrator/generator.py:40-53), whose table is stored as f16 (``generator.py:32``).
 One launch of ``lm_head_kernel`` streams the table once. With the table sharded by
 vocabulary over the ranks of a process group (rank r holds rows ``vocab_start ..
-vocab_start + V_r - 1``), each rank's best (value, index) key is combined with one max
-all-reduce of T int64 values.
+vocab_start + V_r - 1``), each rank's best (value, index) key is combined across the ranks:
+through the peer-memory communicator (``pyre_argmax_combine``, one small launch) when a
+:class:`~pyre_b200.tp.TPComm` is given, or with one max all-reduce of T int64 values over a
+``torch.distributed`` group.
 """
 from __future__ import annotations
 
@@ -21,7 +23,7 @@ _KEY_TOP = -(1 << 63)
 
 class LmHeadOp:
     def __init__(self, lm_head: torch.Tensor, norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
-                 vocab_start: int = 0, group=None, max_tokens: int = 1):
+                 vocab_start: int = 0, group=None, max_tokens: int = 1, comm=None):
         if lm_head.dtype != torch.float16 or lm_head.dim() != 2 or not lm_head.is_cuda:
             raise ValueError("lm_head must be a CUDA f16 tensor [V, H]")
         if not 1 <= max_tokens <= 4:
@@ -34,6 +36,9 @@ class LmHeadOp:
         self.eps = float(eps)
         self.v0 = int(vocab_start)
         self.group = group
+        self.comm = comm if (comm is not None and comm.world > 1) else None
+        if self.comm is not None and group is not None:
+            raise ValueError("give either a communicator or a process group")
         self.max_tokens = max_tokens
         b = ctypes.c_int64(0)
         N.call("pyre_lm_head_workspace_bytes", max_tokens, ctypes.byref(b))
@@ -56,7 +61,11 @@ class LmHeadOp:
         N.call("pyre_lm_head_argmax", D.ptr(h), T, self.H, D.ptr(self.norm) if self.norm is not None else None,
                self.eps, D.ptr(self.table), self.V, self.v0, D.ptr(logits) if logits is not None else None,
                D.ptr(token), D.ptr(key), D.ptr(self.workspace), self.workspace.numel(), D.stream_ptr(stream))
-        if self.group is not None:
+        if self.comm is not None:
+            N.call("pyre_argmax_combine", ctypes.c_void_p(self.comm.handle), D.ptr(key), T, D.ptr(token), None,
+                   D.stream_ptr(stream))
+            tok = token.to(torch.int64)
+        elif self.group is not None:
             import torch.distributed as dist
             dist.all_reduce(key, op=dist.ReduceOp.MAX, group=self.group)
             low = (key ^ _KEY_TOP) & 0xFFFFFFFF

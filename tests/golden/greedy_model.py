@@ -1,21 +1,80 @@
-"""Seeded SmolLM-135M-shaped Llama decoder (hidden 576, 30 layers, 9 q / 3 kv heads, head_dim
-64, gated-SiLU 1536, vocab 49152, tied embeddings, RoPE theta 1e4) for the greedy-token parity
-test. Shared by tests/golden/make_golden.py (which runs the reference orchestrator on these
-weights) and tests/test_greedy_gpu.py (which runs this repository's kernels on them).
+"""Seeded Llama-style decoders for the greedy-token parity tests.
 
-Weights: N(0, std) f32 (std 0.02, and 0.07 for a second fixture) from numpy seed 0 in a fixed order, rounded to bf16 (the loader's
-cast), then Q8_0 with the f16-stored scale (the device format), given to both sides as the
-f32 dequantized matrices; RMSNorm weights are ones. Prompt: 8 token ids from
-np.random.default_rng(0).integers(0, 49152, 8)."""
+Shared by tests/golden/make_golden.py (which runs the reference orchestrator on these weights)
+and the tests (which run the oracle and this repository's kernels on them). Each model is a
+stand-in of one configured shape, built from a numpy seed in a fixed order:
+
+* the embedding table: N(0, 0.02) f32, rounded to bf16 (the loader's cast), stored f16;
+* per layer: q, k, v, o, gate, up, down ([in, out], N(0, std) f32 rounded to bf16, then Q8_0
+  with the f16-stored scale of the device format, given to both sides as the f32 dequantized
+  matrices); with qkv_bias also q_bias, k_bias, v_bias (N(0, 0.02) f32); RMSNorm weights ones;
+* an untied lm_head (N(0, 0.02) bf16 -> f16) after the layers when tied is False;
+* the prompt: prompt_len ids from np.random.default_rng(prompt_seed).integers(0, vocab).
+
+Models (the first two are the SmolLM-135M shape of the correctness config; the others are
+reduced-layer stand-ins of the Qwen2.5-0.5B and Mistral-7B shapes with their full widths,
+heads, vocabularies and RoPE bases, and prompts long enough that the prefill runs on the
+tensor-core path):
+
+* smollm135m_std002  30 layers, projections N(0, 0.02): the configured model. The random stack
+                     maps every context to nearly one hidden state; all 32 tokens are one id.
+* smollm135m_std007  the same with N(0, 0.07): 32 different tokens, but reference top-1/top-2
+                     margins down to 4.1e-3, below the error that f16 KV storage alone causes.
+* qwen05b_l4         hidden 896, 4 layers, 14/2 heads, hd 64, QKV bias, FFN 4864, vocab 151936
+                     tied, theta 1e6; projections N(0, 0.02), seed 2, 512-token prompt (seed 2).
+                     Smallest reference margin 6.7e-3, six times the logit error (1.1e-3) of an
+                     f32 CPU emulation of the device path's f16 roundings.
+* mistral7b_l2       hidden 4096, 2 layers, 32/8 heads, hd 128, FFN 14336, vocab 32768 with an
+                     untied lm_head, theta 1e6; projections N(0, 0.02), seed 3, 512-token prompt.
+                     Prompt seed 5: the first from 3 whose reference run keeps every top-1/top-2
+                     margin above 1.5e-2 (seeds 3 and 4: 5.3e-3 and 8.0e-3, about the 4e-3 to 6e-3
+                     logit error the emulation gives on this wide model), so that the 32 tokens
+                     are decidable at the device path's precision.
+"""
 from __future__ import annotations
+
+from dataclasses import dataclass, replace
 
 import numpy as np
 
-CFG = dict(hidden=576, layers=30, n_heads=9, n_kv=3, head_dim=64, ffn=1536, vocab=49152, theta=10000.0, eps=1e-6)
 N_GREEDY = 32
-# With N(0, 0.02) projections the random 30-layer stack maps every context to nearly the same
-# last hidden state and greedy decoding repeats one token; with N(0, 0.07) the 32 tokens all differ,
-# which makes the token-by-token comparison a real test. Both are fixtures.
+
+
+@dataclass(frozen=True)
+class Model:
+    name: str
+    fixture: str
+    hidden: int
+    layers: int
+    n_heads: int
+    n_kv: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    theta: float
+    std: float
+    seed: int
+    prompt_len: int
+    prompt_seed: int
+    tied: bool = True
+    qkv_bias: bool = False
+    eps: float = 1e-6
+
+
+_SMOL = dict(hidden=576, layers=30, n_heads=9, n_kv=3, head_dim=64, ffn=1536, vocab=49152, theta=10000.0, seed=0,
+             prompt_len=8, prompt_seed=0)
+MODELS = {m.name: m for m in (
+    Model("smollm135m_std002", "greedy_golden.npz", std=0.02, **_SMOL),
+    Model("smollm135m_std007", "greedy_golden_std07.npz", std=0.07, **_SMOL),
+    Model("qwen05b_l4", "greedy_golden_qwen05b_l4.npz", hidden=896, layers=4, n_heads=14, n_kv=2, head_dim=64,
+          ffn=4864, vocab=151936, theta=1e6, std=0.02, seed=2, prompt_len=512, prompt_seed=2, qkv_bias=True),
+    Model("mistral7b_l2", "greedy_golden_mistral7b_l2.npz", hidden=4096, layers=2, n_heads=32, n_kv=8,
+          head_dim=128, ffn=14336, vocab=32768, theta=1e6, std=0.02, seed=3, prompt_len=512, prompt_seed=5,
+          tied=False),
+)}
+
+# the configured SmolLM-shaped model (kept for callers of the original single-model API)
+CFG = dict(hidden=576, layers=30, n_heads=9, n_kv=3, head_dim=64, ffn=1536, vocab=49152, theta=10000.0, eps=1e-6)
 GOLDENS = {"greedy_golden.npz": 0.02, "greedy_golden_std07.npz": 0.07}
 
 
@@ -25,26 +84,39 @@ def _bf16(a: np.ndarray) -> np.ndarray:
     return r.astype(np.uint32).view(np.float32)
 
 
-def prompt_ids() -> np.ndarray:
-    return np.random.default_rng(0).integers(0, CFG["vocab"], 8)
+def prompt_ids(m: Model | None = None) -> np.ndarray:
+    m = m or MODELS["smollm135m_std002"]
+    return np.random.default_rng(m.prompt_seed).integers(0, m.vocab, m.prompt_len)
 
 
-def make_weights(q80_roundtrip, std: float = 0.02):
-    """q80_roundtrip(w f32) -> f32 dequantized Q8_0 with f16 scales. Returns
-    (embedding f16 [V, H], layers: list of dicts of f32 matrices, final_norm f32 [H]). std is
-    the projection weights' standard deviation (the embedding keeps 0.02)."""
-    H, L, nq, nkv, hd, I, V = (CFG[k] for k in ("hidden", "layers", "n_heads", "n_kv", "head_dim", "ffn", "vocab"))
-    rng = np.random.default_rng(0)
+def build(m: Model, q80_roundtrip):
+    """q80_roundtrip(w f32) -> f32 dequantized Q8_0 with f16 scales, called once per matrix in
+    generation order. Returns (embedding f16 [V, H], layers: list of dicts of f32 arrays,
+    final_norm f32 [H], lm_head f16 [V, H] or None when tied)."""
+    H, nq, nkv, hd, I, V = m.hidden, m.n_heads, m.n_kv, m.head_dim, m.ffn, m.vocab
+    rng = np.random.default_rng(m.seed)
 
     def w(shape):
-        return q80_roundtrip(_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std)))
+        return q80_roundtrip(_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(m.std)))
 
     emb = _bf16(rng.standard_normal((V, H), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
     layers = []
-    for _ in range(L):
-        layers.append({
-            "q": w((H, nq * hd)), "k": w((H, nkv * hd)), "v": w((H, nkv * hd)), "o": w((nq * hd, H)),
-            "gate": w((H, I)), "up": w((H, I)), "down": w((I, H)),
-            "ln1": np.ones(H, np.float32), "ln2": np.ones(H, np.float32),
-        })
-    return emb, layers, np.ones(H, np.float32)
+    for _ in range(m.layers):
+        lw = {"q": w((H, nq * hd)), "k": w((H, nkv * hd)), "v": w((H, nkv * hd)), "o": w((nq * hd, H)),
+              "gate": w((H, I)), "up": w((H, I)), "down": w((I, H)),
+              "ln1": np.ones(H, np.float32), "ln2": np.ones(H, np.float32)}
+        if m.qkv_bias:
+            for n, width in (("q_bias", nq * hd), ("k_bias", nkv * hd), ("v_bias", nkv * hd)):
+                lw[n] = rng.standard_normal(width, dtype=np.float32) * np.float32(0.02)
+        layers.append(lw)
+    head = None
+    if not m.tied:
+        head = _bf16(rng.standard_normal((V, H), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    return emb, layers, np.ones(H, np.float32), head
+
+
+def make_weights(q80_roundtrip, std: float = 0.02):
+    """The SmolLM-shaped model with projection std ``std`` (the original single-model API):
+    (embedding f16 [V, H], layers, final_norm f32 [H])."""
+    emb, layers, fn, _ = build(replace(MODELS["smollm135m_std002"], std=std), q80_roundtrip)
+    return emb, layers, fn

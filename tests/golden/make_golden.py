@@ -29,8 +29,9 @@ Run in a container that has the reference checkout (read-only) at /root/referenc
                          final RMSNorm, logits against the f16 lm_head table, greedy token,
                          including rows with tied maxima.
 * greedy_golden*.npz   — the reference orchestrator's greedy decode (RootNode + Generator
-                         loop) of 32 tokens on the seeded SmolLM-shaped models of
-                         tests/golden/greedy_model.py (projections N(0, 0.02) and N(0, 0.07)).
+                         loop) of 32 tokens on the seeded models of tests/golden/greedy_model.py:
+                         the SmolLM-135M shape (projections N(0, 0.02) and N(0, 0.07)) and the
+                         reduced-layer Qwen2.5-0.5B (QKV bias) and Mistral-7B shapes.
 
 Only this script touches /root/reference; tests read the fixtures.
 """
@@ -318,57 +319,64 @@ def make_lmhead() -> None:
     print("lmhead_golden.npz written")
 
 
-def make_greedy(quantizer) -> None:
+def make_greedy(quantizer, only: str | None = None) -> None:
     """The reference orchestrator (RootNode with no workers: head-partitioned, all heads at the
     root, src/orchestrator/root_node.py:344-380, :699-1007) and Generator's prefill / greedy
-    loop (generator.py:73-145, padded prompt of 64, masked padding) on the seeded models of
-    greedy_model.py, with the Mojo kernels replaced by the numpy restatement and the MAX
-    engine by the numpy stand-in. The root's weights are the f32 dequantized Q8_0 matrices,
-    as a reference worker uses them (worker_node.py:59-69), instead of its f16 cache."""
+    loop (generator.py:73-145, the prompt padded to max(64, prompt length), padding masked) on
+    the seeded models of greedy_model.py, with the Mojo kernels replaced by the numpy
+    restatement and the MAX engine by the numpy stand-in. The root's weights are the f32
+    dequantized Q8_0 matrices, as a reference worker uses them (worker_node.py:59-69), instead
+    of its f16 cache; QKV biases are handed over as the root's q_bias / k_bias / v_bias."""
     import types
     import src.orchestrator.root_node as rn
     from src.orchestrator.cluster import ModelConfig
     from src.orchestrator.generator import Generator
     sys.path.insert(0, str(HERE))
     import greedy_model as gm
-    C = gm.CFG
 
     def roundtrip(a):
         q, s, shape = quantizer.quantize_q80(a)
         s16 = s.astype(np.float16).astype(np.float32)
         return quantizer.dequantize_q80(q, s16, shape).astype(np.float32)
 
+    import max.engine
+    max.engine.ANY_SEQ_LEN = True       # prompts beyond the reference's fixed 64-token graph
     rn._PYRE_KERNELS = _KernelShim()
-    cfg = ModelConfig(hidden_dim=C["hidden"], n_heads=C["n_heads"], n_kv_heads=C["n_kv"], head_dim=C["head_dim"],
-                      ffn_dim=C["ffn"], num_layers=C["layers"], vocab_size=C["vocab"], rope_theta=C["theta"])
-    props = types.SimpleNamespace(head_dim=C["head_dim"], has_v_proj=True, rope_fraction=1.0, use_v_norm=False,
-                                  attention_type="full", kv_source_layer=None)
-    wp = types.SimpleNamespace(get_layer_props=lambda i: props)
-    for fname, std in gm.GOLDENS.items():
-        emb, layers, final_norm = gm.make_weights(roundtrip, std)
-        root = rn.RootNode([], cfg, weight_provider=wp, num_layers=C["layers"])
-        _greedy_run(root, Generator, gm, emb, layers, final_norm, HERE / fname)
+    for m in gm.MODELS.values():
+        if only is not None and m.name != only:
+            continue
+        cfg = ModelConfig(hidden_dim=m.hidden, n_heads=m.n_heads, n_kv_heads=m.n_kv, head_dim=m.head_dim,
+                          ffn_dim=m.ffn, num_layers=m.layers, vocab_size=m.vocab, rope_theta=m.theta)
+        props = types.SimpleNamespace(head_dim=m.head_dim, has_v_proj=True, rope_fraction=1.0, use_v_norm=False,
+                                      attention_type="full", kv_source_layer=None)
+        wp = types.SimpleNamespace(get_layer_props=lambda i, props=props: props)
+        emb, layers, final_norm, head = gm.build(m, roundtrip)
+        root = rn.RootNode([], cfg, weight_provider=wp, num_layers=m.layers)
+        _greedy_run(root, Generator, gm, m, emb, layers, final_norm, head, HERE / m.fixture)
 
 
-def _greedy_run(root, Generator, gm, emb, layers, final_norm, path) -> None:
-    C = gm.CFG
-
+def _greedy_run(root, Generator, gm, m, emb, layers, final_norm, head, path) -> None:
     def root_weights(i):
         lw = layers[i]
-        return {"input_layernorm": lw["ln1"], "post_attention_layernorm": lw["ln2"],
-                "attn": {"q": lw["q"], "k": lw["k"], "v": lw["v"], "o": lw["o"]},
+        attn = {"q": lw["q"], "k": lw["k"], "v": lw["v"], "o": lw["o"]}
+        for n in ("q_bias", "k_bias", "v_bias"):
+            if n in lw:
+                attn[n] = lw[n]
+        return {"input_layernorm": lw["ln1"], "post_attention_layernorm": lw["ln2"], "attn": attn,
                 "ffn": {"gate": lw["gate"], "up": lw["up"], "down": lw["down"]},
-                "_props": {"head_dim": C["head_dim"], "has_v_proj": True, "rope_fraction": 1.0,
+                "_props": {"head_dim": m.head_dim, "has_v_proj": True, "rope_fraction": 1.0,
                            "use_v_norm": False, "attention_type": "full", "kv_source_layer": None}}
     root._get_root_layer_weights = root_weights
-    gen = Generator(root, None, lm_head=emb, embedding=emb, seq_len=64, final_norm=final_norm)
-    ids = gm.prompt_ids()
+    ids = gm.prompt_ids(m)
     true_len = len(ids)
-    input_ids = np.zeros((1, 64), dtype=np.int32)
+    seq_len = max(64, true_len)
+    gen = Generator(root, None, lm_head=emb if head is None else head, embedding=emb, seq_len=seq_len,
+                    final_norm=final_norm)
+    input_ids = np.zeros((1, seq_len), dtype=np.int32)
     input_ids[0, :true_len] = ids
     kv = {}
     hs = root.run(gen._embed(input_ids), kv_cache=kv, prefill=True)
-    kv["_pos"], kv["_prefill_len"], kv["_prefill_max_seq"] = true_len, true_len, 64
+    kv["_pos"], kv["_prefill_len"], kv["_prefill_max_seq"] = true_len, true_len, seq_len
     logits = gen._compute_logits(hs)[:, true_len - 1, :]
     first_logits = logits[0].astype(np.float32)
     tokens, top_idx, top_val = [], [], []
@@ -381,16 +389,17 @@ def _greedy_run(root, Generator, gm, emb, layers, final_norm, path) -> None:
         order = np.argsort(-logits[0], kind="stable")[:8]
         top_idx.append(order)
         top_val.append(logits[0][order].astype(np.float32))
+    top_val = np.array(top_val, np.float32)
     np.savez_compressed(path, prompt=ids.astype(np.int64), tokens=np.array(tokens, np.int64),
-                        first_logits=first_logits, top_idx=np.array(top_idx, np.int64),
-                        top_val=np.array(top_val, np.float32))
-    print(path.name, "written:", tokens)
+                        first_logits=first_logits, top_idx=np.array(top_idx, np.int64), top_val=top_val)
+    print(path.name, "written:", tokens, "smallest top-1/top-2 margin %.4g" % (top_val[:, 0] - top_val[:, 1]).min())
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", default=None, help="write one fixture: lmhead or greedy (default: all)")
+    ap.add_argument("--only", default=None,
+                    help="write one fixture: lmhead, greedy (every greedy model) or greedy:<model name>")
     args = ap.parse_args()
     ref = Path(args.ref)
     sys.path.insert(0, str(HERE / "max_shim"))
@@ -398,8 +407,9 @@ def main() -> None:
     if args.only == "lmhead":
         make_lmhead()
         return
-    if args.only == "greedy":
-        make_greedy(_load_module(ref / "src" / "orchestrator" / "quantizer.py", "ref_quantizer"))
+    if args.only is not None and args.only.startswith("greedy"):
+        name = args.only.split(":", 1)[1] if ":" in args.only else None
+        make_greedy(_load_module(ref / "src" / "orchestrator" / "quantizer.py", "ref_quantizer"), name)
         return
     quantizer = _load_module(ref / "src" / "orchestrator" / "quantizer.py", "ref_quantizer")
     make_q80(quantizer)

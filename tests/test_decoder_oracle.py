@@ -28,3 +28,19 @@ def test_oracle_decoder_equals_reference_goldens(name, std):
     np.testing.assert_allclose(logits[0], g["first_logits"], rtol=0, atol=1e-4)
     for step in range(gm.N_GREEDY):
         np.testing.assert_allclose(logits[step][g["top_idx"][step]], g["top_val"][step], rtol=0, atol=1e-4)
+
+
+@pytest.mark.parametrize("name,steps", [("qwen05b_l4", 8), ("mistral7b_l2", 4)])
+def test_oracle_decoder_equals_reference_wide_models(name, steps):
+    """The reduced-layer Qwen2.5-0.5B-shaped (QKV bias, tied 151936 vocabulary) and Mistral-7B-
+    shaped (untied lm_head) models with 512-token prompts: the oracle's first greedy steps equal
+    the reference's tokens and top-8 logits (the first steps keep the CPU time bounded)."""
+    m = gm.MODELS[name]
+    g = np.load(HERE / "golden" / m.fixture)
+    emb, layers, final_norm, head = gm.build(m, lambda a: q80_roundtrip(a, np.float16))
+    ids, logits = OD.greedy(emb, layers, final_norm, g["prompt"], steps, m.n_heads, m.n_kv, m.head_dim, m.theta,
+                            m.eps, lm_head_f16=head)
+    assert ids == g["tokens"][:steps].tolist()
+    np.testing.assert_allclose(logits[0], g["first_logits"], rtol=0, atol=1e-4)
+    for step in range(steps):
+        np.testing.assert_allclose(logits[step][g["top_idx"][step]], g["top_val"][step], rtol=0, atol=1e-4)

@@ -1,124 +1,52 @@
-"""Greedy-token parity with the reference on the seeded SmolLM-135M-shaped model.
+"""Greedy-token parity with the reference on the seeded models of tests/golden/greedy_model.py.
 
 tests/golden/greedy_golden*.npz hold the reference orchestrator's own runs (RootNode's
 head-partitioned layers + Generator's prefill and greedy loop, src/orchestrator/
-root_node.py:344-1007, generator.py:73-145) on the weights of tests/golden/greedy_model.py
-(projections N(0, 0.02), the configured model, and N(0, 0.07), whose greedy tokens all differ):
-the 8-token prompt, the 32 greedy token ids, the logits of the first step and the top-8
-logits (ids and values) of every step. This runs the same model on this library's kernels
-(pyre_b200.generator.Generator) and asks for the same 32 ids, and for every step's top-8
-logits and the whole first-step logit vector within LOGIT_ATOL (device differences: f16 KV
-cache, f16 operands in the tensor-core prefill, other summation orders).
+root_node.py:344-1007, generator.py:73-145): the prompt, the 32 greedy token ids, the logits
+of the first step and the top-8 logits (ids and values) of every step. This runs the same
+models on this library's kernels (pyre_b200.generator.Generator) through the default path —
+the prompt as one pass (tensor-core GEMMs and attention for prompts longer than 4 tokens), then
+the decode steps — and asks for the same 32 ids, and for every step's top-8 logits and the whole
+first-step logit vector within LOGIT_ATOL (device differences: f16 KV cache, f16 operands in the
+tensor-core prefill, other summation orders).
+
+Models: SmolLM-135M shape (8-token prompt, projections N(0, 0.02)), reduced-layer Qwen2.5-0.5B
+shape (QKV bias, 512-token prompt), reduced-layer Mistral-7B shape (untied lm_head, 512-token
+prompt). The SmolLM-shaped N(0, 0.07) model is a separate case: its reference top-1/top-2 margin
+at step 22 is 6.3e-3, below the logit error that storing K and V in f16 causes on its own
+(7.7e-3 in an f32 CPU emulation with exact projections; the reference keeps f32), so whether
+that step's token matches depends on rounding luck in either prefill form. That model runs
+stepwise (every prompt token through the decode kernels) with all 32 tokens compared, and
+through the default path teacher-forced (the reference's tokens fed back) with every step's
+logits compared and the token compared at every step whose reference margin exceeds twice the
+logit tolerance.
 """
 from __future__ import annotations
-
-import sys
-from pathlib import Path
 
 import numpy as np
 import pytest
 
-HERE = Path(__file__).resolve().parent
-sys.path.insert(0, str(HERE / "golden"))
-
-import greedy_model as gm  # noqa: E402
-
-from oracle.q80 import dequantize_q80, quantize_q80  # noqa: E402
+import greedy_device as G
+from greedy_device import gm
 
 LOGIT_ATOL = 2e-2
+DECIDABLE = [m.name for m in gm.MODELS.values() if m.name != "smollm135m_std007"]
 
 
-GOLDENS = sorted(gm.GOLDENS.items())
+def test_golden_prompts_are_the_seeded_prompts():
+    for m in gm.MODELS.values():
+        g = G.golden(m)
+        assert np.array_equal(g["prompt"], gm.prompt_ids(m)), m.name
+        assert g["tokens"].shape == (gm.N_GREEDY,)
+        assert g["top_idx"].shape == (gm.N_GREEDY, 8) and np.array_equal(g["top_idx"][:, 0], g["tokens"])
 
 
-def _golden(name):
-    return np.load(HERE / "golden" / name)
-
-
-def _weights(std):
-    """The model's weights as this library's Q8_0 matrices (the exact q and f16 scales whose
-    dequantized values the reference ran on) plus the f16 embedding and final norm."""
+def _gen(name):
     import torch
-    from pyre_b200.quantizer import Q80Weight
-
-    rec = []
-
-    def roundtrip(a):
-        q, s, shape = quantize_q80(a)
-        s16 = s.astype(np.float16)
-        rec.append((q.reshape(shape), s16.reshape(shape[0], shape[1] // 32)))
-        return dequantize_q80(q, s16.astype(np.float32), shape)
-
-    emb, layers, final_norm = gm.make_weights(roundtrip, std)
-    names = ("q", "k", "v", "o", "gate", "up", "down")
-    assert len(rec) == len(names) * len(layers)
-    dev = torch.device("cuda", 0)
-    out = []
-    for i, lw in enumerate(layers):
-        w = {n: Q80Weight(torch.from_numpy(rec[i * 7 + j][0]).to(dev), torch.from_numpy(rec[i * 7 + j][1]).to(dev))
-             for j, n in enumerate(names)}
-        out.append({"input_layernorm": lw["ln1"], "post_attention_layernorm": lw["ln2"],
-                    "attn": {n: w[n] for n in ("q", "k", "v", "o")},
-                    "ffn": {n: w[n] for n in ("gate", "up", "down")}})
-    return emb, out, final_norm
+    return G.generator(gm.MODELS[name], torch.device("cuda", 0))
 
 
-@pytest.mark.parametrize("name,std", GOLDENS)
-def test_golden_prompt_is_the_seeded_prompt(name, std):
-    g = _golden(name)
-    assert np.array_equal(g["prompt"], gm.prompt_ids())
-    assert g["tokens"].shape == (gm.N_GREEDY,)
-    assert g["top_idx"].shape == (gm.N_GREEDY, 8) and np.array_equal(g["top_idx"][:, 0], g["tokens"])
-
-
-# (golden, projection std, decode steps through pyre_decoder_step, prompt fed stepwise).
-# The N(0, 0.02) model (the configured one) runs its 8-token prompt as one tensor-core pass
-# (f16 operands) and still matches all 32 tokens (measured top-8 logit error 1.8e-3 against a
-# smallest top-1/top-2 margin of 3.4e-3). On the N(0, 0.07) model small differences grow over
-# the 30 layers and its reference margins go down to 4.1e-3, below the f16 prefill's error
-# there (1.0e-2), so it feeds the prompt through the decode kernels (f32 projections and
-# FFN, f16 KV cache): measured top-8 error 7.4e-3 and all 32 tokens equal.
-CASES = [("greedy_golden.npz", 0.02, True, False), ("greedy_golden.npz", 0.02, False, False),
-         ("greedy_golden.npz", 0.02, True, True), ("greedy_golden_std07.npz", 0.07, True, True),
-         ("greedy_golden_std07.npz", 0.07, False, True)]
-
-
-def _generator(std):
-    import torch
-    from pyre_b200.generator import Generator
-    emb, layers, final_norm = _weights(std)
-    C = gm.CFG
-    return Generator(layers, emb, final_norm, n_heads=C["n_heads"], n_kv_heads=C["n_kv"], head_dim=C["head_dim"],
-                     rope_theta=C["theta"], eps=C["eps"], max_seq=128, max_prompt=64, device=torch.device("cuda", 0))
-
-
-@pytest.mark.gpu
-@pytest.mark.parametrize("name,std,stepwise", [("greedy_golden.npz", 0.02, False), ("greedy_golden_std07.npz", 0.07, True)])
-def test_greedy_tokens_graphed_decode(name, std, stepwise):
-    """Decode steps replayed from captured CUDA graphs (position read and advanced on the
-    device), with graphs of 5 steps over 16-position buckets so that the run crosses bucket
-    boundaries and replans the attention grid: the same 32 tokens, twice in a row (the
-    second run replays the cached graphs)."""
-    g = _golden(name)
-    gen = _generator(std)
-    for _ in range(2):
-        ids = gen.generate_ids(g["prompt"], gm.N_GREEDY, stepwise_prefill=stepwise, graphed=True)
-        assert ids == g["tokens"].tolist()
-    tok = gen.prefill(g["prompt"], stepwise=stepwise)
-    hist = gen.decode_graphed(tok, gm.N_GREEDY - 1, steps_per_graph=5, bucket=16)
-    n0 = len(g["prompt"])
-    assert hist[n0:n0 + gm.N_GREEDY].cpu().tolist() == g["tokens"].tolist()
-
-
-@pytest.mark.gpu
-@pytest.mark.parametrize("name,std,native,stepwise", CASES)
-def test_greedy_tokens_match_reference(name, std, native, stepwise):
-    g = _golden(name)
-    gen = _generator(std)
-    ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=native,
-                                   stepwise_prefill=stepwise)
-    lg = logits.cpu().numpy()
-    # logits first: a mismatch there says where the tokens would start to differ
+def _check_run(g, ids, lg):
     d0 = np.abs(lg[0] - g["first_logits"]).max()
     assert d0 <= LOGIT_ATOL, f"first-step logits differ by {d0}"
     n_match = 0
@@ -126,7 +54,74 @@ def test_greedy_tokens_match_reference(name, std, native, stepwise):
         if ids[step] != int(g["tokens"][step]):
             break
         n_match += 1
-        got = lg[step][g["top_idx"][step]]
-        err = np.abs(got - g["top_val"][step]).max()
+        err = np.abs(lg[step][g["top_idx"][step]] - g["top_val"][step]).max()
         assert err <= LOGIT_ATOL, f"step {step}: top-8 logits differ by {err}"
     assert n_match == gm.N_GREEDY, f"tokens diverge at step {n_match}: {ids} vs {g['tokens'].tolist()}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", DECIDABLE)
+@pytest.mark.parametrize("native", [True, False], ids=["decoder_step", "op_by_op"])
+def test_greedy_tokens_match_reference(name, native):
+    """Default path: one-pass prefill, then decode steps (one native call per token, or op by
+    op from Python), with every step's logits."""
+    g = G.golden(gm.MODELS[name])
+    gen = _gen(name)
+    ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=native)
+    _check_run(g, ids, logits.cpu().numpy())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", DECIDABLE)
+def test_greedy_tokens_graphed(name):
+    """The benchmarked path: prefill replayed from a CUDA graph, decode steps replayed from
+    CUDA graphs (position read and advanced on the device), twice in a row (the second run
+    replays the cached graphs); then graphs of 5 steps over 16-position buckets, so the run
+    crosses bucket boundaries and replans the attention grid."""
+    g = G.golden(gm.MODELS[name])
+    gen = _gen(name)
+    for _ in range(2):
+        assert gen.generate_ids(g["prompt"], gm.N_GREEDY, graphed=True) == g["tokens"].tolist()
+    tok = gen.prefill(g["prompt"])
+    hist = gen.decode_graphed(tok, gm.N_GREEDY - 1, steps_per_graph=5, bucket=16)
+    n0 = len(g["prompt"])
+    assert hist[n0:n0 + gm.N_GREEDY].cpu().tolist() == g["tokens"].tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("native", [True, False], ids=["decoder_step", "op_by_op"])
+def test_greedy_std07_stepwise_prompt(native):
+    g = G.golden(gm.MODELS["smollm135m_std007"])
+    gen = _gen("smollm135m_std007")
+    ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=native, stepwise_prefill=True)
+    _check_run(g, ids, logits.cpu().numpy())
+    assert gen.generate_ids(g["prompt"], gm.N_GREEDY, stepwise_prefill=True, graphed=True) == g["tokens"].tolist()
+
+
+@pytest.mark.gpu
+def test_greedy_std07_default_path_teacher_forced():
+    """The default one-pass prefill on the N(0, 0.07) model with the reference's tokens fed
+    back: every step's top-8 logits within LOGIT_ATOL, and the greedy token equal to the
+    reference's wherever the reference's own top-1/top-2 margin exceeds 2 * LOGIT_ATOL."""
+    import torch
+    g = G.golden(gm.MODELS["smollm135m_std007"])
+    gen = _gen("smollm135m_std007")
+    tok, lg0 = gen.prefill(g["prompt"], want_logits=True)
+    dev = gen.device
+    feed = torch.tensor(g["tokens"], dtype=torch.int32, device=dev)
+    out = torch.zeros(1, dtype=torch.int32, device=dev)
+    logits = torch.empty((gm.N_GREEDY, gen.V), dtype=torch.float32, device=dev)
+    logits[0].copy_(lg0[0])
+    for step in range(1, gm.N_GREEDY):
+        gen.step_into(feed[step - 1:step], out, logits[step])
+    gen.check_status()
+    lg = logits.cpu().numpy()
+    margins = g["top_val"][:, 0] - g["top_val"][:, 1]
+    checked = 0
+    for step in range(gm.N_GREEDY):
+        err = np.abs(lg[step][g["top_idx"][step]] - g["top_val"][step]).max()
+        assert err <= LOGIT_ATOL, f"step {step}: top-8 logits differ by {err}"
+        if margins[step] > 2 * LOGIT_ATOL:
+            assert int(np.argmax(lg[step])) == int(g["tokens"][step]), f"step {step}"
+            checked += 1
+    assert checked >= 8

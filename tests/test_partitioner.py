@@ -79,3 +79,20 @@ def test_adaptive_block_rounding_covers_dim():
 def test_shard_plan_from_partitions_rejects_gaps():
     with pytest.raises(ValueError):
         ShardPlan.from_partitions(100, {0: {"ffn_start": 0, "ffn_end": 40}, 1: {"ffn_start": 50, "ffn_end": 100}})
+
+
+def test_decoder_head_and_vocab_splits():
+    """Head partition of a tensor-parallel decode layer (the reference's _solve_partitions rule,
+    src/orchestrator/root_node.py:182-210) and the lm_head vocabulary split."""
+    from pyre_b200.generator import head_split, vocab_split
+    assert head_split(32, 8, 1) == [((0, 32), (0, 8))]
+    assert head_split(32, 8, 4) == [((0, 8), (0, 2)), ((8, 16), (2, 4)), ((16, 24), (4, 6)), ((24, 32), (6, 8))]
+    assert head_split(14, 2, 2) == [((0, 7), (0, 1)), ((7, 14), (1, 2))]
+    assert head_split(9, 3, 2) == [((0, 6), (0, 2)), ((6, 9), (2, 3))]      # uneven: first ranks take one more
+    with pytest.raises(ValueError):
+        head_split(14, 2, 4)                                                # more ranks than kv heads
+    for V, world in ((32768, 8), (151936, 2), (49152, 3), (10, 4)):
+        parts = vocab_split(V, world)
+        assert parts[0][0] == 0 and parts[-1][1] == V
+        assert all(parts[i][1] == parts[i + 1][0] for i in range(world - 1))
+        assert max(b - a for a, b in parts) - min(b - a for a, b in parts) <= 1
