@@ -196,6 +196,11 @@ PYRE_API int pyre_comm_set_timeout_ns(pyre_comm_t* comm, uint64_t ns);
 /* Synchronises stream, then reads and clears the device status word of comm:
  * *status = PYRE_OK, or PYRE_ETIMEOUT if some wait since the last check ran out. */
 PYRE_API int pyre_comm_check(pyre_comm_t* comm, int* status, void* stream);
+/* Recovery after a wait ran out (no counterpart in the reference, whose TCP receive just
+ * blocks): synchronises stream, then zeroes this rank's flag words, collective epoch, arrival
+ * counter and status word. Every rank calls it, between host-side barriers and with none of
+ * its collectives in flight; the ranks then start again from a common state. */
+PYRE_API int pyre_comm_reset(pyre_comm_t* comm, void* stream);
 /* In-place sum over ranks of a f32 buffer of n elements (two-shot: reduce-scatter then
  * all-gather through peer memory), rank order 0..world-1. n <= max_tokens * hidden. */
 PYRE_API int pyre_allreduce_sum_f32(pyre_comm_t* comm, float* buf, int64_t n, void* stream);
@@ -414,6 +419,9 @@ PYRE_API int pyre_ulysses_attention(void* const* bufs, int rank, int P, int S, i
                                     void* stream);
 PYRE_API int pyre_ulysses_finish(void* local_buf, int P, int S, int nq, int nkv, int hd, float* out, int* status,
                                  void* stream);
+/* After a call whose barrier timed out: zeroes this rank's Ulysses flags, epoch and status word
+ * (every rank, between host barriers, nothing in flight), as pyre_comm_reset does for comm. */
+PYRE_API int pyre_ulysses_reset(void* local_buf, int P, int S, int nq, int nkv, int hd, void* stream);
 
 #ifdef __cplusplus
 }

@@ -66,6 +66,8 @@ _SIGNATURES = {
     "pyre_comm_destroy": [_vp],
     "pyre_comm_set_timeout_ns": [_vp, ctypes.c_uint64],
     "pyre_comm_check": [_vp, ctypes.POINTER(_i), _vp],
+    "pyre_comm_reset": [_vp, _vp],
+    "pyre_ulysses_reset": [_vp, _i, _i, _i, _i, _i, _vp],
     "pyre_allreduce_sum_f32": [_vp, _vp, _c_i64, _vp],
     "pyre_q80_linear": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _c_i64, _vp],
     "pyre_q80_linear_bias": [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _c_i64, _vp],

@@ -78,6 +78,18 @@ class UlyssesAttention:
             raise N.PyreTimeout(st.value, f"rank {self.rank}: a Ulysses barrier wait timed out")
         return out
 
+    def reset(self, group=None) -> None:
+        """After a PyreTimeout: every rank calls this (host barrier, clear this rank's flags,
+        epoch and status with pyre_ulysses_reset, host barrier) to start again in step."""
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=group)
+        N.call("pyre_ulysses_reset", ctypes.c_void_p(self._local), self.world, self.S, self.nq, self.nkv, self.hd,
+               D.stream_ptr())
+        if self.world > 1:
+            dist.barrier(group=group)
+
     def close(self) -> None:
         if self._local is None:
             return

@@ -1660,6 +1660,20 @@ extern "C" int pyre_ulysses_attention(void* const* bufs, int rank, int P, int S,
   return launch_prefill(p, hd, static_cast<cudaStream_t>(stream));
 }
 
+// Synchronises the stream, then zeroes this rank's barrier flags, epoch and status word, so the
+// ranks start again from a common state after a call that timed out (every rank calls it,
+// between host barriers, with none of its Ulysses kernels in flight).
+extern "C" int pyre_ulysses_reset(void* local_buf, int P, int S, int nq, int nkv, int hd, void* stream) {
+  int rc = uly_check_shape(S, P, nq, nkv, hd);
+  if (rc) return rc;
+  PYRE_CHECK_ARG(local_buf != nullptr, "pyre_ulysses_reset: null buffer");
+  const UlyLayout L = uly_layout(S, P, nq, nkv, hd);
+  PYRE_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  PYRE_CUDA_TRY(cudaMemset(static_cast<char*>(local_buf) + L.flags, 0, static_cast<size_t>(L.total - L.flags)));
+  PYRE_CUDA_TRY(cudaDeviceSynchronize());
+  return PYRE_OK;
+}
+
 // Synchronises the stream, returns and clears this rank's status word (PYRE_OK or
 // PYRE_ETIMEOUT), and copies its [S/P, nq*hd] attention output into out (device memory).
 extern "C" int pyre_ulysses_finish(void* local_buf, int P, int S, int nq, int nkv, int hd, float* out, int* status,

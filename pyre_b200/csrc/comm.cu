@@ -218,6 +218,7 @@ extern "C" int pyre_comm_create(int rank, int world, void* const* bufs, int max_
   const comm::Layout L = comm::layout(world, max_tokens, hidden);
   c->fused_floats = L.fused_floats;
   c->ar_chunk = L.ar_chunk;
+  c->local = static_cast<char*>(bufs[rank]);
   cudaError_t e = cudaMalloc(&c->d_peers, sizeof(char*) * world);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_status, sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&c->d_epoch, sizeof(uint32_t));
@@ -263,6 +264,18 @@ extern "C" int pyre_comm_check(pyre_comm_t* c, int* status, void* stream) {
   PYRE_CUDA_TRY(cudaMemcpy(&h, c->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   PYRE_CUDA_TRY(cudaMemset(c->d_status, 0, sizeof(int)));
   *status = h;
+  return PYRE_OK;
+}
+
+extern "C" int pyre_comm_reset(pyre_comm_t* c, void* stream) {
+  PYRE_CHECK_ARG(c != nullptr, "pyre_comm_reset: null communicator");
+  const comm::Layout L = comm::layout(c->world, c->max_tokens, c->hidden);
+  PYRE_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  PYRE_CUDA_TRY(cudaMemset(c->local + L.flags_off, 0, static_cast<size_t>(comm::kFlagWords) * 4));
+  PYRE_CUDA_TRY(cudaMemset(c->d_epoch, 0, sizeof(uint32_t)));
+  PYRE_CUDA_TRY(cudaMemset(c->d_done, 0, sizeof(unsigned int)));
+  PYRE_CUDA_TRY(cudaMemset(c->d_status, 0, sizeof(int)));
+  PYRE_CUDA_TRY(cudaDeviceSynchronize());
   return PYRE_OK;
 }
 

@@ -15,6 +15,7 @@ struct pyre_comm {
   int* d_status;           // device status word (PYRE_OK / PYRE_ETIMEOUT)
   int64_t fused_floats;    // per (slot, src) capacity of the fused-epilogue region
   int64_t ar_chunk;        // per (slot, phase, src) capacity of the all-reduce region
+  char* local;             // this rank's receive buffer (bufs[rank] of pyre_comm_create)
 };
 
 namespace pyre {

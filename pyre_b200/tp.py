@@ -142,6 +142,18 @@ class TPComm:
         if st.value != N.PYRE_OK:
             raise N.PyreTimeout(st.value, f"rank {self.rank}: a wait on a peer flag timed out")
 
+    def reset(self, group=None) -> None:
+        """Start every rank again from a common state after a wait ran out (PyreTimeout): all
+        ranks call this; it waits for this rank's work, meets the others on the host, clears
+        this rank's flags, epoch and status (pyre_comm_reset) and meets them again. Ops whose
+        kernels stopped early also clear their own scratch (FfnShardOp.reset)."""
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=group)
+        N.call("pyre_comm_reset", ctypes.c_void_p(self.handle), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if self.world > 1:
+            dist.barrier(group=group)
+
     def allreduce_(self, buf: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """In-place f32 sum over ranks (rank order) through peer memory."""
         if buf.dtype != torch.float32 or not buf.is_contiguous():
