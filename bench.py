@@ -67,7 +67,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     ap.add_argument("--sets", type=int, default=N_SETS, help="distinct weight sets the steps rotate over")
     ap.add_argument("--no-attention", action="store_true", help="skip the attention and lm_head measurements")
-    ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder (7B shape) measurement")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the SmolLM-shaped end-to-end measurement")
+    ap.add_argument("--no-long-context", action="store_true", help="skip the 32768-token Ulysses measurement")
     ap.add_argument("--decoder-only", action="store_true",
                     help="run only the decoder measurement on one GPU (for profiling) and print its JSON object")
     ap.add_argument("--decoder-prompt", type=int, default=2048)
@@ -423,6 +424,81 @@ def cpu_decoder_leg(budget_s: float = 15.0):
     }
 
 
+def long_context_bench(dev, world, rank, barrier, S: int = 32768, reps: int = 3):
+    """The long-context Ulysses configuration: Llama-3-8B attention shape (hidden 4096, 32 q / 8 kv
+    heads, hd 128, causal, RoPE theta 5e5), S bf16 N(0, 1) hidden states (seed 4) split evenly over
+    the ranks, Q/K/V/O weights N(0, 0.02) in Q8_0 (seed 4, identical on every rank). One call:
+    [Wq|Wk|Wv] projection of the rank's tokens (tensor-core Q8_0 GEMM), Ulysses attention (RoPE
+    fused with the QKV all-to-all over NVLink, causal attention of the rank's heads over the whole
+    sequence, output rows stored into their owners), O projection. With one GPU the same pipeline
+    runs with plain prefill attention. CUDA events around each call, median, max over ranks."""
+    import torch
+    from pyre_b200.attention import AttentionOp, Q80Linear, UlyssesAttention
+    from pyre_b200.quantizer import Q80Weight
+    nq, nkv, hd, theta = 32, 8, 128, 5e5
+    Sl = S // world
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn((S, H), generator=g, device=dev).to(torch.bfloat16)[rank * Sl:(rank + 1) * Sl].contiguous()
+
+    def w(k, n):
+        return Q80Weight.from_float((torch.randn((k, n), generator=g, device=dev) * 0.02).to(torch.bfloat16).float(),
+                                    torch.float16)
+    wq, wk, wv, wo = w(H, nq * hd), w(H, nkv * hd), w(H, nkv * hd), w(nq * hd, H)
+    qkv = Q80Linear(Q80Weight(torch.cat([wq.q, wk.q, wv.q], 1).contiguous(),
+                              torch.cat([wq.scale, wk.scale, wv.scale], 1).contiguous()), Sl, dev)
+    o = Q80Linear(wo, Sl, dev)
+    del wq, wk, wv, wo
+    att = UlyssesAttention(S, nq, nkv, hd, rope_theta=theta, timeout_s=10.0) if world > 1 else \
+        AttentionOp(nq, nkv, hd, max_t=S, rope_theta=theta, device=dev)
+    qw, kw = nq * hd, nkv * hd
+
+    def call():
+        y = qkv(x)
+        q, k, v = y[:, :qw], y[:, qw:qw + kw], y[:, qw + kw:]
+        if world > 1:
+            a = att(q, k, v)
+        else:
+            att.reset()
+            a = att.prefill(q, k, v)
+        return o(a)
+
+    call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        barrier()
+        e0.record()
+        out = call()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    barrier()
+    ms = statistics.median(ts)
+    ok = bool(torch.isfinite(out).all())
+    if world > 1:
+        att.close()
+    del qkv, o, att, x
+    torch.cuda.empty_cache()
+    return {"ms": ms, "finite": ok}
+
+
+def long_context_report(ms: float, world: int, tf_burst: float, S: int = 32768):
+    nq, nkv, hd = 32, 8, 128
+    proj = 2 * S * H * (nq * hd + 2 * nkv * hd + nq * hd)
+    attn = 2 * 2 * hd * nq * S * S // 2
+    a2a = (S * (nq + 2 * nkv) * hd * 2 + S * nq * hd * 4) * (world - 1) // world
+    tf = (proj + attn) / (ms * 1e-3) / 1e12
+    return {"workload": "Llama-3-8B attention shape (hidden 4096, 32/8 heads, hd 128, theta 5e5), 32768 bf16 "
+                        "hidden states, Q8_0 Q/K/V/O projections, causal attention, sequence split over the ranks",
+            "ms": round(ms, 3), "tokens_per_s": round(S / (ms * 1e-3), 1),
+            "flop": int(proj + attn), "tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / (tf_burst * world), 4),
+            "all_to_all_bytes": int(a2a),
+            "how": "QKV Q8_0 GEMM -> " + ("Ulysses attention (RoPE + QKV exchange, attention, output scatter over "
+                                         "NVLink)" if world > 1 else "prefill attention") +
+                   " -> O Q8_0 GEMM, CUDA events, median of 3, max over ranks"}
+
+
 def smollm_bench(dev, reps: int = 5):
     """The SmolLM-135M-shaped decoder (hidden 576, 30 layers, 9/3 heads, hd 64, FFN 1536, vocab
     49152, tied f16 embedding, RoPE theta 1e4): 8 prompt ids from default_rng(0), 10 greedy
@@ -686,6 +762,7 @@ def run_ours(args):
     del dec["gen"]
     torch.cuda.empty_cache()
 
+    lc = None if args.no_long_context else long_context_bench(dev, world, rank, barrier)
     attn = lmh = smollm = None
     if world == 1 and not args.no_attention:
         attn = attention_bench(dev, stream, hbm, tf_burst)
@@ -694,11 +771,12 @@ def run_ours(args):
         smollm = smollm_bench(dev)
 
     vals = torch.tensor([dec["dec_ms"], dec["prefill_ms"], dec["e2e_s"], ffn["ms"], ffn["probe_ms"],
-                         ffn.get("prefill_ms", 0.0), ffn.get("nccl_ms", 0.0), -ffn["e2e_tok_s"]],
+                         ffn.get("prefill_ms", 0.0), ffn.get("nccl_ms", 0.0), -ffn["e2e_tok_s"],
+                         lc["ms"] if lc else 0.0],
                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    dec_ms, pf_ms, e2e_s, ffn_ms, probe_ms, ffn_pf_ms, nccl_ms, neg_ffn_e2e = vals.tolist()
+    dec_ms, pf_ms, e2e_s, ffn_ms, probe_ms, ffn_pf_ms, nccl_ms, neg_ffn_e2e, lc_ms = vals.tolist()
 
     if rank == 0:
         K = args.steps
@@ -772,6 +850,9 @@ def run_ours(args):
             res["ffn_op"]["prefill"] = {"tokens": args.prefill_tokens, "ms": round(ffn_pf_ms, 4),
                                         "tflops": round(flops / (ffn_pf_ms * 1e-3) / 1e12, 2),
                                         "frac_of_bf16_peak": round(flops / (ffn_pf_ms * 1e-3) / 1e12 / (tf_burst * world), 4)}
+        if lc:
+            res["long_context"] = long_context_report(lc_ms, world, tf_burst)
+            res["long_context"]["finite"] = lc["finite"]
         if attn:
             res["attention"] = attn
         if lmh:

@@ -115,3 +115,47 @@ def decode_step(q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, k_cache, v_
     out = attention_decode(np.clip(q_r, -1000, 1000), np.clip(k_full, -1000, 1000), np.clip(v_full, -1000, 1000),
                            prefill_real, prefill_max_seq)
     return out, k_full, v_full
+
+
+def attention_rows_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, positions, heads, n_heads: int, n_kv: int,
+                       theta: float, rope_fraction: float = 1.0) -> np.ndarray:
+    """Row-wise f64 restatement of root_node.py:250-314 for chosen (query position, head) pairs
+    of one causal sequence, for sequences whose full score matrix is too large to form (the
+    32768-token long-context case): RoPE with the reference's f32 cos/sin tables
+    (pyre_kernels.mojo:86-89) applied in f64, clip +-1000 (:288-290), the kv head of a query
+    head (GQA, :295-297), q k^T / sqrt(hd) over positions 0..p (causal, :299-303), softmax and
+    probs @ v, all in f64.
+
+    q: [S, n_heads * hd], k, v: [S, n_kv * hd] (token-major projections, f32). positions,
+    heads: equal-length integer sequences. Returns f64 [len(positions), hd]."""
+    S = q.shape[0]
+    hd = q.shape[1] // n_heads
+    dims = int(float(hd) * float(rope_fraction))
+    half = dims // 2 if dims >= 2 else 0
+    c, s = K.rope_tables(theta, 0, S, max(dims, 2))
+    c, s = c.astype(np.float64), s.astype(np.float64)
+
+    rep = n_heads // n_kv
+    out = np.empty((len(positions), hd), dtype=np.float64)
+    kr_cache: dict = {}
+    for i, (p, h) in enumerate(zip(positions, heads)):
+        g = int(h) // rep
+        if g not in kr_cache:
+            kk = k[:, g * hd:(g + 1) * hd].astype(np.float64)
+            vv = v[:, g * hd:(g + 1) * hd].astype(np.float64)
+            if half:
+                k1, k2 = kk[:, :half].copy(), kk[:, half:2 * half].copy()
+                kk[:, :half] = k1 * c[:, :half] - k2 * s[:, :half]
+                kk[:, half:2 * half] = k1 * s[:, :half] + k2 * c[:, :half]
+            kr_cache[g] = (np.clip(kk, -1000, 1000), np.clip(vv, -1000, 1000))
+        kk, vv = kr_cache[g]
+        qq = q[int(p), int(h) * hd:(int(h) + 1) * hd].astype(np.float64)
+        if half:
+            q1, q2 = qq[:half].copy(), qq[half:2 * half].copy()
+            qq[:half] = q1 * c[int(p), :half] - q2 * s[int(p), :half]
+            qq[half:2 * half] = q1 * s[int(p), :half] + q2 * c[int(p), :half]
+        qq = np.clip(qq, -1000, 1000)
+        sc = kk[:int(p) + 1] @ qq / np.sqrt(float(hd))
+        e = np.exp(sc - sc.max())
+        out[i] = (e / e.sum()) @ vv[:int(p) + 1]
+    return out

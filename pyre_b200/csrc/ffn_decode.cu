@@ -67,18 +67,14 @@ int launch_stream(StreamParams p, const StreamArgs& a, cudaStream_t s) {
     p.spg = kChunk * C::LB::kRows / kTileN;
     p.slack = p.cptB;
   }
-  if constexpr (TP) {
-    // the tensor-parallel epilogue synchronises with the other ranks: launched after the
-    // previous kernel has finished
-    kern<<<static_cast<int>(g), kStreamThreads, C::kSmemBytes, s>>>(p);
-    PYRE_LAUNCH_CHECK("q80_ffn_stream_kernel");
-    return PYRE_OK;
-  } else {
-    // may start while the previous kernel finishes: its first weight copies overlap that tail
-    PYRE_CUDA_TRY(launch_pdl(kern, dim3(static_cast<unsigned>(g)), dim3(kStreamThreads),
-                             static_cast<size_t>(C::kSmemBytes), s, p));
-    return PYRE_OK;
-  }
+  // May start while the previous kernel finishes: its first weight copies overlap that tail.
+  // Everything else (activations, scratch, and with tensor parallelism the communicator's
+  // epoch, peer stores and flag waits) comes after griddepcontrol.wait, i.e. after the previous
+  // kernel has completed. A tensor-parallel grid is sized to be co-resident and its CTAs wait
+  // only for peer ranks (never for CTAs of their own grid), so an early start cannot deadlock.
+  PYRE_CUDA_TRY(launch_pdl(kern, dim3(static_cast<unsigned>(g)), dim3(kStreamThreads),
+                           static_cast<size_t>(C::kSmemBytes), s, p));
+  return PYRE_OK;
 }
 
 template <int T, int NA, typename XA, typename XB, typename ST>

@@ -50,3 +50,19 @@ def test_decode_step_matches_prefill_rows():
         out, kc, vc = OA.decode_step(q[:, s:s + 1].transpose(0, 2, 1, 3), k[:, s:s + 1].transpose(0, 2, 1, 3),
                                      v[:, s:s + 1].transpose(0, 2, 1, 3), kc, vc)
         np.testing.assert_allclose(out[0, 0], full[0, s], rtol=1e-5, atol=1e-5)
+
+
+def test_attention_rows_f64_equals_full_oracle():
+    """The row-wise f64 restatement used for the 32768-token check equals the full-matrix
+    oracle (compute_attention, itself pinned to the reference's goldens) on sampled rows."""
+    import numpy as np
+    from oracle import attention as OA
+    rng = np.random.default_rng(1)
+    S, nq, nkv, hd = 200, 8, 2, 64
+    q, k, v = (rng.standard_normal((S, n * hd)).astype(np.float32) * 3 for n in (nq, nkv, nkv))
+    ref = OA.compute_attention([(q.reshape(1, S, nq, hd), k.reshape(1, S, nkv, hd), v.reshape(1, S, nkv, hd))],
+                               nq, nkv, 1.0, 5e5)[0]
+    pos, hs = rng.integers(0, S, 64), rng.integers(0, nq, 64)
+    rows = OA.attention_rows_f64(q, k, v, pos, hs, nq, nkv, 5e5)
+    want = np.stack([ref[p, h * hd:(h + 1) * hd] for p, h in zip(pos, hs)])
+    assert np.abs(rows - want).max() <= 1e-5 * np.abs(want).max()
