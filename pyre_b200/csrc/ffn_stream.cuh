@@ -315,6 +315,9 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       // copy into this CTA's shared memory is in flight when it exits.
       bool ok = true;
       uint32_t issued = 0, par = 0;   // stages with an unconfirmed copy, and that copy's parity
+      // MODE_AB: the last phase-A slab this producer has seen ready (its flag acquired and the
+      // proxy fence done); the following units of the same slab need no second flag round trip
+      int seen_slab = -1;
       auto acquire = [&]() -> bool {
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) return false;
         issued &= ~(1u << s);           // the consumers released the stage: its copy landed
@@ -377,9 +380,14 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
               }
               bool rdy = true;
               if constexpr (MODE == MODE_AB) {
-                // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256)
-                rdy = wait_ready(p.ready + k0 / kTileN, epoch, p.status);
-                fence_proxy_async_global();
+                // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256); a
+                // slab already seen ready in this call needs no second acquire
+                const int slab = k0 / kTileN;
+                if (slab != seen_slab) {
+                  rdy = wait_ready(p.ready + slab, epoch, p.status);
+                  fence_proxy_async_global();
+                  if (rdy) seen_slab = slab;
+                }
               }
               // issued even when the flag wait ran out, so the stage's byte count completes
               tma_load_2d(st + LB::kXOff, &p.txb, k0, 0, &full[s]);
