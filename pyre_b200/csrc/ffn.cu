@@ -118,9 +118,14 @@ extern "C" int pyre_q80_linear_bias(const void* x, int x_dtype, int T, int K, co
   PYRE_CHECK_ARG(w != nullptr && reinterpret_cast<uintptr_t>(w) % 16 == 0,
                  "pyre_q80_linear: packed weights must be non-null and 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (T <= PYRE_FUSED_REDUCE_MAX_T)
-    return ffn_stream_down(x, x_dtype, T, K, w, scale_dtype, N, out, workspace, ws_bytes, nullptr, s, bias);
   char* wsc = static_cast<char*>(workspace);
+  if (T <= PYRE_FUSED_REDUCE_MAX_T) {
+    // matrices up to K = 8192 (the attention projections): one cluster per column slab, every
+    // weight copy in flight at once, the split-K reduction in distributed shared memory
+    if (gemv_cluster_eligible(K, N))
+      return gemv_cluster(x, x_dtype, T, K, w, scale_dtype, N, bias, out, reinterpret_cast<int*>(wsc + kHdrStatus), s);
+    return ffn_stream_down(x, x_dtype, T, K, w, scale_dtype, N, out, workspace, ws_bytes, nullptr, s, bias);
+  }
   GemmRegion g;
   rc = gemm_region(workspace, ws_bytes, T, K, N, 1, &g, "pyre_q80_linear");
   if (rc) return rc;

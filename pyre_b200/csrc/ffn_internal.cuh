@@ -93,6 +93,10 @@ int ffn_check_common(const void* x, int x_dtype, int T, int K, int N, int scale_
 int ffn_decode_check(const void* x, int x_dtype, int T, int H, const void* wgu, int gated, const void* wd,
                      int scale_dtype, int W, const float* out, const void* workspace, int64_t ws_bytes,
                      const pyre_comm_t* comm, const char* fn);
+// Cluster GEMV of gemv_cluster.cu for T <= 4 on one packed matrix [K, N] (K <= 8192).
+bool gemv_cluster_eligible(int K, int N);
+int gemv_cluster(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N, const float* bias,
+                 float* out, int* status, cudaStream_t s);
 int ffn_gemm_tc(const void* a, int a_dtype, int T, int K, const void* w, int nmat, int epi, int scale_dtype, int N,
                 void* out, int out_dtype, void* staging, int64_t staging_bytes, void* partial, int64_t partial_bytes,
                 unsigned int* counters, int* status, cudaStream_t s, const float* bias = nullptr);

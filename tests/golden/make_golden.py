@@ -28,6 +28,8 @@ Run in a container that has the reference checkout (read-only) at /root/referenc
                          ``_sample`` at temperature 0 (src/orchestrator/generator.py:40-53):
                          final RMSNorm, logits against the f16 lm_head table, greedy token,
                          including rows with tied maxima.
+* wire_golden.npz      — the reference's message framing (net.py send_msg) of three root /
+                         worker messages with Q8_0 activation tuples (quantizer.py:54-67).
 * greedy_golden*.npz   — the reference orchestrator's greedy decode (RootNode + Generator
                          loop) of 32 tokens on the seeded models of tests/golden/greedy_model.py:
                          the SmolLM-135M shape (projections N(0, 0.02) and N(0, 0.07)) and the
@@ -319,6 +321,40 @@ def make_lmhead() -> None:
     print("lmhead_golden.npz written")
 
 
+def make_wire(ref_root: Path, quantizer) -> None:
+    """The reference's framing (src/orchestrator/net.py:18-48 send_msg, read back from a
+    socketpair) of three messages a root and its workers exchange, with activations as the
+    reference's Q8_0 tuples (quantize_activation, quantizer.py:54-67)."""
+    import socket
+    import threading
+    net = _load_module(ref_root / "src" / "orchestrator" / "net.py", "ref_net")
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((1, 64, 576)) * 3).astype(np.float32)
+    x1 = (rng.standard_normal((1, 1, 4096)) * 2).astype(np.float32)
+    ffn = rng.standard_normal((1, 1, 896)).astype(np.float32)
+    msgs = [(2, (3, quantizer.quantize_activation(x))), (10, (5, quantizer.quantize_activation(x1), 2175)),
+            (6, ffn)]
+    blobs = []
+    for mtype, obj in msgs:
+        a, b = socket.socketpair()
+        t = threading.Thread(target=net.send_msg, args=(a, mtype, obj))
+        t.start()
+        out = bytearray()
+        hdr = net.recv_exact(b, 12)
+        out += hdr
+        total = int.from_bytes(hdr[4:8], "big")
+        out += net.recv_exact(b, total)
+        t.join()
+        a.close()
+        b.close()
+        blobs.append(np.frombuffer(bytes(out), dtype=np.uint8))
+    q0, s0, sh0 = msgs[0][1][1]
+    q1, s1, sh1 = msgs[1][1][1]
+    np.savez_compressed(HERE / "wire_golden.npz", x=x, x1=x1, ffn=ffn, q0=q0, s0=s0, shape0=np.array(sh0),
+                        q1=q1, s1=s1, shape1=np.array(sh1), msg0=blobs[0], msg1=blobs[1], msg2=blobs[2])
+    print("wire_golden.npz written:", [len(b) for b in blobs], "bytes")
+
+
 def make_greedy(quantizer, only: str | None = None) -> None:
     """The reference orchestrator (RootNode with no workers: head-partitioned, all heads at the
     root, src/orchestrator/root_node.py:344-380, :699-1007) and Generator's prefill / greedy
@@ -399,13 +435,16 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     ap.add_argument("--only", default=None,
-                    help="write one fixture: lmhead, greedy (every greedy model) or greedy:<model name>")
+                    help="write one fixture: lmhead, wire, greedy (every greedy model) or greedy:<model name>")
     args = ap.parse_args()
     ref = Path(args.ref)
     sys.path.insert(0, str(HERE / "max_shim"))
     sys.path.insert(0, str(ref))
     if args.only == "lmhead":
         make_lmhead()
+        return
+    if args.only == "wire":
+        make_wire(ref, _load_module(ref / "src" / "orchestrator" / "quantizer.py", "ref_quantizer"))
         return
     if args.only is not None and args.only.startswith("greedy"):
         name = args.only.split(":", 1)[1] if ":" in args.only else None
@@ -420,6 +459,7 @@ def main() -> None:
     print("partition_golden.json written")
     make_attention()
     make_lmhead()
+    make_wire(ref, quantizer)
     make_greedy(quantizer)
 
 

@@ -57,6 +57,39 @@ def test_q80_linear(T):
     assert rel(out, ref) < (1e-4 if T <= 4 else 1e-2)
 
 
+# Projection shapes of the decode step: SmolLM QKV (K 576, N 960), Qwen QKV (896, 1152, 4.5
+# slabs), 7B QKV and O (4096, 6144 / 4096), a tensor-parallel QKV (4096, 1024), a K at the
+# cluster kernel's limit (8192) and one beyond it (14336, streaming kernel); f32 and bf16
+# activations, f16 and f32 scales, with and without the bias.
+@pytest.mark.parametrize("K,N,T,xbf16,s32,bias", [
+    (576, 960, 1, False, False, True), (896, 1152, 3, False, False, True), (4096, 6144, 1, False, False, False),
+    (4096, 4096, 4, True, False, False), (4096, 1024, 2, False, True, True), (8192, 512, 1, False, False, True),
+    (14336, 4096, 1, False, False, True), (64, 32, 4, False, False, True)])
+def test_q80_linear_decode_shapes(K, N, T, xbf16, s32, bias):
+    from pyre_b200.attention import Q80Linear
+    from pyre_b200.quantizer import Q80Weight
+    rng = np.random.default_rng(K + N + T)
+    w = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    q, sc, sh = oq80.quantize_q80(w)
+    if not s32:
+        sc = sc.astype(np.float16).astype(np.float32)
+    wd = oq80.dequantize_q80(q, sc, sh)
+    b = (rng.standard_normal(N) * 0.5).astype(np.float32) if bias else None
+    lin = Q80Linear(Q80Weight.from_tuple(("q8", q, sc, sh), scale_dtype=torch.float32 if s32 else torch.float16),
+                    max_tokens=T, bias=b)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    if xbf16:
+        xt = xt.to(torch.bfloat16)
+        x = xt.float().cpu().numpy()
+    ref = x.astype(np.float64) @ wd.astype(np.float64) + (b.astype(np.float64) if bias else 0.0)
+    for _ in range(2):          # repeated calls reuse the scratch
+        out = lin(xt).cpu().numpy()
+        assert rel(out, ref) < 1e-4
+    torch.cuda.synchronize()
+    assert int(lin.workspace[8:12].view(torch.int32).item()) == 0
+
+
 def _qkv(rng, T, nq, nkv, hd, scale=2.0):
     q = (rng.standard_normal((T, nq * hd)) * scale).astype(np.float32)
     k = (rng.standard_normal((T, nkv * hd)) * scale).astype(np.float32)
