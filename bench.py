@@ -73,6 +73,7 @@ def parse():
                     help="run only the decoder measurement on one GPU (for profiling) and print its JSON object")
     ap.add_argument("--decoder-prompt", type=int, default=2048)
     ap.add_argument("--e2e-reps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=8, help="static batch of the second decode measurement (1: skip)")
     return ap.parse_args()
 
 
@@ -325,6 +326,11 @@ def decoder_bench(dev, hbm, args, comm, world, barrier):
     layers, emb, ones, head = decoder_7b_weights(dev)
     gen = Generator(layers, emb, ones, n_heads=NQ7, n_kv_heads=NKV7, head_dim=HD7, rope_theta=1e6, lm_head=head,
                     max_seq=prompt + W + K + 2, max_prompt=prompt, device=dev, comm=comm)
+    gen8 = None
+    if args.batch > 1:
+        gen8 = Generator(layers, emb, ones, n_heads=NQ7, n_kv_heads=NKV7, head_dim=HD7, rope_theta=1e6,
+                         lm_head=head, max_seq=prompt + W + K + 2, max_prompt=prompt, device=dev, comm=comm,
+                         batch=args.batch)
     del layers
     torch.cuda.empty_cache()
     ids = np.random.default_rng(3).integers(0, V7, prompt)
@@ -363,10 +369,33 @@ def decoder_bench(dev, hbm, args, comm, world, barrier):
         e2e.append(time.perf_counter() - t0)
     barrier()
     same = out[:W + K + 1] == timed_tokens.tolist()[:n_e2e]
+    batch_info = None
+    if gen8 is not None:
+        # static batch: the prompt above and B - 1 more (seeded), decoded in lockstep
+        Bn = args.batch
+        prompts = np.random.default_rng(3).integers(0, V7, (Bn, prompt))
+        prompts[0] = ids
+        first = gen8.prefill_batch(prompts)
+        gen8.decode_graphed(first, W + K)               # captures the graphs
+        torch.cuda.synchronize()
+        first = gen8.prefill_batch(prompts)
+        hist = gen8.decode_graphed(first, W)
+        nxt = hist[:, prompt + W].clone()
+        barrier()
+        e0.record()
+        hist = gen8.decode_graphed(nxt, K)
+        e1.record()
+        torch.cuda.synchronize()
+        b_ms = e0.elapsed_time(e1) / K
+        barrier()
+        gen8.check_status()
+        seq0 = hist[0, prompt:prompt + W + K + 1].cpu()
+        batch_info = {"ms": b_ms, "batch": Bn, "seq0_equals_batch1": bool(torch.equal(seq0, timed_tokens))}
+        del gen8
     launches = 3 + 6 * L7 + (1 if comm is not None else 0)
     info = {"gen": gen, "dec_ms": dec_ms, "prefill_ms": min(pf), "e2e_s": statistics.median(e2e), "e2e_tokens": n_e2e,
             "launches_per_token": launches, "tokens_equal": bool(same), "ids_bytes": int(prompt) * 4,
-            "out_bytes": n_e2e * 8}
+            "out_bytes": n_e2e * 8, "batch": batch_info}
     return info
 
 
@@ -772,11 +801,11 @@ def run_ours(args):
 
     vals = torch.tensor([dec["dec_ms"], dec["prefill_ms"], dec["e2e_s"], ffn["ms"], ffn["probe_ms"],
                          ffn.get("prefill_ms", 0.0), ffn.get("nccl_ms", 0.0), -ffn["e2e_tok_s"],
-                         lc["ms"] if lc else 0.0],
+                         lc["ms"] if lc else 0.0, dec["batch"]["ms"] if dec["batch"] else 0.0],
                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    dec_ms, pf_ms, e2e_s, ffn_ms, probe_ms, ffn_pf_ms, nccl_ms, neg_ffn_e2e, lc_ms = vals.tolist()
+    dec_ms, pf_ms, e2e_s, ffn_ms, probe_ms, ffn_pf_ms, nccl_ms, neg_ffn_e2e, lc_ms, b_ms = vals.tolist()
 
     if rank == 0:
         K = args.steps
@@ -804,6 +833,14 @@ def run_ours(args):
                        "weight_bytes_per_token": tok_bytes,
                        "frac_of_aggregate_hbm": round(tok_bytes / (dec_ms * 1e-3) / 1e9 / (hbm * world), 4),
                        "launches_per_token": dec["launches_per_token"]},
+            "decode_batch": None if not dec["batch"] else {
+                "batch": dec["batch"]["batch"], "ms_per_step": round(b_ms, 4),
+                "tok_s": round(dec["batch"]["batch"] * 1e3 / b_ms, 1),
+                "frac_of_aggregate_hbm": round(tok_bytes / (b_ms * 1e-3) / 1e9 / (hbm * world), 4),
+                "sequence0_tokens_equal_batch1": dec["batch"]["seq0_equals_batch1"],
+                "how": "Generator(batch=B).decode_graphed: B sequences (the 2048-token prompt and B - 1 seeded "
+                       "ones) in lockstep, projections and FFN on row groups of 4 tokens, one attention launch for "
+                       "all sequences, CUDA graphs of 16 steps, CUDA events, max over ranks"},
             "prefill": {"tokens": prompt, "ms": round(pf_ms, 3), "tok_s": round(prompt / (pf_ms * 1e-3), 1),
                         "linear_tflops": round(2 * prompt * L7 * (H * (NQ7 + 2 * NKV7) * HD7 + NQ7 * HD7 * H + 3 * H * I)
                                                / (pf_ms * 1e-3) / 1e12, 1),

@@ -375,6 +375,12 @@ typedef struct pyre_decoder_desc {
   pyre_comm_t* comm;
   int64_t lm_v0;       /* first vocabulary row of lm_head (0 without a vocabulary split) */
   int lm_V;            /* rows of lm_head; 0: V (the whole table) */
+  /* Static batch (0 or 1: one sequence): B sequences decoded in lockstep at one position.
+   * token_in / token_out hold B ids, the scratch vectors are [B, ...], each layer's caches
+   * [B, nkv, max_t, hd] with attn_ws of pyre_attn_decode_workspace_bytes(B nq, B nkv, hd,
+   * max_t), logits [B, lm_V], history [B, max_t + 1]; the projections and the FFN run on row
+   * groups of at most 4 tokens, so every sequence's arithmetic equals a one-sequence step's. */
+  int batch;
 } pyre_decoder_desc;
 
 /* One decode step: token_in (int32 [1], device) at position pos (= tokens already in the
@@ -389,6 +395,19 @@ PYRE_API int pyre_attn_decode_step_dev(const float* q, const float* k, const flo
                                        int plan_pos, const float* rope_table, double rope_fraction, int nq, int nkv,
                                        int hd, uint16_t* k_cache, uint16_t* v_cache, int max_t, int mask_lo,
                                        int mask_hi, float* out, void* workspace, int64_t ws_bytes, void* stream);
+
+/* The fused decode step for B sequences at one position (a static batch decoded in lockstep):
+ * q, k, v of sequence b start at q + b * qkv_stride, k + b * qkv_stride, v + b * qkv_stride (one
+ * fused QKV projection output [B, (nq + 2 nkv) hd] passed as three offset pointers); the caches
+ * are [B, nkv, max_t, hd] f16 and out [B, nq * hd] f32. Every sequence's cache is split as in a
+ * single-sequence step, so each sequence's result equals pyre_attn_decode_step_dev's bit for
+ * bit. pos_dev (nullable) as in pyre_attn_decode_step_dev, else the position is plan_pos.
+ * workspace: pyre_attn_decode_workspace_bytes(B * nq, B * nkv, hd, max_t), zeroed once. */
+PYRE_API int pyre_attn_decode_step_batch(const float* q, const float* k, const float* v, int64_t qkv_stride, int B,
+                                         const int* pos_dev, int plan_pos, const float* rope_table,
+                                         double rope_fraction, int nq, int nkv, int hd, uint16_t* k_cache,
+                                         uint16_t* v_cache, int max_t, float* out, void* workspace, int64_t ws_bytes,
+                                         void* stream);
 
 /* sizeof(pyre_decoder_layer) and sizeof(pyre_decoder_desc), for bindings that lay the
  * structs out themselves (ctypes, cgo) to check their layout against. */

@@ -77,6 +77,8 @@ _SIGNATURES = {
     "pyre_decoder_step": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp],
     "pyre_attn_decode_step_dev": [_vp, _vp, _vp, _vp, _i, _vp, ctypes.c_double, _i, _i, _i, _vp, _vp, _i, _i, _i,
                                   _vp, _vp, _c_i64, _vp],
+    "pyre_attn_decode_step_batch": [_vp, _vp, _vp, _c_i64, _i, _vp, _i, _vp, ctypes.c_double, _i, _i, _i, _vp, _vp,
+                                    _i, _vp, _vp, _c_i64, _vp],
     "pyre_decoder_struct_sizes": [_vp, _vp],
     "pyre_embed_rms_norm": [_vp, _i, _vp, _i, _i, _vp, ctypes.c_double, _vp, _vp, _vp, _vp],
     "pyre_softmax_rows": [_vp, _c_i64, _i, _vp, _vp],

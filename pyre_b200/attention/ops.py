@@ -102,10 +102,16 @@ def rope_table(theta: float, rope_fraction: float, head_dim: int, n_pos: int, de
 class KVCache:
     """One layer's K and V cache, f16 ``[n_kv, max_t, hd]`` (values clipped to +-1000)."""
 
-    def __init__(self, n_kv: int, max_t: int, head_dim: int, device=None):
+    def __init__(self, n_kv: int, max_t: int, head_dim: int, device=None, k=None, v=None):
+        """``k`` / ``v``: existing contiguous f16 ``[n_kv, max_t, hd]`` tensors to use (a slice of
+        a batch's stacked caches) instead of new ones."""
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.k = torch.zeros((n_kv, max_t, head_dim), dtype=torch.float16, device=dev)
-        self.v = torch.zeros_like(self.k)
+        if k is None:
+            k = torch.zeros((n_kv, max_t, head_dim), dtype=torch.float16, device=dev)
+            v = torch.zeros_like(k)
+        if tuple(k.shape) != (n_kv, max_t, head_dim) or k.shape != v.shape or not (k.is_contiguous() and v.is_contiguous()):
+            raise ValueError("cache tensors must be contiguous f16 [n_kv, max_t, head_dim]")
+        self.k, self.v = k, v
         self.n_kv, self.max_t, self.head_dim = n_kv, max_t, head_dim
         self.length = 0
 
@@ -114,15 +120,17 @@ class AttentionOp:
     """Attention of one layer (one sequence) over a preallocated :class:`KVCache`."""
 
     def __init__(self, n_heads: int, n_kv_heads: int, head_dim: int, max_t: int, rope_theta: float = 10000.0,
-                 rope_fraction: float = 1.0, device=None):
+                 rope_fraction: float = 1.0, device=None, cache: KVCache | None = None,
+                 rope: torch.Tensor | None = None):
         if n_heads % n_kv_heads:
             raise ValueError("n_heads must be a multiple of n_kv_heads")
         if head_dim not in (64, 128):
             raise ValueError("head_dim must be 64 or 128")
         self.nq, self.nkv, self.hd = n_heads, n_kv_heads, head_dim
         self.theta, self.frac = float(rope_theta), float(rope_fraction)
-        self.cache = KVCache(n_kv_heads, max_t, head_dim, device)
-        self.rope = rope_table(self.theta, self.frac, head_dim, max_t, self.cache.k.device)
+        self.cache = cache if cache is not None else KVCache(n_kv_heads, max_t, head_dim, device)
+        self.rope = rope if rope is not None else rope_table(self.theta, self.frac, head_dim, max_t,
+                                                             self.cache.k.device)
         b = ctypes.c_int64(0)
         N.call("pyre_attn_decode_workspace_bytes", n_heads, n_kv_heads, head_dim, max_t, ctypes.byref(b))
         self.dec_ws = torch.zeros(int(b.value), dtype=torch.uint8, device=self.cache.k.device)

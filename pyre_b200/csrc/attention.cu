@@ -389,6 +389,11 @@ struct DecodeParams {
                          // a CUDA graph): t = *pos_dev + 1, rope row *pos_dev of rope_base;
                          // t and rope above are then only the host's plan of the grid
   const float2* rope_base;
+  // Batched fused step: B sequences at one position, their caches [B][nkv_seq] stacked as
+  // nkv = B * nkv_seq kv heads (out likewise [B][nq_seq * hd]); kv head g belongs to sequence
+  // g / nkv_seq, whose q, k, v rows start at qf + b * q_bstride, kf / vf + b * kv_bstride.
+  int nkv_seq;
+  int64_t q_bstride, kv_bstride;
 };
 
 // Shared memory: the static part below, then (dynamic) the warps' rescaled partials
@@ -579,19 +584,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
     // the token's rotated k and clipped v at row t - 1 before any of its warps reads it
     __shared__ __align__(16) __half qs[kDecMaxRep * HD];
     const int pos = t - 1;
+    const int gb = g / p.nkv_seq, gl = g - gb * p.nkv_seq;     // sequence, kv head within it
+    const float* qf = p.qf + gb * p.q_bstride;
+    const float* kf = p.kf + gb * p.kv_bstride;
+    const float* vf = p.vf + gb * p.kv_bstride;
     for (int e = threadIdx.x; e < E; e += kDecThreads) {
       const int r = e / HD, i = e - r * HD;
       const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
       const float2 cs = p.half ? __ldg(rope + jj) : make_float2(0.f, 0.f);
-      qs[e] = __float2half_rn(rope_clip(p.qf + (static_cast<int64_t>(g) * rep + r) * HD, i, p.half, cs.x, cs.y));
+      qs[e] = __float2half_rn(rope_clip(qf + (static_cast<int64_t>(gl) * rep + r) * HD, i, p.half, cs.x, cs.y));
     }
     if (split == S - 1) {
       for (int i = threadIdx.x; i < HD; i += kDecThreads) {
         const int jj = i < 2 * p.half ? (i < p.half ? i : i - p.half) : 0;
         const float2 cs = p.half ? __ldg(rope + jj) : make_float2(0.f, 0.f);
         const int64_t row = (static_cast<int64_t>(g) * p.max_t + pos) * HD;
-        p.kw[row + i] = __float2half_rn(rope_clip(p.kf + static_cast<int64_t>(g) * HD, i, p.half, cs.x, cs.y));
-        p.vw[row + i] = __float2half_rn(fminf(fmaxf(__ldg(p.vf + static_cast<int64_t>(g) * HD + i), -1000.f), 1000.f));
+        p.kw[row + i] = __float2half_rn(rope_clip(kf + static_cast<int64_t>(gl) * HD, i, p.half, cs.x, cs.y));
+        p.vw[row + i] = __float2half_rn(fminf(fmaxf(__ldg(vf + static_cast<int64_t>(gl) * HD + i), -1000.f), 1000.f));
       }
     }
     __syncthreads();
@@ -1259,7 +1268,10 @@ namespace attn {
 template <int HD, bool FUSED>
 int launch_decode(DecodeParams p, void* workspace, int64_t ws_bytes, cudaStream_t stream) {
   int C = 1, X = 1;
-  int rc = decode_splits<HD>(p.nkv, p.t, &C, &X);
+  if (p.nkv_seq <= 0) p.nkv_seq = p.nkv;
+  // the split plan of ONE sequence, so a batched step splits every sequence's cache exactly as
+  // a single-sequence step would (same partial sums in the same order)
+  int rc = decode_splits<HD>(p.nkv_seq, p.t, &C, &X);
   if (rc) return rc;
   const int64_t need = decode_counter_bytes(p.nkv) + static_cast<int64_t>(p.nkv) * X * decode_group_bytes(p.nq, p.nkv, HD);
   if (X > 1)
@@ -1368,6 +1380,49 @@ extern "C" int pyre_attn_decode_step(const float* q, const float* k, const float
                                      float* out, void* workspace, int64_t ws_bytes, void* stream) {
   return attn::decode_step(q, k, v, start_pos, nullptr, rope_table, rope_fraction, nq, nkv, hd, k_cache, v_cache,
                            max_t, mask_lo, mask_hi, out, workspace, ws_bytes, stream, "pyre_attn_decode_step");
+}
+
+extern "C" int pyre_attn_decode_step_batch(const float* q, const float* k, const float* v, int64_t qkv_stride,
+                                           int B, const int* pos_dev, int plan_pos, const float* rope_table,
+                                           double rope_fraction, int nq, int nkv, int hd, uint16_t* k_cache,
+                                           uint16_t* v_cache, int max_t, float* out, void* workspace,
+                                           int64_t ws_bytes, void* stream) {
+  PYRE_CHECK_ARG(B >= 1 && B <= 64, "pyre_attn_decode_step_batch: 1 <= B <= 64 sequences");
+  PYRE_CHECK_ARG(qkv_stride >= static_cast<int64_t>(nq + 2 * nkv) * hd,
+                 "pyre_attn_decode_step_batch: row stride smaller than the q, k and v of a token");
+  PYRE_CHECK_ARG(q && k && v && k_cache && v_cache && out, "pyre_attn_decode_step_batch: null pointer");
+  PYRE_CHECK_ARG(plan_pos >= 0 && plan_pos < max_t && nkv >= 1 && nq % nkv == 0 && nq / nkv <= kDecMaxRep,
+                 "pyre_attn_decode_step_batch: bad sizes (cache full, or more than 8 query heads per kv head)");
+  PYRE_CHECK_ARG(hd == 64 || hd == 128, "pyre_attn_decode_step_batch: head dim must be 64 or 128");
+  PYRE_CHECK_ARG(reinterpret_cast<uintptr_t>(k_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(v_cache) % 16 == 0,
+                 "pyre_attn_decode_step_batch: the caches must be 16-byte aligned");
+  const int dims = static_cast<int>(static_cast<double>(hd) * rope_fraction);
+  PYRE_CHECK_ARG(dims >= 0 && dims <= hd, "pyre_attn_decode_step_batch: rope_fraction must be in [0, 1]");
+  const int half = dims >= 2 ? dims / 2 : 0;
+  PYRE_CHECK_ARG(rope_table != nullptr || half == 0, "pyre_attn_decode_step_batch: null RoPE table");
+  DecodeParams p{};
+  p.kc = reinterpret_cast<const __half*>(k_cache);
+  p.vc = reinterpret_cast<const __half*>(v_cache);
+  p.kw = reinterpret_cast<__half*>(k_cache);
+  p.vw = reinterpret_cast<__half*>(v_cache);
+  p.qf = q;
+  p.kf = k;
+  p.vf = v;
+  p.rope = half ? reinterpret_cast<const float2*>(rope_table) + static_cast<int64_t>(plan_pos) * half : nullptr;
+  p.rope_base = reinterpret_cast<const float2*>(rope_table);
+  p.pos_dev = pos_dev;
+  p.half = half;
+  p.out = out;
+  p.nq = nq * B;
+  p.nkv = nkv * B;
+  p.nkv_seq = nkv;
+  p.q_bstride = qkv_stride;
+  p.kv_bstride = qkv_stride;
+  p.t = plan_pos + 1;
+  p.max_t = max_t;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return hd == 64 ? launch_decode<64, true>(p, workspace, ws_bytes, st)
+                  : launch_decode<128, true>(p, workspace, ws_bytes, st);
 }
 
 extern "C" int pyre_attn_decode_step_dev(const float* q, const float* k, const float* v, const int* pos_dev,

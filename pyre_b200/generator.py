@@ -34,7 +34,7 @@ import torch
 
 from . import _device as D
 from . import _native as N
-from .attention.ops import AttentionOp, Q80Linear
+from .attention.ops import AttentionOp, KVCache, Q80Linear
 from .ffn.op import FfnShardOp, FfnWeights
 from .lmhead import LmHeadOp
 from .quantizer import Q80Weight
@@ -61,7 +61,7 @@ class DecoderDesc(ctypes.Structure):
                 ("lm_ws_bytes", ctypes.c_int64)] + \
                [(n, ctypes.c_void_p) for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f", "status", "key",
                                                 "pos_dev", "history", "comm")] + \
-               [("lm_v0", ctypes.c_int64), ("lm_V", ctypes.c_int)]
+               [("lm_v0", ctypes.c_int64), ("lm_V", ctypes.c_int), ("batch", ctypes.c_int)]
 
 
 def check_struct_layout() -> None:
@@ -144,7 +144,7 @@ class _Layer:
     GPU), its FFN shard, norms, KV cache and the kernels' scratch."""
 
     def __init__(self, lw: dict, H: int, nq: int, nkv: int, hd: int, max_seq: int, max_prompt: int, theta: float,
-                 frac: float, device, heads=None, ffn_range=None, comm=None):
+                 frac: float, device, heads=None, ffn_range=None, comm=None, batch: int = 1):
         attn, ffn = lw["attn"], lw["ffn"]
         q, k, v, o = (_q80(attn[n], device) for n in ("q", "k", "v", "o"))
         if q.shape != (H, nq * hd) or k.shape != (H, nkv * hd) or v.shape != (H, nkv * hd) or o.shape != (nq * hd, H):
@@ -174,6 +174,21 @@ class _Layer:
         self.ln1 = _vec(lw["input_layernorm"], H, device)
         self.ln2 = _vec(lw["post_attention_layernorm"], H, device)
         self.attn = AttentionOp(self.nq, self.nkv, hd, max_seq, rope_theta=theta, rope_fraction=frac, device=device)
+        self.attns = [self.attn]
+        self.batch_ws = None
+        if batch > 1:
+            # a static batch: the sequences' caches stacked [B, nkv, max_t, hd] (the batched decode
+            # step reads them as B * nkv kv heads), one attention op per sequence over its slice
+            self.kv_k = torch.zeros((batch, self.nkv, max_seq, hd), dtype=torch.float16, device=device)
+            self.kv_v = torch.zeros_like(self.kv_k)
+            self.attns = [AttentionOp(self.nq, self.nkv, hd, max_seq, rope_theta=theta, rope_fraction=frac,
+                                      device=device, cache=KVCache(self.nkv, max_seq, hd, device, self.kv_k[b],
+                                                                   self.kv_v[b]), rope=self.attn.rope)
+                          for b in range(batch)]
+            self.attn = self.attns[0]
+            nb = ctypes.c_int64(0)
+            N.call("pyre_attn_decode_workspace_bytes", batch * self.nq, batch * self.nkv, hd, max_seq, ctypes.byref(nb))
+            self.batch_ws = torch.zeros(int(nb.value), dtype=torch.uint8, device=device)
 
     def o_proj(self, a: torch.Tensor, stream=None) -> torch.Tensor:
         """a @ Wo for this rank's heads; with tensor parallelism summed over the ranks (the
@@ -194,13 +209,17 @@ class Generator:
 
     def __init__(self, layers: list[dict], embedding, final_norm=None, *, n_heads: int, n_kv_heads: int,
                  head_dim: int, rope_theta: float = 10000.0, rope_fraction: float = 1.0, eps: float = 1e-6,
-                 lm_head=None, max_seq: int = 4096, max_prompt: int = 64, device=None, comm=None, ffn_plan=None):
+                 lm_head=None, max_seq: int = 4096, max_prompt: int = 64, device=None, comm=None, ffn_plan=None,
+                 batch: int = 1):
         """``comm`` (a :class:`~pyre_b200.tp.TPComm` of hidden size H and at least ``max_prompt``
         tokens) makes this object one rank of a tensor-parallel decoder: it keeps the heads
         :func:`head_split` gives its rank (QKV columns, O rows, KV cache), the FFN columns
         ``ffn_plan`` (a :class:`~pyre_b200.tp.ShardPlan`, default equal 32-blocks) gives it and
         the lm_head rows of :func:`vocab_split`; every rank is given the same full weights and
-        runs the same calls. Without it the whole model runs on this GPU."""
+        runs the same calls. Without it the whole model runs on this GPU.
+
+        ``batch`` > 1 keeps that many KV caches per layer for a static batch of equally long
+        prompts decoded in lockstep (:meth:`generate_batch`)."""
         D.require_cuda()
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev = self.device
@@ -227,13 +246,18 @@ class Generator:
             raise ValueError("ffn_plan does not match the FFN width or the world size")
         ffn_range = ffn_plan.bounds[rank] if world > 1 else None
         self.lm_v0, v1 = vocab_split(self.V, world)[rank]
-        self.lm_head = LmHeadOp(table[self.lm_v0:v1].contiguous(), fn, eps, vocab_start=self.lm_v0, comm=comm)
+        if not 1 <= batch <= 64:
+            raise ValueError("batch must be in [1, 64]")
+        self.batch = int(batch)
+        self.lm_head = LmHeadOp(table[self.lm_v0:v1].contiguous(), fn, eps, vocab_start=self.lm_v0, comm=comm,
+                                max_tokens=min(4, self.batch))
         self.eps = float(eps)
         self.n_heads, self.n_kv_heads = n_heads, n_kv_heads
         self.nq, self.nkv, self.hd = heads[0][1] - heads[0][0], heads[1][1] - heads[1][0], head_dim
         self.max_seq, self.max_prompt = int(max_seq), int(max_prompt)
         self.layers = [_Layer(lw, self.H, n_heads, n_kv_heads, head_dim, self.max_seq, self.max_prompt, rope_theta,
-                              rope_fraction, dev, heads=heads, ffn_range=ffn_range, comm=comm) for lw in layers]
+                              rope_fraction, dev, heads=heads, ffn_range=ffn_range, comm=comm, batch=self.batch)
+                       for lw in layers]
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.length = 0
         self._desc = self._native_desc()
@@ -251,19 +275,21 @@ class Generator:
         if len(widths) != 1:
             raise ValueError("every layer needs the same FFN width")
         nqkv = (self.nq + 2 * self.nkv) * self.hd
-        self._buf = {n: torch.zeros(k, dtype=torch.float32, device=dev)
+        B = self.batch
+        self._buf = {n: torch.zeros(B * k, dtype=torch.float32, device=dev)
                      for n, k in (("x", H), ("xn", H), ("hn", H), ("qkv", nqkv), ("attn", self.nq * self.hd),
                                   ("ao", H), ("f", H))}
-        self._key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._key = torch.zeros(B, dtype=torch.int64, device=dev)
         arr = (DecoderLayerDesc * len(self.layers))()
         for i, L in enumerate(self.layers):
+            kc, vc = (L.kv_k, L.kv_v) if B > 1 else (L.attn.cache.k, L.attn.cache.v)
+            aws = L.batch_ws if B > 1 else L.attn.dec_ws
             arr[i] = DecoderLayerDesc(
                 L.qkv.w.data.data_ptr(), L.qkv.workspace.data_ptr(), L.qkv.workspace.numel(),
                 L.o.w.data.data_ptr(), L.o.workspace.data_ptr(), L.o.workspace.numel(),
                 L.ffn_w.gateup.data.data_ptr(), L.ffn_w.down.data.data_ptr(), int(L.ffn_w.gated),
                 L.ffn.workspace.data_ptr(), L.ffn.workspace.numel(), L.ln1.data_ptr(), L.ln2.data_ptr(),
-                L.attn.cache.k.data_ptr(), L.attn.cache.v.data_ptr(), L.attn.rope.data_ptr(),
-                L.attn.dec_ws.data_ptr(), L.attn.dec_ws.numel(),
+                kc.data_ptr(), vc.data_ptr(), L.attn.rope.data_ptr(), aws.data_ptr(), aws.numel(),
                 L.qkv.bias.data_ptr() if L.qkv.bias is not None else None)
         self._layer_arr = arr
         lm = self.lm_head
@@ -274,13 +300,13 @@ class Generator:
                         lm.workspace.data_ptr(), lm.workspace.numel(),
                         *(self._buf[n].data_ptr() for n in ("x", "xn", "hn", "qkv", "attn", "ao", "f")),
                         self.status.data_ptr(), self._key.data_ptr(), None, None,
-                        self.comm.handle if self.comm is not None else None, self.lm_v0, lm.V)
+                        self.comm.handle if self.comm is not None else None, self.lm_v0, lm.V, B)
         return d
 
     # ---- one pass of the decoder over T new tokens ------------------------------------------
-    def _forward(self, ids: torch.Tensor, prefill: bool, stream=None) -> torch.Tensor:
-        """ids: int32 [T] on the device (the prompt, or one decode token). Returns the last
-        hidden state, f32 [1, H]."""
+    def _forward(self, ids: torch.Tensor, prefill: bool, stream=None, seq: int = 0) -> torch.Tensor:
+        """ids: int32 [T] on the device (the prompt, or one decode token) of batch sequence
+        ``seq``. Returns the last hidden state, f32 [1, H]."""
         T, H = ids.numel(), self.H
         s = D.stream_ptr(stream)
         x = torch.empty((T, H), dtype=torch.float32, device=self.device)
@@ -293,7 +319,8 @@ class Generator:
         for i, L in enumerate(self.layers):
             qkv = L.qkv(xn, stream=stream)
             q, k, v = qkv[:, :nq_w], qkv[:, nq_w:nq_w + nkv_w], qkv[:, nq_w + nkv_w:]
-            a = L.attn.prefill(q, k, v, stream=stream) if prefill else L.attn.decode(q, k, v, stream=stream)
+            att = L.attns[seq]
+            a = att.prefill(q, k, v, stream=stream) if prefill else att.decode(q, k, v, stream=stream)
             ao = L.o_proj(a, stream=stream)
             N.call("pyre_add_rms_norm", D.ptr(x), D.ptr(ao), T, H, D.ptr(L.ln2), self.eps, D.ptr(x), D.ptr(hn), s)
             f = L.ffn.run(hn, L.ffn_w, stream=stream)
@@ -304,7 +331,8 @@ class Generator:
 
     def reset(self) -> None:
         for L in self.layers:
-            L.attn.reset()
+            for a in L.attns:
+                a.reset()
         self.length = 0
 
     # captured prefill graphs kept at once (least recently used dropped first)
@@ -348,10 +376,75 @@ class Generator:
         with torch.cuda.stream(self._pf_stream):
             g.replay()
         cur.wait_stream(self._pf_stream)
-        self.length = T
-        for L in self.layers:
-            L.attn.cache.length = T
+        self._set_length(T)
         return tok
+
+    def _one_sequence(self, what: str) -> None:
+        if self.batch > 1:
+            raise ValueError(f"{what} runs one sequence; a Generator with batch > 1 uses prefill_batch / "
+                             "generate_batch")
+
+    def prefill_batch(self, prompts, want_logits: bool = False):
+        """The prompts of a static batch (``batch`` prompts of equal length, ids [B, T]), each run
+        as one pass into its own caches (the same kernels as :meth:`prefill`). Returns the B first
+        greedy tokens, int32 [B] on the device (and their logits f32 [B, V] of this rank's
+        vocabulary rows with want_logits)."""
+        B = self.batch
+        if B < 2:
+            raise ValueError("prefill_batch needs a Generator with batch > 1")
+        ids = np.asarray(prompts)
+        if ids.ndim != 2 or ids.shape[0] != B or not 1 <= ids.shape[1] <= self.max_prompt:
+            raise ValueError(f"prompts must be [{B}, T] ids with 1 <= T <= {self.max_prompt}")
+        if ids.min() < 0 or ids.max() >= self.V:
+            raise ValueError(f"token ids must be in [0, {self.V})")
+        self.reset()
+        dev_ids = torch.as_tensor(ids.astype(np.int32)).to(self.device)
+        h = torch.empty((B, self.H), dtype=torch.float32, device=self.device)
+        for b in range(B):
+            h[b].copy_(self._forward(dev_ids[b], True, seq=b)[0])
+        toks = torch.empty(B, dtype=torch.int32, device=self.device)
+        logits = torch.empty((B, self.lm_head.V), dtype=torch.float32, device=self.device) if want_logits else None
+        for r0 in range(0, B, 4):
+            n = min(4, B - r0)
+            out = self.lm_head(h[r0:r0 + n], want_logits=want_logits)
+            t, lg = (out if want_logits else (out, None))
+            toks[r0:r0 + n].copy_(t.reshape(-1))
+            if want_logits:
+                logits[r0:r0 + n].copy_(lg)
+        self._set_length(int(ids.shape[1]))
+        return (toks, logits) if want_logits else toks
+
+    def generate_batch(self, prompts, max_tokens: int, want_logits: bool = False, graphed: bool = True):
+        """Greedy ids of a static batch (``Generator.generate`` at temperature 0 for each of B
+        equally long prompts, decoded in lockstep): a list of B lists of ``max_tokens`` ids. Each
+        decode step runs the projections and the FFN on the B tokens together (row groups of at
+        most 4, one weight pass per group) and the attention of all B sequences in one launch;
+        every sequence's arithmetic is that of a one-sequence run. graphed: steps replayed from
+        CUDA graphs (no logits); else one pyre_decoder_step call per step, with want_logits the
+        logits [max_tokens, B, V] on the device."""
+        B = self.batch
+        if max_tokens < 1 or max_tokens > self.max_seq + 1:
+            raise ValueError("max_tokens out of range")
+        if graphed and want_logits:
+            raise ValueError("graphed decoding returns no logits")
+        out = self.prefill_batch(prompts, want_logits=want_logits)
+        first, lg0 = (out if want_logits else (out, None))
+        if graphed:
+            start = self.length
+            hist = self.decode_graphed(first, max_tokens - 1)
+            self.check_status()
+            return hist[:, start:start + max_tokens].cpu().tolist()
+        toks = torch.zeros((max_tokens, B), dtype=torch.int32, device=self.device)
+        toks[0].copy_(first)
+        logits = None
+        if want_logits:
+            logits = torch.empty((max_tokens, B, self.lm_head.V), dtype=torch.float32, device=self.device)
+            logits[0].copy_(lg0)
+        for i in range(1, max_tokens):
+            self.step_into(toks[i - 1], toks[i], logits[i] if want_logits else None)
+        self.check_status()
+        ids = toks.t().cpu().tolist()
+        return (ids, logits) if want_logits else ids
 
     def prefill(self, ids, want_logits: bool = False, stream=None, stepwise: bool = False, graphed: bool = False):
         """Run the prompt (a fresh sequence) and return the first greedy token, int64 [1, 1] on
@@ -364,6 +457,7 @@ class Generator:
         dequantized weights (slower; the reference computes every prompt position in f32).
         ``graphed`` replays the one-pass prefill from a CUDA graph captured per prompt length
         (no logits; the returned token tensor is reused by the next graphed prefill)."""
+        self._one_sequence("prefill")
         ids = np.asarray(ids).reshape(-1)
         if ids.size < 1 or ids.size > self.max_prompt:
             raise ValueError(f"prompt length {ids.size} outside [1, {self.max_prompt}]")
@@ -391,6 +485,7 @@ class Generator:
     def step(self, token: torch.Tensor, want_logits: bool = False, stream=None):
         """One decode step on the previous greedy token (int [1, 1] on the device), op by op
         from Python (:meth:`step_into` is the same step in one native call)."""
+        self._one_sequence("step")
         if self.length == 0:
             raise ValueError("step() needs a prefill() first")
         if self.length + 1 > self.max_seq:
@@ -412,13 +507,20 @@ class Generator:
         for t in (token_in, token_out):
             if t.dtype != torch.int32 or not t.is_cuda:
                 raise ValueError("tokens must be int32 on the device")
-        if logits is not None and (logits.dtype != torch.float32 or logits.numel() != self.lm_head.V):
-            raise ValueError(f"logits must be f32 with {self.lm_head.V} elements (this rank's vocabulary rows)")
+        B = self.batch
+        if token_in.numel() < B or token_out.numel() < B:
+            raise ValueError(f"token_in and token_out need {B} entries (one per sequence)")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() != B * self.lm_head.V):
+            raise ValueError(f"logits must be f32 with {B} x {self.lm_head.V} elements (this rank's vocabulary rows)")
         N.call("pyre_decoder_step", ctypes.byref(self._desc), D.ptr(token_in), self.length, 0, 0, D.ptr(token_out),
                D.ptr(logits), D.stream_ptr(stream))
-        self.length += 1
+        self._set_length(self.length + 1)
+
+    def _set_length(self, n: int) -> None:
+        self.length = n
         for L in self.layers:
-            L.attn.cache.length = self.length
+            for a in L.attns:
+                a.cache.length = n
 
     def decode_graphed(self, first_token: torch.Tensor, n_steps: int, steps_per_graph: int = 16,
                        bucket: int = 512) -> torch.Tensor:
@@ -428,17 +530,19 @@ class Generator:
         tokens with one host call. The attention grids of a graph are planned for the first
         position of its ``bucket``-wide position range and the graph is replayed for every
         position in that range (captured graphs are cached on this object). first_token: the
-        prefill's greedy token. Returns the int32 device tensor of all tokens by position
-        (entries prompt length .. prompt length + n_steps)."""
+        prefill's greedy token (one per sequence for a batch). Returns the int32 device tensor of
+        all tokens by position (entries prompt length .. prompt length + n_steps), [max_seq + 1],
+        or [batch, max_seq + 1] for a batch."""
         if self.length == 0:
             raise ValueError("decode_graphed() needs a prefill() first")
         if self.length + n_steps > self.max_seq:
             raise ValueError("sequence longer than max_seq")
         dev = self.device
+        B = self.batch
         if not hasattr(self, "_gdesc"):
             self._gpos = torch.zeros(1, dtype=torch.int32, device=dev)
-            self._gslot = torch.zeros(1, dtype=torch.int32, device=dev)
-            self._ghist = torch.zeros(self.max_seq + 1, dtype=torch.int32, device=dev)
+            self._gslot = torch.zeros(B, dtype=torch.int32, device=dev)
+            self._ghist = torch.zeros(B * (self.max_seq + 1), dtype=torch.int32, device=dev)
             self._gdesc = DecoderDesc.from_buffer_copy(self._desc)
             self._gdesc.pos_dev = self._gpos.data_ptr()
             self._gdesc.history = self._ghist.data_ptr()
@@ -446,8 +550,9 @@ class Generator:
             self._graphs = {}
         start = self.length
         self._gpos.fill_(start)
-        self._gslot.copy_(first_token.reshape(-1)[:1].to(torch.int32))
-        self._ghist[start:start + 1].copy_(self._gslot)
+        self._gslot.copy_(first_token.reshape(-1)[:B].to(torch.int32))
+        hist = self._ghist.view(B, self.max_seq + 1)
+        hist[:, start].copy_(self._gslot)
         cur = torch.cuda.current_stream(dev)
         self._gstream.wait_stream(cur)
         pos, left = start, n_steps
@@ -468,10 +573,8 @@ class Generator:
             pos += k
             left -= k
         cur.wait_stream(self._gstream)
-        self.length = pos
-        for L in self.layers:
-            L.attn.cache.length = pos
-        return self._ghist
+        self._set_length(pos)
+        return self._ghist if B == 1 else hist
 
     def check_status(self) -> None:
         """Raise if a kernel reported a problem: the embedding gather's status word and the
@@ -505,6 +608,7 @@ class Generator:
         pyre_decoder_step (else op by op from Python); stepwise_prefill: see :meth:`prefill`;
         graphed: decode steps as CUDA-graph replays (:meth:`decode_graphed`, no logits). With
         tensor parallelism the logits are this rank's vocabulary rows (lm_v0 onwards)."""
+        self._one_sequence("generate_ids")
         if max_tokens < 1 or max_tokens > self.max_seq + 1:
             raise ValueError("max_tokens out of range")
         if graphed and want_logits:
