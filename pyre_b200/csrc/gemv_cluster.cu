@@ -36,11 +36,15 @@ constexpr int kThreadsC = kConsumers + 32;          // 8 consumer warps + 1 prod
 template <typename ST>
 constexpr int block_bytes() { return kRows * kTileN + kRows * 8 * static_cast<int>(sizeof(ST)); }
 
+// Shared memory: partial [T][256] | warp partials [warps][T][256] | barriers (128 B) |
+// x [T][units*64] f32 | blocks. The partial comes first so that it sits at the same offset in
+// every rank of the cluster (the ranks read each other's partials through distributed shared
+// memory at the address of their own), whatever each rank's block count.
+template <int T>
+constexpr int head_bytes() { return T * kTileN * 4 + kConsumerWarps * T * kTileN * 4 + 128; }
 template <int T, typename ST>
 constexpr int smem_bytes(int units) {
-  // stages | x [T][units*64] f32 | warp partials [warps][T][256] | partial [T][256] | barriers
-  return units * block_bytes<ST>() + T * units * kRows * 4 + kConsumerWarps * T * kTileN * 4 + T * kTileN * 4 +
-         kMaxUnits * 8 + 16;
+  return head_bytes<T>() + T * units * kRows * 4 + units * block_bytes<ST>();
 }
 
 struct Params {
@@ -106,10 +110,11 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
   const int u1 = static_cast<int>(static_cast<int64_t>(p.upt) * (rank + 1) / C);
   const int nu = u1 - u0;                    // 1..kMaxUnits (the host picks C so)
   const int pitch = nu * kRows;
-  float* xs = reinterpret_cast<float*>(smem + nu * kBB);
-  float* red = xs + T * pitch;
-  float* fin = red + kConsumerWarps * T * kTileN;
-  uint64_t* full = reinterpret_cast<uint64_t*>(fin + T * kTileN);
+  float* fin = reinterpret_cast<float*>(smem);                        // same offset in every rank
+  float* red = fin + T * kTileN;
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * T * kTileN);
+  float* xs = reinterpret_cast<float*>(smem + head_bytes<T>());
+  uint8_t* blocks = smem + head_bytes<T>() + T * pitch * 4;          // 16-byte aligned
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < nu; ++i) mbar_init(&full[i], 1);
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
     const uint8_t* src = p.w + (static_cast<int64_t>(tile) * p.upt + u0) * kBB;
     for (int i = 0; i < nu; ++i) {
       mbar_arrive_expect_tx(&full[i], kBB);
-      bulk_load(smem + i * kBB, src + static_cast<int64_t>(i) * kBB, kBB, &full[i]);
+      bulk_load(blocks + i * kBB, src + static_cast<int64_t>(i) * kBB, kBB, &full[i]);
     }
   }
   pdl_wait();      // x comes from the previous kernel of the stream
@@ -139,7 +144,7 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
     zero_acc<1, T>(acc);
     for (int i = 0; i < nu; ++i) {
       mbar_wait(&full[i], 0, p.status);
-      consume_block<T, ST>(smem + i * kBB, xs + i * kRows, pitch, acc, warp, rs, cc);
+      consume_block<T, ST>(blocks + i * kBB, xs + i * kRows, pitch, acc, warp, rs, cc);
     }
     reduce_tile<T, 1>(acc, red, fin, warp, rs, cc, tid);   // fin[t * 256 + c]: this CTA's partial
   }
