@@ -416,6 +416,25 @@ PYRE_API int pyre_decoder_struct_sizes(int64_t* layer_bytes, int64_t* desc_bytes
 PYRE_API int pyre_decoder_step(const pyre_decoder_desc* d, const int* token_in, int pos, int mask_lo, int mask_hi,
                                int* token_out, float* logits, void* stream);
 
+/* The same decode step with every layer in ONE persistent launch (RootNode._decode_single_layer,
+ * root_node.py:739-1007, for all layers; Generator's decode loop, generator.py:117-131):
+ * embedding gather -> decode_persistent_kernel (one CTA per SM for the whole token: a work queue
+ * of QKV, attention, O, FFN gate/up and down items over all layers, weight blocks and KV rows
+ * streamed through a shared-memory ring while the consumers wait on the previous stage's
+ * flags) -> lm_head_argmax (-> position advance with pos_dev). Same arguments and results as
+ * pyre_decoder_step for one sequence on one GPU (batch <= 1, comm NULL, f16 scales, head_dim 64
+ * or 128, (nq / nkv) * head_dim <= 512, H, nq * hd and ffn_width multiples of 64), no prefill
+ * mask; the per-layer scratch workspaces of the descriptor are not used. workspace:
+ * pyre_decoder_persistent_workspace_bytes(d) bytes, 256-byte aligned, zeroed once and reused
+ * call after call on one stream (every call leaves it ready for the next). A bounded wait that
+ * ran out, an out-of-range partial or a graphed position outside the cache leaves PYRE_ETIMEOUT /
+ * PYRE_ERANGE / PYRE_EINVAL in the workspace's status word (pyre_decoder_persistent_status). */
+PYRE_API int pyre_decoder_persistent_workspace_bytes(const pyre_decoder_desc* d, int64_t* bytes);
+PYRE_API int pyre_decoder_step_persistent(const pyre_decoder_desc* d, void* workspace, int64_t ws_bytes,
+                                          const int* token_in, int pos, int* token_out, float* logits, void* stream);
+/* Reads the persistent workspace's status word (synchronous copy; 0 = no problem). */
+PYRE_API int pyre_decoder_persistent_status(const void* workspace, int* status);
+
 /* ---- Ulysses sequence parallelism over NVLink (one process per GPU, P <= 16) ----------
  * Replaces the gather of every node's q/k/v at the root over TCP and the full-sequence
  * attention there (src/orchestrator/root_node.py:250-314; Ulysses mode :110): rank r owns

@@ -80,6 +80,9 @@ _SIGNATURES = {
     "pyre_attn_decode_step_batch": [_vp, _vp, _vp, _c_i64, _i, _vp, _i, _vp, ctypes.c_double, _i, _i, _i, _vp, _vp,
                                     _i, _vp, _vp, _c_i64, _vp],
     "pyre_decoder_struct_sizes": [_vp, _vp],
+    "pyre_decoder_persistent_workspace_bytes": [_vp, ctypes.POINTER(_c_i64)],
+    "pyre_decoder_persistent_status": [_vp, ctypes.POINTER(_i)],
+    "pyre_decoder_step_persistent": [_vp, _vp, _c_i64, _vp, _i, _vp, _vp, _vp],
     "pyre_embed_rms_norm": [_vp, _i, _vp, _i, _i, _vp, ctypes.c_double, _vp, _vp, _vp, _vp],
     "pyre_softmax_rows": [_vp, _c_i64, _i, _vp, _vp],
     "pyre_rope_table": [ctypes.c_double, ctypes.c_double, _i, _i, _vp],

@@ -43,9 +43,10 @@ def device_weights(m: "gm.Model", device):
     return emb, out, final_norm, head
 
 
-def generator(m: "gm.Model", device, comm=None, ffn_plan=None):
+def generator(m: "gm.Model", device, comm=None, ffn_plan=None, persistent=False):
     from pyre_b200.generator import Generator
     emb, layers, final_norm, head = device_weights(m, device)
     return Generator(layers, emb, final_norm, n_heads=m.n_heads, n_kv_heads=m.n_kv, head_dim=m.head_dim,
                      rope_theta=m.theta, eps=m.eps, lm_head=head, max_seq=m.prompt_len + gm.N_GREEDY + 16,
-                     max_prompt=max(64, m.prompt_len), device=device, comm=comm, ffn_plan=ffn_plan)
+                     max_prompt=max(64, m.prompt_len), device=device, comm=comm, ffn_plan=ffn_plan,
+                     persistent=persistent)

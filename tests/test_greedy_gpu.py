@@ -41,9 +41,9 @@ def test_golden_prompts_are_the_seeded_prompts():
         assert g["top_idx"].shape == (gm.N_GREEDY, 8) and np.array_equal(g["top_idx"][:, 0], g["tokens"])
 
 
-def _gen(name):
+def _gen(name, persistent=False):
     import torch
-    return G.generator(gm.MODELS[name], torch.device("cuda", 0))
+    return G.generator(gm.MODELS[name], torch.device("cuda", 0), persistent=persistent)
 
 
 def _check_run(g, ids, lg):
@@ -61,25 +61,28 @@ def _check_run(g, ids, lg):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", DECIDABLE)
-@pytest.mark.parametrize("native", [True, False], ids=["decoder_step", "op_by_op"])
-def test_greedy_tokens_match_reference(name, native):
-    """Default path: one-pass prefill, then decode steps (one native call per token, or op by
-    op from Python), with every step's logits."""
+@pytest.mark.parametrize("mode", ["persistent", "decoder_step", "op_by_op"])
+def test_greedy_tokens_match_reference(name, mode):
+    """Default path: one-pass prefill, then decode steps (one native call per token: the
+    persistent one-launch step or the launch-per-op step; or op by op from Python), with every
+    step's logits."""
     g = G.golden(gm.MODELS[name])
-    gen = _gen(name)
-    ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=native)
+    gen = _gen(name, persistent=mode == "persistent")
+    assert gen.persistent == (mode == "persistent")
+    ids, logits = gen.generate_ids(g["prompt"], gm.N_GREEDY, want_logits=True, native=mode != "op_by_op")
     _check_run(g, ids, logits.cpu().numpy())
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", DECIDABLE)
-def test_greedy_tokens_graphed(name):
+@pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "decoder_step"])
+def test_greedy_tokens_graphed(name, persistent):
     """The benchmarked path: prefill replayed from a CUDA graph, decode steps replayed from
     CUDA graphs (position read and advanced on the device), twice in a row (the second run
     replays the cached graphs); then graphs of 5 steps over 16-position buckets, so the run
     crosses bucket boundaries and replans the attention grid."""
     g = G.golden(gm.MODELS[name])
-    gen = _gen(name)
+    gen = _gen(name, persistent=persistent)
     for _ in range(2):
         assert gen.generate_ids(g["prompt"], gm.N_GREEDY, graphed=True) == g["tokens"].tolist()
     tok = gen.prefill(g["prompt"])
