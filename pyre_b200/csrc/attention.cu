@@ -366,6 +366,13 @@ constexpr int kDecMaxGroups = 8;       // X, clusters per kv head
 constexpr int kDecMinChunk = 128;      // positions per CTA at least (one batch per warp)
 constexpr int kDecGroupChunk = 2048;   // positions per cluster before another cluster is added
 
+constexpr int64_t kDecPrefetchBytes = 32768;   // bytes per L2 prefetch instruction
+
+// Brings [src, src + bytes) into L2 (16-byte aligned, bytes % 16 == 0); nothing to wait for.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Status word of the attention kernels (read and cleared by pyre_attn_status).
 __device__ int g_attn_status;
 
@@ -550,6 +557,31 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(const Decod
   const int C = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
   const int split = blockIdx.x, S = gridDim.x, g = blockIdx.y;
+  {
+    // This CTA's K and V rows into L2 while the previous kernel finishes. A prefetch only
+    // warms L2 (the loads below read whatever the rows hold after the wait), so the position it
+    // is planned from may be read before the wait.
+    int tp = p.t;
+    if constexpr (FUSED) {
+      if (p.pos_dev != nullptr) {
+        const int q = *reinterpret_cast<const volatile int*>(p.pos_dev);
+        if (q >= 0 && q < p.max_t) tp = q + 1;
+      }
+    }
+    if (threadIdx.x == 0) {
+      const int a0 = static_cast<int>(static_cast<int64_t>(tp) * split / S);
+      const int a1 = static_cast<int>(static_cast<int64_t>(tp) * (split + 1) / S);
+      if (a1 > a0) {
+        const int64_t off = (static_cast<int64_t>(g) * p.max_t + a0) * HD;
+        const int64_t bytes = static_cast<int64_t>(a1 - a0) * HD * 2;
+        for (int64_t b = 0; b < bytes; b += kDecPrefetchBytes) {
+          const uint32_t n = static_cast<uint32_t>(bytes - b < kDecPrefetchBytes ? bytes - b : kDecPrefetchBytes);
+          prefetch_l2(reinterpret_cast<const char*>(p.kc + off) + b, n);
+          prefetch_l2(reinterpret_cast<const char*>(p.vc + off) + b, n);
+        }
+      }
+    }
+  }
   pdl_wait();      // q, k, v (and the position) come from the previous kernels of the stream
   pdl_trigger();
   int t = p.t;
