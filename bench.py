@@ -72,6 +72,10 @@ def parse():
     ap.add_argument("--decoder-only", action="store_true",
                     help="run only the decoder measurement on one GPU (for profiling) and print its JSON object")
     ap.add_argument("--decoder-prompt", type=int, default=2048)
+    ap.add_argument("--decoder-layers", type=int, default=L7,
+                    help="layers of the Mistral-7B-shaped decoder in --decoder-only runs (profiling a smaller model)")
+    ap.add_argument("--persistent", action="store_true",
+                    help="--decoder-only: decode through the persistent one-launch step (Generator(persistent=True))")
     ap.add_argument("--e2e-reps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=8, help="static batch of the second decode measurement (1: skip)")
     return ap.parse_args()
@@ -293,7 +297,7 @@ class ClockSampler:
 # GPU leg
 # ---------------------------------------------------------------------------------------
 
-def decoder_7b_weights(dev):
+def decoder_7b_weights(dev, n_layers: int = L7):
     """The Mistral-7B-shaped decoder's weights, identical on every rank (a seeded CUDA generator):
     Q8_0 N(0, 0.02) matrices (bf16-rounded, f16 scales), unit norms, f16 embedding and lm_head."""
     import torch
@@ -307,7 +311,7 @@ def decoder_7b_weights(dev):
     ones = torch.ones(H, device=dev)
     layers = [{"input_layernorm": ones, "post_attention_layernorm": ones,
                "attn": {"q": w(H, NQ7 * HD7), "k": w(H, NKV7 * HD7), "v": w(H, NKV7 * HD7), "o": w(NQ7 * HD7, H)},
-               "ffn": {"gate": w(H, I), "up": w(H, I), "down": w(I, H)}} for _ in range(L7)]
+               "ffn": {"gate": w(H, I), "up": w(H, I), "down": w(I, H)}} for _ in range(n_layers)]
     emb = (torch.randn((V7, H), generator=g, device=dev) * 0.02).half()
     head = (torch.randn((V7, H), generator=g, device=dev) * 0.02).half()
     return layers, emb, ones, head
@@ -323,9 +327,11 @@ def decoder_bench(dev, hbm, args, comm, world, barrier):
     import torch
     from pyre_b200.generator import Generator
     prompt, W, K = args.decoder_prompt, max(args.warmup, 3), args.steps
-    layers, emb, ones, head = decoder_7b_weights(dev)
+    n_layers = args.decoder_layers if args.decoder_only else L7
+    layers, emb, ones, head = decoder_7b_weights(dev, n_layers)
     gen = Generator(layers, emb, ones, n_heads=NQ7, n_kv_heads=NKV7, head_dim=HD7, rope_theta=1e6, lm_head=head,
-                    max_seq=prompt + W + K + 2, max_prompt=prompt, device=dev, comm=comm)
+                    max_seq=prompt + W + K + 2, max_prompt=prompt, device=dev, comm=comm,
+                    persistent=args.decoder_only and args.persistent)
     gen8 = None
     if args.batch > 1:
         gen8 = Generator(layers, emb, ones, n_heads=NQ7, n_kv_heads=NKV7, head_dim=HD7, rope_theta=1e6,
@@ -392,7 +398,17 @@ def decoder_bench(dev, hbm, args, comm, world, barrier):
         seq0 = hist[0, prompt:prompt + W + K + 1].cpu()
         batch_info = {"ms": b_ms, "batch": Bn, "seq0_equals_batch1": bool(torch.equal(seq0, timed_tokens))}
         del gen8
-    launches = 3 + 6 * L7 + (1 if comm is not None else 0)
+    if args.decoder_only:
+        # one decode step, one native call, inside an NVTX range: profilers select its launches
+        # by that range (ncu --nvtx --nvtx-include "decode_step/")
+        t_in = torch.tensor([int(out[-1])], dtype=torch.int32, device=dev)
+        t_out = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        gen.step_into(t_in, t_out)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    launches = 5 if gen.persistent else 3 + 6 * n_layers + (1 if comm is not None else 0)
     info = {"gen": gen, "dec_ms": dec_ms, "prefill_ms": min(pf), "e2e_s": statistics.median(e2e), "e2e_tokens": n_e2e,
             "launches_per_token": launches, "tokens_equal": bool(same), "ids_bytes": int(prompt) * 4,
             "out_bytes": n_e2e * 8, "batch": batch_info}
