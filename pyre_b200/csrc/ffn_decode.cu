@@ -14,14 +14,23 @@ int64_t stream_acc_bytes(int T, int N, int nmat) {
 }
 
 // Workspace layouts (after the kHeaderBytes header):
-//   MODE_A / MODE_B : accumulators of that phase
-//   MODE_AB         : accumulators A | accumulators B | ... | h [T, W] f32 at the end
-// The accumulators must be zero when a call starts (each call zeroes what it used); h and the
-// tensor-core GEMM's staging and partial tiles are plain data and sit at the END of the
-// workspace, so calls with any T (and of either path) can share one workspace.
-int64_t decode_ws_bytes(int T, int H, int W, int na) {
-  return kHeaderBytes + align256(static_cast<int64_t>(T) * W * 4) + stream_acc_bytes(T, W, na) +
-         stream_acc_bytes(T, H, 1);
+//   MODE_A / MODE_B : accumulators of that phase, from the start of the lead region
+//   MODE_AB         : accumulators B from the start of the lead region; after the lead region
+//                     (sized for T = PYRE_FUSED_REDUCE_MAX_T and both phases, so no call of
+//                     any T or mode reaches past it) the two sets of gate/up slab sums
+//                     [2][tiles(W)][kSlabSums] int64 and chunk counts [2][tiles(W)] u32
+// Everything in the lead region must be zero when a call starts (each call zeroes what it
+// used); the MODE_AB sets are cleared by alternate calls. The tensor-core GEMM's staging and
+// partial tiles are plain data and sit at the END of the workspace, so calls with any T (and
+// of either path) can share one workspace.
+int64_t lead_bytes(int H, int W) {
+  const int64_t a = stream_acc_bytes(PYRE_FUSED_REDUCE_MAX_T, W, 2);
+  const int64_t b = stream_acc_bytes(PYRE_FUSED_REDUCE_MAX_T, H, 1);
+  return a > b ? a : b;
+}
+int64_t ab_sums_bytes(int W) { return align256(2 * static_cast<int64_t>(tiles_of(W)) * kSlabSums * 8); }
+int64_t decode_ws_bytes(int H, int W) {
+  return kHeaderBytes + lead_bytes(H, W) + ab_sums_bytes(W) + align256(2 * static_cast<int64_t>(tiles_of(W)) * 4);
 }
 
 struct StreamArgs {
@@ -29,7 +38,7 @@ struct StreamArgs {
   bool tp;
   const void* xa;      // phase-A activation [T, KA]
   int xa_dtype;
-  const void* xb;      // phase-B activation [T, KB] (MODE_B); MODE_AB uses h in the workspace
+  const void* xb;      // phase-B activation [T, KB] (MODE_B); MODE_AB computes h from the slab sums
   int xb_dtype;
 };
 
@@ -44,9 +53,8 @@ int launch_stream(StreamParams p, const StreamArgs& a, cudaStream_t s) {
                       C::LA::kRows);
     if (rc) return rc;
   }
-  if constexpr ((MODE & MODE_B) != 0) {
-    const void* xb = MODE == MODE_AB ? p.outA : a.xb;
-    rc = make_tmap_2d(&p.txb, xb, tma_dtype<XB>(), sizeof(XB), T, p.KB, static_cast<uint64_t>(p.KB) * sizeof(XB), T,
+  if constexpr (MODE == MODE_B) {
+    rc = make_tmap_2d(&p.txb, a.xb, tma_dtype<XB>(), sizeof(XB), T, p.KB, static_cast<uint64_t>(p.KB) * sizeof(XB), T,
                       C::LB::kRows);
     if (rc) return rc;
   }
@@ -192,8 +200,7 @@ extern "C" int pyre_ffn_workspace_bytes(int T, int H, int W, int64_t* bytes) {
   // decode (T <= 4, also the two-call forms) at the start and, for larger T, the tensor-core
   // GEMM's f16 activation staging and partial tiles after it (placed from the end by the
   // GEMM calls): the two never overlap, so calls of either kind can follow each other
-  const int td = T < PYRE_FUSED_REDUCE_MAX_T ? T : PYRE_FUSED_REDUCE_MAX_T;
-  int64_t need = decode_ws_bytes(td, H, W, 2);
+  int64_t need = decode_ws_bytes(H, W);
   if (T > PYRE_FUSED_REDUCE_MAX_T) {
     const int64_t pg = ffn_gemm_partial_bytes(T, W, 2), pd = ffn_gemm_partial_bytes(T, H, 1);
     need += ffn_gemm_staging_bytes(T, H, W) + (pg > pd ? pg : pd) + 256;
@@ -223,7 +230,7 @@ int ffn_decode_check(const void* x, int x_dtype, int T, int H, const void* wgu, 
     PYRE_CHECK_ARG(T <= comm->max_tokens, f + ": T exceeds the communicator's max_tokens");
     PYRE_CHECK_ARG(!tp || tiles_of(H) <= kMaxOwnedTiles, f + ": H too large for the fused reduce");
   }
-  if (ws_bytes < decode_ws_bytes(T, H, W, gated ? 2 : 1))
+  if (ws_bytes < decode_ws_bytes(H, W))
     return set_error(PYRE_ENOMEM, f + ": workspace smaller than pyre_ffn_workspace_bytes()");
   return PYRE_OK;
 }
@@ -244,12 +251,12 @@ extern "C" int pyre_ffn_decode_q80(const void* x, int x_dtype, int T, int H, con
   p.wb = static_cast<const uint8_t*>(wd);
   fill_phase(p, false, H, W, na);
   fill_phase(p, true, W, H, 1);
-  // accumulators (zero on entry, zeroed again by the kernel) right after the header; h, plain
-  // data, at the end of the workspace, where a call with another T finds no accumulator of its own
-  p.accA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
-  p.accB = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(p.accA) + stream_acc_bytes(T, W, na));
-  p.outA = wsc + (ws_bytes - align256(static_cast<int64_t>(T) * W * 4)) / 256 * 256;   // h [T, W] f32
-  p.outA_bf16 = 0;
+  // phase-B accumulators (zero on entry, zeroed again by the kernel) right after the header;
+  // the gate/up slab sums and counts after the lead region (see decode_ws_bytes)
+  p.accB = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes);
+  p.sumA = reinterpret_cast<unsigned long long*>(wsc + kHeaderBytes + lead_bytes(H, W));
+  p.cntAB = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(p.sumA) + ab_sums_bytes(W));
+  p.ab_calls = reinterpret_cast<unsigned int*>(wsc + kHdrAbCalls);
   p.outB = out;
   fill_header(p, wsc);
   if (tp) p.comm = comm::device_view(comm);

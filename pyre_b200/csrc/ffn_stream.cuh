@@ -17,14 +17,22 @@
 // chunk reads the accumulator back, clears it for the next call and runs the slab epilogue
 // (SiLU-mul and h store, or the output store / cross-rank push) while its consumers stream on.
 //
+// MODE_AB keeps no h. The gate/up slab sums are read directly by the phase-B stages that need
+// them: the producer waits (acquire) until the slab's chunk count reaches cptA, then copies the
+// sums of the stage's R_B rows next to the down block, and each consumer warp computes
+// h = silu(g) * u of the rows it reads (the same arithmetic as the slab epilogue). A slab thus
+// becomes usable one count after its last chunk instead of after count, read-back, h store and
+// flag release, every one a round trip through a fully loaded memory system. The sums and
+// counts stay in place until the next call, so there are two sets used by alternate calls
+// (ab_calls parity): each call clears the other set, which the previous call used.
+//
 // MODE_AB queue. Phase-B chunk column c (chunk c of every output slab) reads rows
 // [c*512, c*512+512) of h, which phase-A slabs [c*spg, c*spg+spg) produce (group c). The
 // queue is: groups 0..slack-1 of phase A, then for each later group g its phase-A chunks
 // followed by phase-B column g-slack, then the last `slack` phase-B columns. Phase B thus
 // runs alongside phase A instead of after it, each phase-B column comes about `slack`
-// groups after the rows it reads, and the tail is short chunks of both phases. The epilogue
-// of a phase-A slab publishes a ready flag tagged with the call's epoch; the producer waits
-// for the flag of the slab holding rows k0.. of h before it loads that h slice.
+// groups after the rows it reads, and the tail is short chunks of both phases. The producer
+// waits for the chunk count of the slab holding rows k0.. of h before it copies its sums.
 // No deadlock: every chunk depends only on phase-A chunks earlier in the queue, chunks are
 // taken in queue order by running CTAs, and a CTA's stages are consumed in order, so the
 // earliest unfinished chunk can always proceed. Every wait is bounded besides.
@@ -60,6 +68,9 @@ struct alignas(64) StreamParams {
   unsigned int* cntB;
   uint32_t* ready;           // [tilesA] per-slab ready flags (MODE_AB)
   unsigned int* next;        // queue position counter
+  unsigned long long* sumA;  // MODE_AB: [2][tilesA][kSlabSums] gate/up slab sums, one set per call parity
+  unsigned int* cntAB;       // MODE_AB: [2][tilesA] finished phase-A chunks, one set per call parity
+  unsigned int* ab_calls;    // MODE_AB: calls made so far on this workspace (its parity picks the set)
   uint32_t* ws_epoch;
   unsigned int* ws_done;
   int* status;
@@ -67,6 +78,11 @@ struct alignas(64) StreamParams {
 };
 
 constexpr int kMaxOwnedTiles = 64;   // tensor-parallel: slabs one CTA may finish (H <= 16384)
+
+// MODE_AB slab sums: per phase-A slab [2 matrices][PYRE_FUSED_REDUCE_MAX_T tokens][kTileN] int64,
+// the same layout for every T and for gated or not, so calls of any shape can share a workspace.
+constexpr int kSumT = PYRE_FUSED_REDUCE_MAX_T;
+constexpr int kSlabSums = 2 * kSumT * kTileN;
 
 // Warp roles: kConsumerWarps consumers, one producer, kHelperWarps helpers.
 constexpr int kHelperWarps = 1;
@@ -79,7 +95,12 @@ template <int T, int NA, typename XA, typename XB, typename ST>
 struct StreamCfg {
   using LA = StageLayout<T, NA, XA, ST>;
   using LB = StageLayout<T, 1, XB, ST>;
-  static constexpr int kStageBytes = LA::kBytes > LB::kBytes ? LA::kBytes : LB::kBytes;
+  // MODE_AB phase-B stage: packed down block, then h of its rows (f32 [T][R_B], computed by the
+  // consumers), then the slab sums those rows come from ([NA][T][R_B] int64, one bulk copy each)
+  static constexpr int kSumOff = LB::kXOff + LB::kXBytes;
+  static constexpr int kSumBytesMax = 2 * T * LB::kRows * 8;
+  static constexpr int kBytesAB = (kSumOff + kSumBytesMax + 127) / 128 * 128;
+  static constexpr int kStageBytes = LA::kBytes > kBytesAB ? LA::kBytes : kBytesAB;
   static constexpr int kCtasPerSm = (T <= 2) ? 2 : 1;
   static constexpr int kStages = (T <= 2) ? 4 : 5;
   static constexpr int kRedFloats = kConsumerWarps * NA * T * kTileN;
@@ -96,8 +117,8 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Bounded wait for a per-slab ready flag (2 s); records PYRE_ETIMEOUT and returns false
-// on expiry.
+// Bounded wait (2 s) until a flag or counter word equals `epoch` (acquire); records
+// PYRE_ETIMEOUT and returns false on expiry.
 __device__ __forceinline__ bool wait_ready(const uint32_t* flag, uint32_t epoch, int* status) {
   if (ld_acquire_gpu(flag) == epoch) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -132,10 +153,12 @@ constexpr float kFixInv = 2.3283064365386963e-10f;    // 2^-32
 constexpr float kFixLimit = 1073741824.0f;            // 2^30
 
 // Sums acc over the two row lanes and all consumer warps (in warp order) and adds the
-// chunk's partial [NMAT][T][kTileN] into the slab accumulator. A partial that is not finite
-// or not below 2^30 in magnitude is added as 0 and flags PYRE_ERANGE.
+// chunk's partial [NMAT][T][kTileN] into the slab accumulator, laid out [NMAT][TS][kTileN]
+// (TS >= T tokens of stride). A partial that is not finite or not below 2^30 in magnitude is
+// added as 0 and flags PYRE_ERANGE. kProxy: the sums are read next by bulk copies (async
+// proxy), so every adding thread fences its adds against that proxy.
 // red: kConsumerWarps * NMAT * T * kTileN floats.
-template <int T, int NMAT>
+template <int T, int NMAT, int TS = T, bool kProxy = false>
 __device__ __forceinline__ void reduce_to_acc(float2 (&acc)[NMAT][T][8], float* red, unsigned long long* accum,
                                               int* status, int warp, int rs, int cc, int tid) {
 #pragma unroll
@@ -171,8 +194,11 @@ __device__ __forceinline__ void reduce_to_acc(float2 (&acc)[NMAT][T][8], float* 
       atomicCAS(status, PYRE_OK, PYRE_ERANGE);
       v = 0.f;
     }
-    atomicAdd(accum + i, static_cast<unsigned long long>(__float2ll_rn(v * kFixScale)));
+    const int row = i / kTileN, m = row / T;
+    atomicAdd(accum + (m * TS + (row - m * T)) * kTileN + (i - row * kTileN),
+              static_cast<unsigned long long>(__float2ll_rn(v * kFixScale)));
   }
+  if constexpr (kProxy) fence_proxy_async_global();
   consumer_sync();   // red is rewritten at the next chunk's end
 }
 
@@ -273,19 +299,24 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
   // of its first chunk (weights are constant; the chunk is this CTA's fixed first item, so
   // the workspace is not touched), then waits before any activation load or workspace access.
   const bool producer = warp == kConsumerWarps && lane == 0;
-  uint32_t epoch = 0, cepoch = 0;
+  uint32_t epoch = 0, cepoch = 0, ab_call = 0;
   if (!producer) {
     pdl_wait();
-    // epoch of this call (tags the per-slab ready flags); published by the last CTA to exit
+    // epoch of this call; published by the last CTA to exit
     epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
+    if constexpr (MODE == MODE_AB) ab_call = *reinterpret_cast<volatile uint32_t*>(p.ab_calls);
     if constexpr (TP) cepoch = comm::epoch_begin(p.comm);
   }
+  // MODE_AB: slab sums and chunk counts of a call parity (this call's: ab_call & 1; the other
+  // set is the previous call's, cleared during this call for the next one)
+  auto sums_of = [&](uint32_t q) { return p.sumA + static_cast<int64_t>(q & 1u) * p.tilesA * kSlabSums; };
+  auto cnt_of = [&](uint32_t q) { return p.cntAB + static_cast<int64_t>(q & 1u) * p.tilesA; };
 
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     if (lane == 0) {
       if constexpr (kHasA) prefetch_tmap(&p.txa);
-      if constexpr (kHasB) prefetch_tmap(&p.txb);
+      if constexpr (kHasB && MODE != MODE_AB) prefetch_tmap(&p.txb);
       int s = 0;
       uint32_t ph = 0;
       // activation loads of the stages issued before pdl_wait (at most one ring of stages)
@@ -299,6 +330,7 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
         pdl_trigger();
         dep = true;
         epoch = *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) + 1u;
+        if constexpr (MODE == MODE_AB) ab_call = *reinterpret_cast<volatile uint32_t*>(p.ab_calls);
         for (int i = 0; i < ndef; ++i) {
           uint8_t* st = stages + def_s[i] * C::kStageBytes;
           if (def_b[i]) {
@@ -315,8 +347,8 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       // copy into this CTA's shared memory is in flight when it exits.
       bool ok = true;
       uint32_t issued = 0, par = 0;   // stages with an unconfirmed copy, and that copy's parity
-      // MODE_AB: the last phase-A slab this producer has seen ready (its flag acquired and the
-      // proxy fence done); the following units of the same slab need no second flag round trip
+      // MODE_AB: the last phase-A slab this producer has seen complete (its count acquired and
+      // the proxy fence done); the following units of the same slab need no second round trip
       int seen_slab = -1;
       auto acquire = [&]() -> bool {
         if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) return false;
@@ -360,13 +392,41 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
           if constexpr (kHasB) {
             const int u0 = chunk * kChunk;
             const int u1 = min(u0 + kChunk, p.uptB);
-            // MODE_AB: h is this kernel's own phase-A output, read only after the wait
+            // MODE_AB: h comes from this kernel's own phase-A sums, read only after the wait
             if (MODE == MODE_AB) resolve();
             for (int u = u0; u < u1; ++u) {
               if (ndef == C::kStages) resolve();
               if (!acquire()) return false;
               meta[s] = StageMeta{1, tile, chunk, u + 1 == u1};
               uint8_t* st = stages + s * C::kStageBytes;
+              if constexpr (MODE == MODE_AB) {
+                // the down block, and the gate/up slab sums of its R_B rows of h (slab k0 / 256;
+                // R_B divides 256) once every chunk of that slab has counted; a slab already
+                // seen complete in this call needs no second acquire
+                constexpr uint32_t kSumPiece = LB::kRows * 8;
+                mbar_arrive_expect_tx(&full[s], LB::kWBytes + NA * T * kSumPiece);
+                bulk_load(st, p.wb + (static_cast<int64_t>(tile) * p.uptB + u) * LB::kWBytes, LB::kWBytes, &full[s]);
+                const int k0 = u * LB::kRows;
+                const int slab = k0 / kTileN;
+                bool rdy = true;
+                if (slab != seen_slab) {
+                  rdy = wait_ready(cnt_of(ab_call) + slab, static_cast<uint32_t>(p.cptA), p.status);
+                  fence_proxy_async_global();
+                  if (rdy) seen_slab = slab;
+                }
+                // issued even when the wait ran out, so the stage's byte count completes
+                const unsigned long long* src =
+                    sums_of(ab_call) + static_cast<int64_t>(slab) * kSlabSums + (k0 - slab * kTileN);
+#pragma unroll
+                for (int m = 0; m < NA; ++m)
+#pragma unroll
+                  for (int t = 0; t < T; ++t)
+                    bulk_load(st + C::kSumOff + (m * T + t) * kSumPiece, src + (m * kSumT + t) * kTileN, kSumPiece,
+                              &full[s]);
+                issue_done();
+                if (!rdy) return false;
+                continue;
+              }
               mbar_arrive_expect_tx(&full[s], LB::kTxBytes);
               bulk_load(st, p.wb + (static_cast<int64_t>(tile) * p.uptB + u) * LB::kWBytes, LB::kWBytes, &full[s]);
               const int k0 = u * LB::kRows;
@@ -378,21 +438,8 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
                 issue_done();
                 continue;
               }
-              bool rdy = true;
-              if constexpr (MODE == MODE_AB) {
-                // rows k0..k0+R_B-1 of h come from phase-A slab k0 / 256 (R_B divides 256); a
-                // slab already seen ready in this call needs no second acquire
-                const int slab = k0 / kTileN;
-                if (slab != seen_slab) {
-                  rdy = wait_ready(p.ready + slab, epoch, p.status);
-                  fence_proxy_async_global();
-                  if (rdy) seen_slab = slab;
-                }
-              }
-              // issued even when the flag wait ran out, so the stage's byte count completes
               tma_load_2d(st + LB::kXOff, &p.txb, k0, 0, &full[s]);
               issue_done();
-              if (!rdy) return false;
             }
           }
         }
@@ -473,6 +520,23 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       const StageMeta m = meta[s];
       if (m.phase < 0) break;
       const uint8_t* st = stages + s * C::kStageBytes;
+      if constexpr (MODE == MODE_AB) {
+        if (m.phase == 1) {
+          // h of the rows this warp reads (row pass * 16 + 2 * warp + rs of every pass, every
+          // token) from the gate/up slab sums, with the arithmetic of the slab epilogue: silu(g) * u
+          // of the fixed-point sums scaled back to f32; written where consume_unit reads it
+          constexpr int kWarpRows = LB::kRows / kRowsPerPass * 2;
+          if (lane < T * kWarpRows) {
+            const int t = lane / kWarpRows, j = lane - t * kWarpRows;
+            const int r = (j >> 1) * kRowsPerPass + warp * 2 + (j & 1);
+            const long long* sm = reinterpret_cast<const long long*>(st + C::kSumOff);
+            float h = silu_f32(__ll2float_rn(sm[t * LB::kRows + r]) * kFixInv);
+            if constexpr (NA == 2) h *= __ll2float_rn(sm[(T + t) * LB::kRows + r]) * kFixInv;
+            reinterpret_cast<float*>(stages + s * C::kStageBytes + LB::kXOff)[t * LB::kRows + r] = h;
+          }
+          __syncwarp();
+        }
+      }
       if (kHasA && m.phase == 0) {
         consume_unit<T, NA, XA, ST>(st, acc, warp, rs, cc);
       } else if constexpr (kHasB) {
@@ -486,7 +550,10 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
         ph ^= 1u;
       }
       if (!m.last) continue;
-      if (kHasA && m.phase == 0) {
+      if (MODE == MODE_AB && m.phase == 0) {
+        reduce_to_acc<T, NA, kSumT, true>(acc, red, sums_of(ab_call) + static_cast<int64_t>(m.tile) * kSlabSums,
+                                          p.status, warp, rs, cc, tid);
+      } else if (kHasA && m.phase == 0) {
         reduce_to_acc<T, NA>(acc, red, p.accA + static_cast<int64_t>(m.tile) * (NA * T * kTileN), p.status, warp, rs,
                              cc, tid);
       } else if constexpr (kHasB) {
@@ -516,6 +583,24 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       }
       if (job.end) break;
       const bool isA = kHasA && job.phase == 0;
+      if constexpr (MODE == MODE_AB) {
+        if (isA) {
+          // count the chunk for its slab: the consumers' sum adds (each fenced against the async
+          // proxy) are ordered before this (barrier, then mbarrier release/acquire) and the fence
+          // makes them visible GPU-wide before the count; the phase-B producers wait for the
+          // count to reach cptA, then read the sums with bulk copies
+          if (htid == 0) {
+            __threadfence();
+            atomicAdd(cnt_of(ab_call) + job.tile, 1u);
+          }
+          // clear this chunk's share of the slab's sums and count of the previous call (the
+          // other set), which the next call uses: blocks of 32 words, block b for chunk b % cptA
+          unsigned long long* old = sums_of(ab_call ^ 1u) + static_cast<int64_t>(job.tile) * kSlabSums;
+          for (int i = job.chunk * 32 + htid; i < kSlabSums; i += p.cptA * 32) old[i] = 0ull;
+          if (job.chunk == 0 && htid == 0) cnt_of(ab_call ^ 1u)[job.tile] = 0u;
+          continue;
+        }
+      }
       const int cpt = isA ? p.cptA : p.cptB;
       if (htid == 0) {
         // the consumers' accumulator adds are ordered before this (barrier, then mbarrier
@@ -557,16 +642,6 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
               }
               if (col < p.NA) store_out(p.outA, p.outA_bf16, p.NA, t, col, h0);
               if (col + 1 < p.NA) store_out(p.outA, p.outA_bf16, p.NA, t, col + 1, h1);
-            }
-          }
-          if constexpr (MODE == MODE_AB) {
-            // h is read next by other CTAs' TMA (async proxy): proxy fence per writer, then
-            // one cumulative release of the slab's flag
-            fence_proxy_async_global();
-            helper_sync();
-            if (htid == 0) {
-              __threadfence();
-              st_release_gpu(p.ready + job.tile, epoch);
             }
           }
         }
@@ -629,6 +704,7 @@ q80_ffn_stream_kernel(const __grid_constant__ StreamParams p) {
       // last CTA: reset the queue counter and publish the epoch for the next call
       p.next[0] = 0u;
       *reinterpret_cast<volatile unsigned int*>(p.ws_done) = 0u;
+      if constexpr (MODE == MODE_AB) *reinterpret_cast<volatile unsigned int*>(p.ab_calls) = ab_call + 1u;
       __threadfence();
       *reinterpret_cast<volatile uint32_t*>(p.ws_epoch) = epoch;
     }

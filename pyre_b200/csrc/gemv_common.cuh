@@ -46,6 +46,7 @@ constexpr int64_t kHdrEpoch = 0;
 constexpr int64_t kHdrDone = 4;
 constexpr int64_t kHdrStatus = 8;
 constexpr int64_t kHdrNext = 16;       // two u32 chunk counters (dynamic scheduling)
+constexpr int64_t kHdrAbCalls = 64;    // u32: one-launch decode FFN calls made on this workspace
 constexpr int64_t kHdrCntA = 1024;
 constexpr int64_t kHdrCntB = kHdrCntA + kMaxTiles * 4;
 constexpr int64_t kHdrReady = kHdrCntB + kMaxTiles * 4;

@@ -83,15 +83,26 @@ def test_ffn_deterministic_and_workspace_reuse():
     outs = [op(x, g, u, d).clone() for _ in range(5)]
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
-    hdr = op.workspace[:32768].view(torch.int32)
+    ws = op.workspace
+    hdr = ws[:32768].view(torch.int32)
     assert int(hdr[0]) == 5                                  # call epoch: one per call
     assert int(hdr[2]) == 0                                  # status word
     assert int(hdr[4]) == 0                                  # chunk queue position reset
+    assert int(hdr[16]) == 5                                 # one-launch decode calls made
     assert int(hdr[256:256 + 2 * 2048].abs().sum()) == 0     # per-slab chunk counters reset
-    # the fixed-point slab accumulators follow the header and are cleared; the h buffer
-    # ([2, 3072] f32, plain data) is the last part of the workspace
-    acc = op.workspace[32768:op.workspace.numel() - 2 * 3072 * 4]
-    assert int(acc.count_nonzero()) == 0
+    # after the header: the fixed-point accumulators (sized for 4 tokens and both phases),
+    # cleared by every call
+    tiles_w, cpt_a = 3072 // 256, (1024 // 32 + 7) // 8
+    lead = max(tiles_w * 2 * 4 * 256 * 8, (1024 // 256) * 4 * 256 * 8)
+    assert int(ws[32768:32768 + lead].count_nonzero()) == 0
+    # then the two sets of gate/up slab sums and chunk counts used by alternate calls: the last
+    # call's set (calls 0..4: parity 0) stays until the next call clears it; the previous
+    # call's set (parity 1) has been cleared by the last call
+    n_sums = 2 * tiles_w * 2048 * 8
+    sums = ws[32768 + lead:32768 + lead + n_sums].view(2, -1)
+    cnt = ws[32768 + lead + n_sums:32768 + lead + n_sums + 2 * tiles_w * 4].view(torch.int32).view(2, tiles_w)
+    assert int(sums[0].count_nonzero()) > 0 and int(sums[1].count_nonzero()) == 0
+    assert cnt[0].tolist() == [cpt_a] * tiles_w and int(cnt[1].count_nonzero()) == 0
 
 
 def test_one_workspace_serves_prefill_and_decode_calls():
