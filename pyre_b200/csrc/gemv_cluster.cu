@@ -20,6 +20,9 @@
 // use the streaming kernel of ffn_stream.cuh.
 #include <cooperative_groups.h>
 
+#include <mutex>
+#include <vector>
+
 #include "ffn_internal.cuh"
 
 namespace pyre {
@@ -36,15 +39,20 @@ constexpr int kThreadsC = kConsumers + 32;          // 8 consumer warps + 1 prod
 template <typename ST>
 constexpr int block_bytes() { return kRows * kTileN + kRows * 8 * static_cast<int>(sizeof(ST)); }
 
-// Shared memory: partial [T][256] | warp partials [warps][T][256] | barriers (128 B) |
-// x [T][units*64] f32 | blocks. The partial comes first so that it sits at the same offset in
-// every rank of the cluster (the ranks read each other's partials through distributed shared
-// memory at the address of their own), whatever each rank's block count.
+// Shared memory: partial [T][256] | barriers (128 B) | x [T][units*64] f32 | blocks, where the
+// warp partials ([warps][T][256] f32) reuse the block area once every warp is done with the
+// blocks. The partial comes first so that it sits at the same offset in every rank of the
+// cluster (the ranks read each other's partials through distributed shared memory at the
+// address of their own), whatever each rank's block count. Keeping the head small lets three
+// CTAs of four blocks share an SM, so a 24-slab Q/K/V matrix runs as one wave of clusters.
 template <int T>
-constexpr int head_bytes() { return T * kTileN * 4 + kConsumerWarps * T * kTileN * 4 + 128; }
+constexpr int head_bytes() { return T * kTileN * 4 + 128; }
+template <int T>
+constexpr int red_bytes() { return kConsumerWarps * T * kTileN * 4; }
 template <int T, typename ST>
 constexpr int smem_bytes(int units) {
-  return head_bytes<T>() + T * units * kRows * 4 + units * block_bytes<ST>();
+  return head_bytes<T>() + T * units * kRows * 4 +
+         (units * block_bytes<ST>() > red_bytes<T>() ? units * block_bytes<ST>() : red_bytes<T>());
 }
 
 struct Params {
@@ -111,10 +119,10 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
   const int nu = u1 - u0;                    // 1..kMaxUnits (the host picks C so)
   const int pitch = nu * kRows;
   float* fin = reinterpret_cast<float*>(smem);                        // same offset in every rank
-  float* red = fin + T * kTileN;
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * T * kTileN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(fin + T * kTileN);
   float* xs = reinterpret_cast<float*>(smem + head_bytes<T>());
   uint8_t* blocks = smem + head_bytes<T>() + T * pitch * 4;          // 16-byte aligned
+  float* red = reinterpret_cast<float*>(blocks);                      // after the last block is read
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < nu; ++i) mbar_init(&full[i], 1);
@@ -146,6 +154,7 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
       mbar_wait(&full[i], 0, p.status);
       consume_block<T, ST>(blocks + i * kBB, xs + i * kRows, pitch, acc, warp, rs, cc);
     }
+    consumer_sync();   // every warp is done with the blocks: the warp partials go there
     reduce_tile<T, 1>(acc, red, fin, warp, rs, cc, tid);   // fin[t * 256 + c]: this CTA's partial
   }
   cluster.sync();          // every rank's partial is complete and visible
@@ -166,23 +175,83 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
   cluster.sync();          // no rank leaves while another still reads its partial
 }
 
-// Cluster size for [K, N]: enough ranks that each holds at most kMaxUnits blocks, then more
-// (up to 16, at most one block per rank) until the grid has about two CTAs per SM.
-int pick_cluster(int upt, int tiles) {
-  int c = 1;
-  while (c * kMaxUnits < upt) c <<= 1;
-  if (c > kMaxCluster) return 0;
-  const int want = 2 * sm_count();
-  while (c < kMaxCluster && c * 2 <= upt && tiles * c < want) c <<= 1;
-  return c;
+// Smallest cluster for [K, N]: enough ranks that each holds at most kMaxUnits blocks (0: K too
+// large for this kernel).
+int min_cluster(int upt) {
+  const int c = (upt + kMaxUnits - 1) / kMaxUnits;
+  return c <= kMaxCluster ? (c < 1 ? 1 : c) : 0;
+}
+
+template <int T, typename XT, typename ST>
+cudaLaunchConfig_t launch_cfg(int C, int tiles, int upt, cudaStream_t s, cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(C), static_cast<unsigned>(tiles), 1);
+  cfg.blockDim = dim3(kThreadsC, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes<T, ST>((upt + C - 1) / C));
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cfg;
+}
+
+// Cluster size for [K, N] on this device: the one that runs the tiles' clusters in the fewest
+// waves of co-resident one-token clusters (all of a CTA's blocks are in flight at once, so a
+// second wave costs a whole second fetch latency), the larger one (more SMs fetching) among
+// equals. The cluster size fixes how K is split into partial sums, so it is decided for the
+// matrix alone (one token, and the same for every T and activation type: a row of a batch then
+// gets exactly the sums it gets alone) and cached per (device, upt, tiles, scale type).
+template <typename ST>
+int pick_cluster(int upt, int tiles, cudaStream_t s, int* C) {
+  auto kern = q80_gemv_cluster_kernel<1, float, ST>;
+  struct Pick { int dev, upt, tiles, C; };
+  static std::mutex mu;
+  static std::vector<Pick> cache;
+  int dev = 0;
+  PYRE_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Pick& q : cache)
+    if (q.dev == dev && q.upt == upt && q.tiles == tiles) {
+      *C = q.C;
+      return PYRE_OK;
+    }
+  int rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<1, ST>(kMaxUnits));
+  if (rc) return rc;
+  PYRE_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  const int c0 = min_cluster(upt);
+  int best = 0, best_waves = 0;
+  for (int c = c0; c <= kMaxCluster && c <= (upt > c0 ? upt : c0); ++c) {
+    cudaLaunchAttribute attr[2]{};
+    cudaLaunchConfig_t cfg = launch_cfg<1, float, ST>(c, tiles, upt, s, attr);
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active < 1) {
+      (void)cudaGetLastError();
+      continue;
+    }
+    const int waves = (tiles + active - 1) / active;
+    if (best == 0 || waves <= best_waves) {
+      best = c;
+      best_waves = waves;
+    }
+  }
+  if (best == 0) return set_error(PYRE_ECUDA, "q80_gemv_cluster_kernel: no cluster size fits on the device");
+  cache.push_back(Pick{dev, upt, tiles, best});
+  *C = best;
+  return PYRE_OK;
 }
 
 template <int T, typename XT, typename ST>
 int launch_t(Params p, int tiles, cudaStream_t s) {
   auto kern = q80_gemv_cluster_kernel<T, XT, ST>;
-  const int max_units = (p.upt + p.C - 1) / p.C;
-  const int smem = smem_bytes<T, ST>(max_units);
-  int rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<T, ST>(kMaxUnits));
+  int rc = pick_cluster<ST>(p.upt, tiles, s, &p.C);
+  if (rc) return rc;
+  rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<T, ST>(kMaxUnits));
   if (rc) return rc;
   if (p.C > 8) {
     static bool nonportable_set[64] = {};
@@ -194,33 +263,8 @@ int launch_t(Params p, int tiles, cudaStream_t s) {
       nonportable_set[d & 63] = true;
     }
   }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.C), static_cast<unsigned>(tiles), 1);
-  cfg.blockDim = dim3(kThreadsC, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
-  cfg.stream = s;
   cudaLaunchAttribute attr[2]{};
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(p.C);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  // that a cluster of this size fits is checked once per (device, cluster size), with the
-  // largest shared-memory request
-  static bool fits[64][kMaxCluster + 1] = {};
-  int dev = 0;
-  PYRE_CUDA_TRY(cudaGetDevice(&dev));
-  if (!fits[dev & 63][p.C]) {
-    cudaLaunchConfig_t probe = cfg;
-    probe.dynamicSmemBytes = static_cast<size_t>(smem_bytes<T, ST>(kMaxUnits));
-    int clusters = 0;
-    PYRE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &probe));
-    if (clusters < 1) return set_error(PYRE_ECUDA, "q80_gemv_cluster_kernel: the cluster does not fit on the device");
-    fits[dev & 63][p.C] = true;
-  }
+  cudaLaunchConfig_t cfg = launch_cfg<T, XT, ST>(p.C, tiles, p.upt, s, attr);
   PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
   PYRE_LAUNCH_CHECK("q80_gemv_cluster_kernel");
   return PYRE_OK;
@@ -241,8 +285,8 @@ int launch_types(Params p, int T, int tiles, cudaStream_t s) {
 
 // Whether the cluster GEMV serves [K, N] (K <= 8192 at 64 rows per block and 8 blocks per rank).
 bool gemv_cluster_eligible(int K, int N) {
-  const int upt = (K + gcl::kRows - 1) / gcl::kRows;
-  return gcl::pick_cluster(upt, gemv::tiles_of(N)) > 0;
+  (void)N;
+  return gcl::min_cluster((K + gcl::kRows - 1) / gcl::kRows) > 0;
 }
 
 int gemv_cluster(const void* x, int x_dtype, int T, int K, const void* w, int scale_dtype, int N, const float* bias,
@@ -257,8 +301,7 @@ int gemv_cluster(const void* x, int x_dtype, int T, int K, const void* w, int sc
   p.N = N;
   p.upt = (K + gcl::kRows - 1) / gcl::kRows;
   const int tiles = gemv::tiles_of(N);
-  p.C = gcl::pick_cluster(p.upt, tiles);
-  PYRE_CHECK_ARG(p.C > 0, "q80 GEMV: K too large for the cluster kernel");
+  PYRE_CHECK_ARG(gcl::min_cluster(p.upt) > 0, "q80 GEMV: K too large for the cluster kernel");
   const bool f16s = scale_dtype == PYRE_F16;
   if (x_dtype == PYRE_BF16)
     return f16s ? gcl::launch_types<__nv_bfloat16, __half>(p, T, tiles, s)

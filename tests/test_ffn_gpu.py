@@ -53,7 +53,8 @@ def run_case(H, W, T, gated, scale_dtype, x_dtype, seed=0):
 
 
 SHAPES = [(256, 384, 1), (256, 384, 2), (256, 384, 3), (256, 384, 4), (256, 96, 1), (256, 160, 3),
-          (576, 768, 1), (896, 2432, 1), (256, 384, 5), (256, 384, 17), (576, 768, 64), (1024, 2048, 200)]
+          (576, 768, 1), (896, 2432, 1), (512, 8192, 4), (256, 384, 5), (256, 384, 17), (576, 768, 64),
+          (1024, 2048, 200)]
 
 
 @pytest.mark.parametrize("H,W,T", SHAPES)
