@@ -6,9 +6,11 @@
 // Layout: one cluster of C CTAs per 256-column slab of the packed matrix (gemv_common.cuh,
 // M = 1: blocks of 64 rows x 256 columns, one bulk copy each). CTA r of the cluster owns the
 // contiguous block range [r*upt/C, (r+1)*upt/C) of the slab (upt = blocks per slab, at most 8
-// per CTA) and keeps ALL of them in flight at once: its producer lane issues every bulk copy
-// before griddepcontrol.wait (weights are constant), so under programmatic dependent launch
-// the whole weight fetch overlaps the previous kernel's tail. After the wait the CTA reads its
+// per CTA) and normally keeps ALL of them in flight at once: its producer lane issues every
+// bulk copy before griddepcontrol.wait (weights are constant), so under programmatic dependent
+// launch the whole weight fetch overlaps the previous kernel's tail. When that leaves too few
+// clusters co-resident for one wave, the blocks go through a ring of fewer slots instead (the
+// first slots before the wait, each later block as soon as its slot is consumed). After the wait the CTA reads its
 // slice of x into shared memory, the consumer warps accumulate block by block (the exact
 // int8 -> f32 conversion and packed f32x2 FMA of gemv_common.cuh), reduce over warps into a
 // [T, 256] partial, and the cluster reduces the C partials through distributed shared memory:
@@ -50,9 +52,9 @@ constexpr int head_bytes() { return T * kTileN * 4 + 128; }
 template <int T>
 constexpr int red_bytes() { return kConsumerWarps * T * kTileN * 4; }
 template <int T, typename ST>
-constexpr int smem_bytes(int units) {
+constexpr int smem_bytes(int units, int slots) {
   return head_bytes<T>() + T * units * kRows * 4 +
-         (units * block_bytes<ST>() > red_bytes<T>() ? units * block_bytes<ST>() : red_bytes<T>());
+         (slots * block_bytes<ST>() > red_bytes<T>() ? slots * block_bytes<ST>() : red_bytes<T>());
 }
 
 struct Params {
@@ -62,6 +64,7 @@ struct Params {
   float* out;             // [T, N]
   int* status;            // PYRE_ETIMEOUT if a copy wait ran out
   int K, N, upt, C;
+  int slots;              // block slots per CTA (a ring when fewer than the CTA's blocks)
 };
 
 template <typename XT>
@@ -119,26 +122,42 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
   const int nu = u1 - u0;                    // 1..kMaxUnits (the host picks C so)
   const int pitch = nu * kRows;
   float* fin = reinterpret_cast<float*>(smem);                        // same offset in every rank
-  uint64_t* full = reinterpret_cast<uint64_t*>(fin + T * kTileN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(fin + T * kTileN);     // [kMaxUnits]
+  uint64_t* empty = full + kMaxUnits;                                 // [kMaxUnits]
+  const int S = p.slots < nu ? p.slots : nu;
   float* xs = reinterpret_cast<float*>(smem + head_bytes<T>());
   uint8_t* blocks = smem + head_bytes<T>() + T * pitch * 4;          // 16-byte aligned
   float* red = reinterpret_cast<float*>(blocks);                      // after the last block is read
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < nu; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == kConsumerWarps && lane == 0) {
-    // every block of this CTA in flight at once, before the wait: weights are constant
-    const uint8_t* src = p.w + (static_cast<int64_t>(tile) * p.upt + u0) * kBB;
-    for (int i = 0; i < nu; ++i) {
+  const bool producer = warp == kConsumerWarps && lane == 0;
+  const uint8_t* src = p.w + (static_cast<int64_t>(tile) * p.upt + u0) * kBB;
+  if (producer) {
+    // the first S blocks of this CTA (all of them when S == nu) in flight before the wait:
+    // weights are constant
+    for (int i = 0; i < S; ++i) {
       mbar_arrive_expect_tx(&full[i], kBB);
       bulk_load(blocks + i * kBB, src + static_cast<int64_t>(i) * kBB, kBB, &full[i]);
     }
   }
   pdl_wait();      // x comes from the previous kernel of the stream
   pdl_trigger();
+  if (producer) {
+    // ring: block i into slot i % S once the consumers have released that slot's previous block
+    for (int i = S; i < nu; ++i) {
+      const int sl = i % S;
+      if (!mbar_wait(&empty[sl], static_cast<uint32_t>((i / S - 1) & 1), p.status)) break;
+      mbar_arrive_expect_tx(&full[sl], kBB);
+      bulk_load(blocks + sl * kBB, src + static_cast<int64_t>(i) * kBB, kBB, &full[sl]);
+    }
+  }
   if (warp < kConsumerWarps) {
     const int tid = threadIdx.x;
     const int k0 = u0 * kRows;
@@ -151,8 +170,13 @@ __global__ void __launch_bounds__(kThreadsC, 1) q80_gemv_cluster_kernel(const __
     float2 acc[1][T][8];
     zero_acc<1, T>(acc);
     for (int i = 0; i < nu; ++i) {
-      mbar_wait(&full[i], 0, p.status);
-      consume_block<T, ST>(blocks + i * kBB, xs + i * kRows, pitch, acc, warp, rs, cc);
+      const int sl = i % S;
+      mbar_wait(&full[sl], static_cast<uint32_t>((i / S) & 1), p.status);
+      consume_block<T, ST>(blocks + sl * kBB, xs + i * kRows, pitch, acc, warp, rs, cc);
+      if (nu > S) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);
+      }
     }
     consumer_sync();   // every warp is done with the blocks: the warp partials go there
     reduce_tile<T, 1>(acc, red, fin, warp, rs, cc, tid);   // fin[t * 256 + c]: this CTA's partial
@@ -183,11 +207,11 @@ int min_cluster(int upt) {
 }
 
 template <int T, typename XT, typename ST>
-cudaLaunchConfig_t launch_cfg(int C, int tiles, int upt, cudaStream_t s, cudaLaunchAttribute (&attr)[2]) {
+cudaLaunchConfig_t launch_cfg(int C, int slots, int tiles, int upt, cudaStream_t s, cudaLaunchAttribute (&attr)[2]) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(C), static_cast<unsigned>(tiles), 1);
   cfg.blockDim = dim3(kThreadsC, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes<T, ST>((upt + C - 1) / C));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes<T, ST>((upt + C - 1) / C, slots));
   cfg.stream = s;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(C);
@@ -200,16 +224,18 @@ cudaLaunchConfig_t launch_cfg(int C, int tiles, int upt, cudaStream_t s, cudaLau
   return cfg;
 }
 
-// Cluster size for [K, N] on this device: the one that runs the tiles' clusters in the fewest
-// waves of co-resident one-token clusters (all of a CTA's blocks are in flight at once, so a
-// second wave costs a whole second fetch latency), the larger one (more SMs fetching) among
-// equals. The cluster size fixes how K is split into partial sums, so it is decided for the
-// matrix alone (one token, and the same for every T and activation type: a row of a batch then
-// gets exactly the sums it gets alone) and cached per (device, upt, tiles, scale type).
+// Cluster size and block slots for [K, N] on this device: the pair that runs the tiles'
+// clusters in the fewest waves of co-resident one-token clusters (a second wave costs a whole
+// second fetch latency); among equals every block in flight at once (no ring) before a ring
+// of kRingSlots, then the larger cluster (more SMs fetching). The cluster size fixes how K is
+// split into partial sums, so it is decided for the matrix alone (one token, and the same for
+// every T and activation type: a row of a batch then gets exactly the sums it gets alone) and
+// cached per (device, upt, tiles, scale type).
+constexpr int kRingSlots = 3;
 template <typename ST>
-int pick_cluster(int upt, int tiles, cudaStream_t s, int* C) {
+int pick_cluster(int upt, int tiles, cudaStream_t s, int* C, int* slots) {
   auto kern = q80_gemv_cluster_kernel<1, float, ST>;
-  struct Pick { int dev, upt, tiles, C; };
+  struct Pick { int dev, upt, tiles, C, slots; };
   static std::mutex mu;
   static std::vector<Pick> cache;
   int dev = 0;
@@ -218,40 +244,49 @@ int pick_cluster(int upt, int tiles, cudaStream_t s, int* C) {
   for (const Pick& q : cache)
     if (q.dev == dev && q.upt == upt && q.tiles == tiles) {
       *C = q.C;
+      *slots = q.slots;
       return PYRE_OK;
     }
-  int rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<1, ST>(kMaxUnits));
+  int rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<1, ST>(kMaxUnits, kMaxUnits));
   if (rc) return rc;
   PYRE_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   const int c0 = min_cluster(upt);
-  int best = 0, best_waves = 0;
-  for (int c = c0; c <= kMaxCluster && c <= (upt > c0 ? upt : c0); ++c) {
-    cudaLaunchAttribute attr[2]{};
-    cudaLaunchConfig_t cfg = launch_cfg<1, float, ST>(c, tiles, upt, s, attr);
-    int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active < 1) {
-      (void)cudaGetLastError();
-      continue;
-    }
-    const int waves = (tiles + active - 1) / active;
-    if (best == 0 || waves <= best_waves) {
-      best = c;
-      best_waves = waves;
+  int best = 0, best_slots = 0, best_waves = 0;
+  for (int ring = 0; ring < 2; ++ring) {
+    for (int c = c0; c <= kMaxCluster && c <= (upt > c0 ? upt : c0); ++c) {
+      const int units = (upt + c - 1) / c;
+      const int sl = ring ? kRingSlots : units;
+      if (ring && units <= kRingSlots) continue;
+      cudaLaunchAttribute attr[2]{};
+      cudaLaunchConfig_t cfg = launch_cfg<1, float, ST>(c, sl, tiles, upt, s, attr);
+      int active = 0;
+      if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active < 1) {
+        (void)cudaGetLastError();
+        continue;
+      }
+      const int waves = (tiles + active - 1) / active;
+      // no ring: the larger cluster among equals; ring: only if it needs fewer waves
+      if (best == 0 || waves < best_waves || (!ring && waves == best_waves)) {
+        best = c;
+        best_slots = sl;
+        best_waves = waves;
+      }
     }
   }
   if (best == 0) return set_error(PYRE_ECUDA, "q80_gemv_cluster_kernel: no cluster size fits on the device");
-  cache.push_back(Pick{dev, upt, tiles, best});
+  cache.push_back(Pick{dev, upt, tiles, best, best_slots});
   *C = best;
+  *slots = best_slots;
   return PYRE_OK;
 }
 
 template <int T, typename XT, typename ST>
 int launch_t(Params p, int tiles, cudaStream_t s) {
   auto kern = q80_gemv_cluster_kernel<T, XT, ST>;
-  int rc = pick_cluster<ST>(p.upt, tiles, s, &p.C);
+  int rc = pick_cluster<ST>(p.upt, tiles, s, &p.C, &p.slots);
   if (rc) return rc;
-  rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<T, ST>(kMaxUnits));
+  rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem_bytes<T, ST>(kMaxUnits, kMaxUnits));
   if (rc) return rc;
   if (p.C > 8) {
     static bool nonportable_set[64] = {};
@@ -264,7 +299,7 @@ int launch_t(Params p, int tiles, cudaStream_t s) {
     }
   }
   cudaLaunchAttribute attr[2]{};
-  cudaLaunchConfig_t cfg = launch_cfg<T, XT, ST>(p.C, tiles, p.upt, s, attr);
+  cudaLaunchConfig_t cfg = launch_cfg<T, XT, ST>(p.C, p.slots, tiles, p.upt, s, attr);
   PYRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
   PYRE_LAUNCH_CHECK("q80_gemv_cluster_kernel");
   return PYRE_OK;
